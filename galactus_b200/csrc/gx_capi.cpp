@@ -1,0 +1,656 @@
+// C-ABI of galactus_b200: slot policy, HBM slot arena with its pinned host
+// tier, the remap node, the expert kernels and the MoE layer entry point.
+// No C++ exception crosses this boundary; every entry point returns GX_*.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <unordered_set>
+#include <vector>
+
+#include "../../include/galactus_b200.h"
+#include "gx_formats.h"
+#include "gx_kernels.h"
+#include "gx_policy.hpp"
+
+using gx::PolicyError;
+using gx::SlotPolicy;
+
+struct gx_policy {
+    SlotPolicy impl;
+    explicit gx_policy(SlotPolicy && p) : impl(std::move(p)) {}
+};
+
+namespace {
+
+constexpr int kStageRing = 16;
+
+struct CudaFail {
+    cudaError_t err;
+};
+
+inline void ck(cudaError_t e) {
+    if (e != cudaSuccess) throw CudaFail{e};
+}
+
+template <typename F>
+int guarded(F && f) {
+    try {
+        return f();
+    } catch (const PolicyError & e) {
+        return e.code;
+    } catch (const CudaFail & e) {
+        std::fprintf(stderr, "galactus_b200: CUDA error: %s\n", cudaGetErrorString(e.err));
+        return e.err == cudaErrorMemoryAllocation ? GX_ERR_NOMEM : GX_ERR_CUDA;
+    } catch (const std::bad_alloc &) {
+        return GX_ERR_NOMEM;
+    } catch (...) {
+        return GX_ERR_INVALID;
+    }
+}
+
+SlotPolicy make_policy(const gx_profile & prof, uint64_t capacity, double fraction, int policy, const uint32_t * plan) {
+    if (prof.record_bytes == nullptr) throw PolicyError(GX_ERR_INVALID, "profile without record table");
+    if (prof.first_layer > prof.last_layer) throw PolicyError(GX_ERR_INVALID, "inverted layer range");
+    const uint32_t n = prof.last_layer - prof.first_layer + 1;
+    std::vector<uint64_t> rec(prof.record_bytes, prof.record_bytes + n);
+    return SlotPolicy(prof.first_layer, prof.last_layer, prof.experts, prof.used, rec, capacity, fraction, policy, plan);
+}
+
+// Serve one micro-batch of one layer through the policy: the engine's
+// micro-batch guard, begin_batch, one access per key in order (release of an
+// evicted slot before any allocation), then the slot of every key.
+// Misses are appended as (expert, slot).
+int serve_policy(SlotPolicy & P, uint32_t layer, const int32_t * experts, uint32_t count, int32_t * slots,
+                 uint8_t * hit_out, int32_t * evicted_out, std::vector<std::pair<int32_t, int32_t>> * misses,
+                 gx_serve_stats * st) {
+    if (layer < P.first_layer() || layer > P.last_layer()) return GX_ERR_INVALID;
+    for (uint32_t i = 0; i < count; ++i)
+        if (experts[i] < 0 || (uint32_t)experts[i] >= P.experts()) return GX_ERR_DOMAIN;
+    std::vector<uint8_t> seen(P.experts(), 0);
+    uint32_t distinct = 0;
+    for (uint32_t i = 0; i < count; ++i)
+        if (!seen[experts[i]]) { seen[experts[i]] = 1; ++distinct; }
+    if (distinct > P.batch_bound(layer)) return GX_ERR_BATCH;
+    gx_serve_stats local{};
+    local.distinct = distinct;
+    P.begin_batch(layer);
+    for (uint32_t i = 0; i < count; ++i) {
+        const gx::ServeOutcome o = P.access(layer, (uint32_t)experts[i]);
+        if (evicted_out) evicted_out[i] = o.evicted;
+        if (hit_out) hit_out[i] = o.hit ? 1 : 0;
+        if (o.evicted >= 0) {
+            P.release_slot(layer, (uint32_t)o.evicted);
+            ++local.evictions;
+        }
+        if (o.hit) {
+            ++local.hits;
+            continue;
+        }
+        ++local.misses;
+        const int32_t s = P.allocate_slot(layer, (uint32_t)experts[i]);
+        if (misses) misses->emplace_back(experts[i], s);
+    }
+    for (uint32_t i = 0; i < count; ++i) {
+        const int32_t s = P.slot_of(layer, (uint32_t)experts[i]);
+        if (s < 0) return GX_ERR_SLOTS;  // a served key without a slot (scripts/derive-remap-strides.py:70)
+        slots[i] = s;
+    }
+    if (st) *st = local;
+    return GX_OK;
+}
+
+}  // namespace
+
+struct gx_arena {
+    gx_policy * policy = nullptr;
+    int device = 0;
+    std::vector<uint64_t> record, record_raw;
+    std::vector<uint64_t> slab_base;    // device offset of each layer's slab
+    std::vector<uint64_t> host_base;    // host-tier offset of each layer's records
+    uint8_t * d_arena = nullptr;
+    uint64_t arena_bytes = 0;
+    uint8_t * h_tier = nullptr;
+    uint64_t tier_bytes = 0;
+    cudaStream_t copy_stream = nullptr;
+    std::vector<cudaEvent_t> ev_done, ev_copy;
+    cudaEvent_t ev_snapshot = nullptr;
+    // layer entry point scratch
+    int64_t max_tokens = 0, hidden = 0, intermediate = 0;
+    uint32_t used = 0;
+    float * d_act = nullptr;            // [I, k, T] activations between gate/up and down
+    int32_t * d_ids = nullptr;          // kStageRing x (used * max_tokens) slot ids
+    int32_t * h_ids = nullptr;          // pinned staging of the same
+    cudaEvent_t ev_stage[kStageRing] = {};
+    int stage_next = 0;
+    gx_arena_stats stats{};
+    std::mutex mu;
+
+    uint32_t L(uint32_t layer) const { return layer - policy->impl.first_layer(); }
+};
+
+extern "C" {
+
+const char * gx_status_string(int status) {
+    switch (status) {
+        case GX_OK: return "ok";
+        case GX_ERR_INVALID: return "invalid argument";
+        case GX_ERR_TYPE: return "weight type without a bit-exact kernel";
+        case GX_ERR_ALIGN: return "row length, base or stride not supported by the staged kernels";
+        case GX_ERR_DOMAIN: return "expert id outside [0, n_expert)";
+        case GX_ERR_BATCH: return "micro-batch holds more distinct experts than the probation segment";
+        case GX_ERR_SLOTS: return "slot ledger exhausted or served key without a slot";
+        case GX_ERR_CUDA: return "CUDA runtime error";
+        case GX_ERR_TIMEOUT: return "bounded device wait ran out";
+        case GX_ERR_NOMEM: return "out of memory";
+        case GX_ERR_COPY: return "host->HBM copy failed";
+        case GX_ERR_STATE: return "call out of order";
+        case GX_ERR_DEVICE: return "a kernel reported an error";
+        default: return "unknown status";
+    }
+}
+
+const char * gx_version(void) { return "galactus_b200 0.1 sm_100a (bulk-TMA row tiles, dp4a integer partials)"; }
+
+int gx_device_init(int device) {
+    return guarded([&] {
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return GX_ERR_CUDA;
+        if (device < 0 || device >= n) return GX_ERR_INVALID;
+        ck(cudaSetDevice(device));
+        ck(cudaFree(nullptr));
+        return GX_OK;
+    });
+}
+
+int gx_device_error(int32_t * code_out) {
+    return guarded([&] {
+        int code = 0;
+        ck(gx::read_and_clear_device_error(&code));
+        if (code_out) *code_out = code;
+        return GX_OK;
+    });
+}
+
+// ------------------------------------------------------------------ policy
+
+int gx_policy_create(const gx_profile * profile, uint64_t capacity_bytes, double protected_fraction, int policy,
+                     const uint32_t * plan_quotas, gx_policy ** out) {
+    if (profile == nullptr || out == nullptr) return GX_ERR_INVALID;
+    return guarded([&] {
+        *out = new gx_policy(make_policy(*profile, capacity_bytes, protected_fraction, policy, plan_quotas));
+        return GX_OK;
+    });
+}
+
+void gx_policy_destroy(gx_policy * policy) { delete policy; }
+
+int gx_policy_quota(const gx_policy * policy, uint32_t layer, uint32_t * quota, uint32_t * protected_quota,
+                    uint32_t * probation_quota) {
+    if (policy == nullptr) return GX_ERR_INVALID;
+    const SlotPolicy & P = policy->impl;
+    if (layer < P.first_layer() || layer > P.last_layer()) return GX_ERR_INVALID;
+    if (quota) *quota = P.quota_of(layer);
+    if (protected_quota) *protected_quota = P.protected_of(layer);
+    if (probation_quota) *probation_quota = P.probation_of(layer);
+    return GX_OK;
+}
+
+int gx_policy_serve(gx_policy * policy, uint32_t layer, const int32_t * experts, uint32_t count, int32_t * slots_out,
+                    uint8_t * hit_out, int32_t * evicted_out, gx_serve_stats * stats) {
+    if (policy == nullptr || (count > 0 && (experts == nullptr || slots_out == nullptr))) return GX_ERR_INVALID;
+    return guarded([&] {
+        return serve_policy(policy->impl, layer, experts, count, slots_out, hit_out, evicted_out, nullptr, stats);
+    });
+}
+
+int32_t gx_policy_slot_of(const gx_policy * policy, uint32_t layer, uint32_t expert) {
+    if (policy == nullptr) return -1;
+    const SlotPolicy & P = policy->impl;
+    if (layer < P.first_layer() || layer > P.last_layer() || expert >= P.experts()) return -1;
+    return P.slot_of(layer, expert);
+}
+
+int gx_policy_counters(const gx_policy * policy, uint64_t * hits, uint64_t * accesses, uint64_t * cold_bytes) {
+    if (policy == nullptr) return GX_ERR_INVALID;
+    if (hits) *hits = policy->impl.hits();
+    if (accesses) *accesses = policy->impl.accesses();
+    if (cold_bytes) *cold_bytes = policy->impl.cold_bytes();
+    return GX_OK;
+}
+
+// ------------------------------------------------------------------- arena
+
+int gx_arena_destroy(gx_arena * a) {
+    if (a == nullptr) return GX_OK;
+    cudaSetDevice(a->device);
+    if (a->copy_stream) cudaStreamSynchronize(a->copy_stream);
+    for (auto e : a->ev_done) if (e) cudaEventDestroy(e);
+    for (auto e : a->ev_copy) if (e) cudaEventDestroy(e);
+    for (auto e : a->ev_stage) if (e) cudaEventDestroy(e);
+    if (a->ev_snapshot) cudaEventDestroy(a->ev_snapshot);
+    if (a->copy_stream) cudaStreamDestroy(a->copy_stream);
+    if (a->d_arena) cudaFree(a->d_arena);
+    if (a->d_act) cudaFree(a->d_act);
+    if (a->d_ids) cudaFree(a->d_ids);
+    if (a->h_ids) cudaFreeHost(a->h_ids);
+    if (a->h_tier) cudaFreeHost(a->h_tier);
+    delete a->policy;
+    delete a;
+    return GX_OK;
+}
+
+int gx_arena_create(const gx_arena_config * c, gx_arena ** out) {
+    if (c == nullptr || out == nullptr) return GX_ERR_INVALID;
+    *out = nullptr;
+    gx_arena * a = new (std::nothrow) gx_arena();
+    if (a == nullptr) return GX_ERR_NOMEM;
+    const int rc = guarded([&] {
+        a->device = c->device;
+        ck(cudaSetDevice(c->device));
+        a->policy = new gx_policy(make_policy(c->profile, c->capacity_bytes, c->protected_fraction, c->policy,
+                                              c->plan_quotas));
+        const SlotPolicy & P = a->policy->impl;
+        const uint32_t n = P.layer_count();
+        a->record.assign(c->profile.record_bytes, c->profile.record_bytes + n);
+        if (c->profile.record_bytes_raw)
+            a->record_raw.assign(c->profile.record_bytes_raw, c->profile.record_bytes_raw + n);
+        else
+            a->record_raw = a->record;
+        for (uint32_t i = 0; i < n; ++i)
+            if (a->record_raw[i] == 0 || a->record_raw[i] > a->record[i]) return GX_ERR_INVALID;
+        uint64_t off = 0, hoff = 0;
+        for (uint32_t i = 0; i < n; ++i) {
+            a->slab_base.push_back(off);
+            off += a->record[i] * P.quota_of(P.first_layer() + i);
+            a->host_base.push_back(hoff);
+            hoff += a->record[i] * P.experts();
+        }
+        a->arena_bytes = off;
+        a->tier_bytes = hoff;
+        ck(cudaMalloc(&a->d_arena, a->arena_bytes));
+        if (c->host_tier) ck(cudaHostAlloc(&a->h_tier, a->tier_bytes, cudaHostAllocDefault));
+        ck(cudaStreamCreateWithFlags(&a->copy_stream, cudaStreamNonBlocking));
+        a->ev_done.resize(n);
+        a->ev_copy.resize(n);
+        for (uint32_t i = 0; i < n; ++i) {
+            ck(cudaEventCreateWithFlags(&a->ev_done[i], cudaEventDisableTiming));
+            ck(cudaEventCreateWithFlags(&a->ev_copy[i], cudaEventDisableTiming));
+        }
+        ck(cudaEventCreateWithFlags(&a->ev_snapshot, cudaEventDisableTiming));
+        a->max_tokens = c->max_tokens;
+        a->used = c->profile.used;
+        a->hidden = c->hidden;
+        a->intermediate = c->intermediate;
+        if (c->max_tokens > 0 && c->intermediate > 0) {
+            const int64_t pairs = (int64_t)c->profile.used * c->max_tokens;
+            ck(cudaMalloc(&a->d_act, (size_t)(pairs * c->intermediate * sizeof(float))));
+            ck(cudaMalloc(&a->d_ids, (size_t)(kStageRing * pairs * sizeof(int32_t))));
+            ck(cudaHostAlloc(&a->h_ids, (size_t)(kStageRing * pairs * sizeof(int32_t)), cudaHostAllocDefault));
+            for (int i = 0; i < kStageRing; ++i) ck(cudaEventCreateWithFlags(&a->ev_stage[i], cudaEventDisableTiming));
+        }
+        return GX_OK;
+    });
+    if (rc != GX_OK) {
+        gx_arena_destroy(a);
+        return rc;
+    }
+    *out = a;
+    return GX_OK;
+}
+
+void * gx_arena_host_record(gx_arena * a, uint32_t layer, uint32_t expert) {
+    if (a == nullptr || a->h_tier == nullptr) return nullptr;
+    const SlotPolicy & P = a->policy->impl;
+    if (layer < P.first_layer() || layer > P.last_layer() || expert >= P.experts()) return nullptr;
+    const uint32_t i = a->L(layer);
+    return a->h_tier + a->host_base[i] + (uint64_t)expert * a->record[i];
+}
+
+int gx_load_record(gx_arena * a, uint32_t layer, uint32_t expert, const void * src, uint64_t bytes) {
+    void * dst = gx_arena_host_record(a, layer, expert);
+    if (dst == nullptr || src == nullptr) return a && a->h_tier == nullptr ? GX_ERR_STATE : GX_ERR_INVALID;
+    if (bytes > a->record[a->L(layer)]) return GX_ERR_INVALID;
+    std::memcpy(dst, src, bytes);
+    return GX_OK;
+}
+
+int gx_arena_layer_view(gx_arena * a, uint32_t layer, void ** base, uint64_t * record_bytes, uint32_t * slots) {
+    if (a == nullptr) return GX_ERR_INVALID;
+    const SlotPolicy & P = a->policy->impl;
+    if (layer < P.first_layer() || layer > P.last_layer()) return GX_ERR_INVALID;
+    const uint32_t i = a->L(layer);
+    if (base) *base = a->d_arena + a->slab_base[i];
+    if (record_bytes) *record_bytes = a->record[i];
+    if (slots) *slots = P.quota_of(layer);
+    return GX_OK;
+}
+
+gx_policy * gx_arena_policy(gx_arena * a) { return a ? a->policy : nullptr; }
+
+int gx_stats(gx_arena * a, gx_arena_stats * s) {
+    if (a == nullptr || s == nullptr) return GX_ERR_INVALID;
+    *s = a->stats;
+    return GX_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Serve a micro-batch and issue one host->HBM copy per miss on the copy
+// stream. The copies start after `after` (the last consumer of the layer's
+// slots) and `consumer` waits for them.
+int arena_serve(gx_arena * a, uint32_t layer, const int32_t * experts, uint32_t count, int32_t * slots,
+                cudaEvent_t after, cudaStream_t consumer, gx_serve_stats * st_out) {
+    std::vector<std::pair<int32_t, int32_t>> misses;
+    gx_serve_stats st{};
+    const int rc = serve_policy(a->policy->impl, layer, experts, count, slots, nullptr, nullptr, &misses, &st);
+    if (rc != GX_OK) return rc;
+    const uint32_t i = a->L(layer);
+    if (!misses.empty()) {
+        if (a->h_tier == nullptr) return GX_ERR_STATE;
+        ck(cudaStreamWaitEvent(a->copy_stream, after, 0));
+        for (const auto & m : misses) {
+            uint8_t * dst = a->d_arena + a->slab_base[i] + (uint64_t)m.second * a->record[i];
+            const uint8_t * src = a->h_tier + a->host_base[i] + (uint64_t)m.first * a->record[i];
+            if (cudaMemcpyAsync(dst, src, a->record_raw[i], cudaMemcpyHostToDevice, a->copy_stream) != cudaSuccess)
+                return GX_ERR_COPY;
+            st.bytes_copied += a->record_raw[i];
+        }
+        ck(cudaEventRecord(a->ev_copy[i], a->copy_stream));
+        ck(cudaStreamWaitEvent(consumer, a->ev_copy[i], 0));
+        a->stats.copies += misses.size();
+    }
+    a->stats.serves += 1;
+    a->stats.hits += st.hits;
+    a->stats.misses += st.misses;
+    a->stats.evictions += st.evictions;
+    a->stats.bytes_h2d += st.bytes_copied;
+    if (st_out) *st_out = st;
+    return GX_OK;
+}
+
+// Rows per expert tile: a divisor of ne01 whose byte span keeps the 16-byte
+// alignment of bulk copies, whose shared memory fits, preferring enough CTAs
+// to fill the 148 SMs several times over.
+int pick_rows(int type, int mode, gx::RowsParams & p, int64_t ctas_per_tile, const int * cands, int ncand) {
+    int best = 0;
+    for (int ci = 0; ci < ncand; ++ci) {
+        const int R = cands[ci];
+        if (p.ne01 % R != 0) continue;
+        if (((int64_t)R * p.nb01) % 16 != 0) continue;
+        p.R = R;
+        if (gx::rows_smem_layout(type, mode, p) == 0) continue;
+        best = R;
+        if ((int64_t)(p.ne01 / R) * ctas_per_tile >= 4 * 148) break;
+    }
+    p.R = best;
+    return best;
+}
+
+bool aligned16(const void * p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int gx_remap_serve(gx_arena * a, uint32_t layer, const int32_t * ids, int64_t ne0, int64_t ne1, int64_t nb0, int64_t nb1,
+                   int32_t * slots, int64_t dnb0, int64_t dnb1, void * stream, gx_serve_stats * stats) {
+    if (a == nullptr || ids == nullptr || slots == nullptr || ne0 < 0 || ne1 < 0) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        ck(cudaSetDevice(a->device));
+        const int64_t n = ne0 * ne1;
+        std::vector<int32_t> experts((size_t)n), sl((size_t)n);
+        // strided read, token-major (scripts/derive-remap-strides.py:30-48)
+        const char * src = reinterpret_cast<const char *>(ids);
+        for (int64_t i1 = 0, f = 0; i1 < ne1; ++i1)
+            for (int64_t i0 = 0; i0 < ne0; ++i0, ++f)
+                experts[(size_t)f] = *reinterpret_cast<const int32_t *>(src + i1 * nb1 + i0 * nb0);
+        cudaStream_t consumer = reinterpret_cast<cudaStream_t>(stream);
+        // everything already queued on the consumer stream may read the slab
+        ck(cudaEventRecord(a->ev_snapshot, consumer));
+        const int rc = arena_serve(a, layer, experts.data(), (uint32_t)n, sl.data(), a->ev_snapshot, consumer, stats);
+        if (rc != GX_OK) return rc;
+        char * dst = reinterpret_cast<char *>(slots);
+        for (int64_t i1 = 0, f = 0; i1 < ne1; ++i1)
+            for (int64_t i0 = 0; i0 < ne0; ++i0, ++f)
+                *reinterpret_cast<int32_t *>(dst + i1 * dnb1 + i0 * dnb0) = sl[(size_t)f];
+        return GX_OK;
+    });
+}
+
+int gx_arena_read_slot(gx_arena * a, uint32_t layer, uint32_t slot, void * dst, uint64_t bytes) {
+    if (a == nullptr || dst == nullptr) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        const SlotPolicy & P = a->policy->impl;
+        if (layer < P.first_layer() || layer > P.last_layer() || slot >= P.quota_of(layer)) return GX_ERR_INVALID;
+        const uint32_t i = a->L(layer);
+        if (bytes > a->record[i]) return GX_ERR_INVALID;
+        ck(cudaSetDevice(a->device));
+        ck(cudaStreamSynchronize(a->copy_stream));
+        ck(cudaMemcpy(dst, a->d_arena + a->slab_base[i] + (uint64_t)slot * a->record[i], bytes, cudaMemcpyDeviceToHost));
+        return GX_OK;
+    });
+}
+
+int gx_arena_warm_all(gx_arena * a, void * stream) {
+    if (a == nullptr) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        ck(cudaSetDevice(a->device));
+        const SlotPolicy & P = a->policy->impl;
+        cudaStream_t consumer = reinterpret_cast<cudaStream_t>(stream);
+        for (uint32_t layer = P.first_layer(); layer <= P.last_layer(); ++layer) {
+            const uint32_t bound = P.batch_bound(layer);
+            for (uint32_t e0 = 0; e0 < P.experts(); e0 += bound) {
+                const uint32_t cnt = std::min(bound, P.experts() - e0);
+                std::vector<int32_t> ex(cnt), sl(cnt);
+                for (uint32_t j = 0; j < cnt; ++j) ex[j] = (int32_t)(e0 + j);
+                ck(cudaEventRecord(a->ev_snapshot, consumer));
+                const int rc = arena_serve(a, layer, ex.data(), cnt, sl.data(), a->ev_snapshot, consumer, nullptr);
+                if (rc != GX_OK) return rc;
+            }
+        }
+        return GX_OK;
+    });
+}
+
+// ----------------------------------------------------------------- kernels
+
+int gx_mul_mat_id(int type, const void * as, int64_t ne00, int64_t ne01, int64_t nb01, int64_t nb02, int64_t n_as,
+                  const float * b, int64_t ne11, int64_t ne12, int64_t nb11, int64_t nb12, const int32_t * ids,
+                  int64_t ne20, int64_t ne21, int64_t nbi1, float * dst, void * stream) {
+    if (!gx::supported_weight_type(type)) return GX_ERR_TYPE;
+    if (as == nullptr || b == nullptr || ids == nullptr || dst == nullptr) return GX_ERR_INVALID;
+    if (ne00 <= 0 || ne01 <= 0 || n_as <= 0 || ne20 <= 0 || ne21 < 0 || ne12 != ne21) return GX_ERR_INVALID;
+    if (ne11 != 1 && ne11 != ne20) return GX_ERR_INVALID;
+    if (ne00 % gx::row_align(type) != 0) return GX_ERR_ALIGN;
+    if (nb01 < gx::row_bytes(type, ne00) || (nb11 % 4) || (nb12 % 4) || (nbi1 % 4)) return GX_ERR_INVALID;
+    if (!aligned16(as) || nb02 % 16 != 0) return GX_ERR_ALIGN;
+    if (ne21 == 0) return GX_OK;
+    if (ne20 * ne21 > 65535) return GX_ERR_INVALID;
+    return guarded([&] {
+        gx::RowsParams p{};
+        p.w0 = static_cast<const uint8_t *>(as);
+        p.nb01 = nb01; p.nb02 = nb02;
+        p.ne00 = (int32_t)ne00; p.ne01 = (int32_t)ne01; p.n_as = (int32_t)n_as;
+        p.src = b; p.nb11 = nb11; p.nb12 = nb12; p.ne11 = (int32_t)ne11;
+        p.ids = ids; p.nbi1 = nbi1; p.k = (int32_t)ne20; p.T = (int32_t)ne21;
+        p.dst = dst;
+        static const int cands[] = {8, 4, 2, 1};
+        if (pick_rows(type, gx::kModePlain, p, ne20 * ne21, cands, 4) == 0) return GX_ERR_ALIGN;
+        const dim3 grid((unsigned)(ne01 / p.R), (unsigned)(ne20 * ne21));
+        ck(gx::launch_rows(type, gx::kModePlain, p, grid, reinterpret_cast<cudaStream_t>(stream)));
+        return GX_OK;
+    });
+}
+
+int gx_quantize_rows(int vdt, const float * src, int64_t ne0, int64_t nrows, int64_t nb1, void * dst, int64_t dst_row_stride,
+                     void * stream) {
+    if (vdt != GX_TYPE_Q8_0 && vdt != GX_TYPE_Q8_K) return GX_ERR_TYPE;
+    if (src == nullptr || dst == nullptr || ne0 <= 0 || nrows < 0 || nb1 % 4) return GX_ERR_INVALID;
+    if (ne0 % (vdt == GX_TYPE_Q8_0 ? 32 : 256) != 0) return GX_ERR_ALIGN;
+    if (dst_row_stride < gx::row_bytes(vdt, ne0)) return GX_ERR_INVALID;
+    if (vdt == GX_TYPE_Q8_K && (dst_row_stride % 4 || !aligned16(dst))) return GX_ERR_ALIGN;
+    return guarded([&] {
+        ck(gx::launch_quantize_rows(vdt, src, (int)ne0, nrows, nb1, static_cast<uint8_t *>(dst), dst_row_stride,
+                                    reinterpret_cast<cudaStream_t>(stream)));
+        return GX_OK;
+    });
+}
+
+int gx_swiglu(const float * g, const float * u, float * out, int64_t n, void * stream) {
+    if (g == nullptr || u == nullptr || out == nullptr || n < 0) return GX_ERR_INVALID;
+    return guarded([&] {
+        ck(gx::launch_swiglu(g, u, out, n, reinterpret_cast<cudaStream_t>(stream)));
+        return GX_OK;
+    });
+}
+
+int gx_swiglu_oai(const float * g, const float * u, float * out, int64_t n, float alpha, float limit, void * stream) {
+    if (g == nullptr || u == nullptr || out == nullptr || n < 0) return GX_ERR_INVALID;
+    return guarded([&] {
+        ck(gx::launch_swiglu_oai(g, u, out, n, alpha, limit, reinterpret_cast<cudaStream_t>(stream)));
+        return GX_OK;
+    });
+}
+
+int gx_combine(const float * y, const float * w, float * out, int64_t H, int64_t k, int64_t T, void * stream) {
+    if (y == nullptr || w == nullptr || out == nullptr || H < 0 || k <= 0 || T < 0) return GX_ERR_INVALID;
+    return guarded([&] {
+        ck(gx::launch_combine(y, w, out, H, (int)k, T, reinterpret_cast<cudaStream_t>(stream)));
+        return GX_OK;
+    });
+}
+
+int gx_expf(const float * x, float * y, int64_t n, void * stream) {
+    if (x == nullptr || y == nullptr || n < 0) return GX_ERR_INVALID;
+    return guarded([&] {
+        ck(gx::launch_expf(x, y, n, reinterpret_cast<cudaStream_t>(stream)));
+        return GX_OK;
+    });
+}
+
+// --------------------------------------------------------------- MoE layer
+
+int gx_moe_layer_forward(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x, const int32_t * ids,
+                         const float * w, int64_t k, int64_t T, float * out, void * stream, gx_serve_stats * stats) {
+    if (a == nullptr || d == nullptr || x == nullptr || ids == nullptr || w == nullptr || out == nullptr) return GX_ERR_INVALID;
+    if (!gx::supported_weight_type(d->type_gate) || !gx::supported_weight_type(d->type_down)) return GX_ERR_TYPE;
+    if (d->type_up != d->type_gate) return GX_ERR_TYPE;
+    if (d->act != GX_ACT_SWIGLU && d->act != GX_ACT_SWIGLU_OAI) return GX_ERR_INVALID;
+    if (T < 0 || k <= 0 || T > a->max_tokens || d->hidden != a->hidden || d->intermediate != a->intermediate)
+        return GX_ERR_INVALID;
+    if (k > (int64_t)a->used) return GX_ERR_INVALID;
+    const int64_t H = d->hidden, I = d->intermediate;
+    if (H % gx::row_align(d->type_gate) != 0 || I % gx::row_align(d->type_down) != 0) return GX_ERR_ALIGN;
+    if (d->off_gate % 16 || d->off_up % 16) return GX_ERR_ALIGN;
+    if (T == 0) return GX_OK;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        ck(cudaSetDevice(a->device));
+        const SlotPolicy & P = a->policy->impl;
+        if (layer < P.first_layer() || layer > P.last_layer()) return GX_ERR_INVALID;
+        const uint32_t li = a->L(layer);
+        if (d->off_up + gx::row_bytes(d->type_up, H) * I > a->record_raw[li] ||
+            (uint64_t)gx::row_bytes(d->type_down, I) * H > d->off_gate)
+            return GX_ERR_INVALID;
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        const int64_t n = k * T;
+        std::vector<int32_t> slots((size_t)n);
+        int rc = arena_serve(a, layer, ids, (uint32_t)n, slots.data(), a->ev_done[li], s, stats);
+        if (rc != GX_OK) return rc;
+
+        uint8_t * base = a->d_arena + a->slab_base[li];
+        gx::RowsParams p{};
+        p.k = (int32_t)k;
+        p.T = (int32_t)T;
+        p.n_as = (int32_t)P.quota_of(layer);
+        p.nb02 = (int64_t)a->record[li];
+        if (n <= gx::kInlineIds) {
+            p.use_inline = 1;
+            for (int64_t j = 0; j < n; ++j) p.inline_ids[j] = slots[(size_t)j];
+        } else {
+            // stage the slot ids through a pinned ring; a ring entry is reused
+            // only after the copy that read it has run
+            const int st = a->stage_next;
+            a->stage_next = (st + 1) % kStageRing;
+            const int64_t stride = (int64_t)a->used * a->max_tokens;
+            if (n > stride) return GX_ERR_INVALID;
+            ck(cudaEventSynchronize(a->ev_stage[st]));
+            int32_t * h = a->h_ids + (size_t)st * stride;
+            int32_t * dd = a->d_ids + (size_t)st * stride;
+            std::memcpy(h, slots.data(), (size_t)n * sizeof(int32_t));
+            ck(cudaMemcpyAsync(dd, h, (size_t)n * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+            ck(cudaEventRecord(a->ev_stage[st], s));
+            p.ids = dd;
+            p.nbi1 = k * 4;
+        }
+
+        // gate + up + activation -> act [I, k, T]
+        gx::RowsParams g = p;
+        g.w0 = base + d->off_gate;
+        g.w1 = base + d->off_up;
+        g.nb01 = gx::row_bytes(d->type_gate, H);
+        g.ne00 = (int32_t)H;
+        g.ne01 = (int32_t)I;
+        g.src = x;
+        g.nb11 = H * 4;
+        g.nb12 = H * 4;
+        g.ne11 = 1;
+        g.dst = a->d_act;
+        g.act = d->act;
+        g.alpha = d->alpha;
+        g.limit = d->limit;
+        static const int cands_gu[] = {8, 4, 2, 1};
+        if (pick_rows(d->type_gate, gx::kModeGateUp, g, n, cands_gu, 4) == 0) return GX_ERR_ALIGN;
+        ck(gx::launch_rows(d->type_gate, gx::kModeGateUp, g, dim3((unsigned)(I / g.R), (unsigned)n), s));
+
+        // down + weighted combine in slot order -> out [H, T]
+        gx::RowsParams dn = p;
+        dn.w0 = base;
+        dn.nb01 = gx::row_bytes(d->type_down, I);
+        dn.ne00 = (int32_t)I;
+        dn.ne01 = (int32_t)H;
+        dn.src = a->d_act;
+        dn.nb11 = I * 4;
+        dn.nb12 = I * k * 4;
+        dn.ne11 = (int32_t)k;
+        dn.rw = w;
+        dn.dst = out;
+        static const int cands_dn[] = {8, 4, 2, 1};
+        if (pick_rows(d->type_down, gx::kModeDownCombine, dn, T, cands_dn, 4) == 0) return GX_ERR_ALIGN;
+        ck(gx::launch_rows(d->type_down, gx::kModeDownCombine, dn, dim3((unsigned)(H / dn.R), (unsigned)T), s));
+        ck(cudaEventRecord(a->ev_done[li], s));
+        return GX_OK;
+    });
+}
+
+// --------------------------------------------------------------- synthetic
+
+int gx_synth_normal(float * dst, int64_t n, uint64_t seed, uint64_t stream_id, float sigma, void * stream) {
+    if (dst == nullptr || n < 0) return GX_ERR_INVALID;
+    return guarded([&] {
+        ck(gx::launch_synth_normal(dst, n, seed, stream_id, sigma, reinterpret_cast<cudaStream_t>(stream)));
+        return GX_OK;
+    });
+}
+
+int gx_synth_weights(int type, void * dst, int64_t ne00, int64_t n_rows, uint64_t seed, uint64_t stream_id, float sigma,
+                     void * stream) {
+    if (!gx::supported_weight_type(type)) return GX_ERR_TYPE;
+    if (dst == nullptr || ne00 <= 0 || n_rows < 0) return GX_ERR_INVALID;
+    if (ne00 % gx::block_elems(type) != 0) return GX_ERR_ALIGN;
+    return guarded([&] {
+        ck(gx::launch_synth_weights(type, dst, ne00, n_rows, seed, stream_id, sigma, reinterpret_cast<cudaStream_t>(stream)));
+        return GX_OK;
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,539 @@
+// CUDA kernels of the routed-expert FFN (sm_100a).
+//
+// The expert contraction runs on row tiles: one CTA stages R consecutive rows
+// of an expert matrix (a contiguous byte range of the slot arena) into shared
+// memory with one bulk TMA copy (cp.async.bulk, completion on an mbarrier),
+// quantizes its activation row(s) to Q8_0/Q8_K while the copy is in flight,
+// then computes every output of the tile in two phases: exact integer partial
+// sums per 64-element unit (all threads, any order), then the float tail of
+// the reference's CPU loop, serially per row and chain, in unit order.
+//
+// Three modes share that core:
+//   PLAIN         ggml_mul_mat_id: one (token, slot) pair, R rows -> dst
+//   GATE_UP       gate and up tiles of one (token, slot), then SwiGLU / SWIGLU_OAI
+//   DOWN_COMBINE  the k down tiles of one token, then the weighted sum in slot order
+#include <cstdint>
+#include <cstdio>
+#include <cuda_runtime.h>
+
+#include "gx_device.cuh"
+#include "gx_kernels.h"
+
+namespace gx {
+
+__device__ int g_dev_error = 0;
+
+__device__ __forceinline__ void record_error(int code) { atomicCAS(&g_dev_error, 0, code); }
+
+// --------------------------------------------------------- TMA / mbarrier
+
+__device__ __forceinline__ uint32_t smem_u32(const void * p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// bulk copy global -> shared, completion counted on the mbarrier (no multicast)
+__device__ __forceinline__ void bulk_g2s(void * dst_smem, const void * src_gmem, uint32_t bytes, uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Every wait is bounded: after the limit the kernel records a timeout and
+// gives up instead of spinning forever.
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t * bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+    }
+    return false;
+}
+
+// ------------------------------------------------------------ row kernel
+
+enum { MODE_PLAIN = 0, MODE_GATE_UP = 1, MODE_DOWN_COMBINE = 2 };
+
+__device__ __forceinline__ int32_t get_id(const RowsParams & p, int t, int s) {
+    if (p.use_inline) return p.inline_ids[t * p.k + s];
+    return *reinterpret_cast<const int32_t *>(reinterpret_cast<const char *>(p.ids) + (int64_t)t * p.nbi1 + 4 * s);
+}
+
+template <int TYPE, int MODE>
+__global__ void __launch_bounds__(kRowsThreads) k_rows(const RowsParams p) {
+    using D = Dot<TYPE>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t * bar = reinterpret_cast<uint64_t *>(smem + p.bar_off);
+    uint8_t * tile = smem + p.tile_off;
+    uint8_t * act = smem + p.act_off;
+    uint32_t * terms = reinterpret_cast<uint32_t *>(smem + p.terms_off);
+    float * dots = reinterpret_cast<float *>(smem + p.dots_off);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nwarps = kRowsThreads / 32;
+    const int R = p.R;
+    const int r0 = blockIdx.x * R;
+    const int n_exp = MODE == MODE_DOWN_COMBINE ? p.k : 1;
+    const int NR = MODE == MODE_GATE_UP ? 2 * R : n_exp * R;
+    const int U = p.ne00 / 64;
+    const uint32_t tile_bytes = (uint32_t)(R * p.nb01);
+
+    int t, s0;
+    if (MODE == MODE_DOWN_COMBINE) { t = blockIdx.y; s0 = 0; }
+    else { t = blockIdx.y / p.k; s0 = blockIdx.y % p.k; }
+
+    // expert ids of this CTA, checked before any load
+    bool bad = false;
+    for (int i = 0; i < n_exp; ++i) {
+        const int32_t e = get_id(p, t, s0 + i);
+        if (e < 0 || e >= p.n_as) bad = true;
+    }
+    if (bad) {
+        if (tid == 0) record_error(GX_DEVERR_DOMAIN);
+        for (int r = tid; r < R; r += blockDim.x) {
+            const float nanv = __int_as_float(0x7fc00000);
+            if (MODE == MODE_DOWN_COMBINE) p.dst[(int64_t)t * p.ne01 + r0 + r] = nanv;
+            else p.dst[((int64_t)t * p.k + s0) * p.ne01 + r0 + r] = nanv;
+        }
+        return;
+    }
+
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t total = tile_bytes * (uint32_t)(MODE == MODE_GATE_UP ? 2 : n_exp);
+        mbar_arrive_expect_tx(bar, total);
+        if (MODE == MODE_GATE_UP) {
+            const int32_t e = get_id(p, t, s0);
+            bulk_g2s(tile, p.w0 + (int64_t)e * p.nb02 + (int64_t)r0 * p.nb01, tile_bytes, bar);
+            bulk_g2s(tile + tile_bytes, p.w1 + (int64_t)e * p.nb02 + (int64_t)r0 * p.nb01, tile_bytes, bar);
+        } else {
+            for (int i = 0; i < n_exp; ++i) {
+                const int32_t e = get_id(p, t, s0 + i);
+                bulk_g2s(tile + (uint32_t)i * tile_bytes, p.w0 + (int64_t)e * p.nb02 + (int64_t)r0 * p.nb01, tile_bytes, bar);
+            }
+        }
+    }
+
+    // quantize the activation row(s) while the weights are in flight
+    for (int a = 0; a < p.n_act; ++a) {
+        int s_row;
+        if (MODE == MODE_DOWN_COMBINE) s_row = a;
+        else if (MODE == MODE_PLAIN) s_row = s0 % p.ne11;
+        else s_row = 0;
+        const float * x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(p.src) + (int64_t)t * p.nb12 +
+                                                          (int64_t)s_row * p.nb11);
+        quantize_row_cta<D::VDT>(x, p.ne00, act + a * p.act_pitch, warp, nwarps, lane);
+    }
+    __syncthreads();
+
+    if (!mbar_wait_bounded(bar, 0)) {
+        if (tid == 0) record_error(GX_DEVERR_TIMEOUT);
+        mbar_wait_bounded(bar, 0);  // give copies in flight one more bounded chance
+        return;
+    }
+
+    // phase 1: integer partial sums and block scales of every (row, unit)
+    const int items = NR * U;
+    for (int it = tid; it < items; it += kRowsThreads) {
+        const int r = it / U, u = it - r * U;
+        const uint8_t * arow = act + (MODE == MODE_DOWN_COMBINE ? (r / R) * p.act_pitch : 0);
+        D::unit(tile, r * (int)p.nb01, arow, u, terms + ((size_t)r * U + u) * D::TERMS);
+    }
+    __syncthreads();
+
+    // phase 2: the serial float tail, one thread per (row, chain)
+    const int chains = NR * D::CHAINS;
+    for (int base = 0; base < chains; base += kRowsThreads) {
+        const int it = base + tid;
+        const bool ok = it < chains;
+        const int r = it / D::CHAINS, c = it % D::CHAINS;
+        float v = ok ? D::chain(terms + (size_t)r * U * D::TERMS, U, c) : 0.0f;
+        if (D::CHAINS == 8) {
+            // ((e0+e1)+(e2+e3)) + ((o0+o1)+(o2+o3)) on lane c == 0 of each group of 8
+            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+        }
+        if (ok && c == 0) dots[r] = v;
+    }
+    __syncthreads();
+
+    // epilogue
+    for (int r = tid; r < R; r += kRowsThreads) {
+        if (MODE == MODE_PLAIN) {
+            p.dst[((int64_t)t * p.k + s0) * p.ne01 + r0 + r] = dots[r];
+        } else if (MODE == MODE_GATE_UP) {
+            const float g = dots[r], u = dots[R + r];
+            const float a = p.act == 1 ? act_swiglu_oai(g, u, p.alpha, p.limit) : act_swiglu(g, u);
+            p.dst[((int64_t)t * p.k + s0) * p.ne01 + r0 + r] = a;
+        } else {
+            const float * w = p.rw + (int64_t)t * p.k;
+            float acc = __fmul_rn(dots[r], w[0]);
+            for (int s = 1; s < p.k; ++s) acc = __fadd_rn(acc, __fmul_rn(dots[s * R + r], w[s]));
+            p.dst[(int64_t)t * p.ne01 + r0 + r] = acc;
+        }
+    }
+}
+
+// ------------------------------------------------------- small kernels
+
+template <int VDT>
+__global__ void k_quantize_rows(const float * src, int ne0, int64_t nb1, uint8_t * dst, int64_t pitch, int nblocks) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int ib = blockIdx.y * (blockDim.x / 32) + w;
+    if (ib >= nblocks) return;
+    const float * x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(src) + (int64_t)blockIdx.x * nb1);
+    uint8_t * row = dst + (int64_t)blockIdx.x * pitch;
+    if (VDT == GX_T_Q8_0) {
+        quantize_q8_0_block_warp(x[ib * 32 + lane], row + ib * 34, lane);
+    } else {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = x[ib * 256 + 8 * lane + j];
+        quantize_q8_K_block_warp(v, row + ib * 292, lane);
+    }
+}
+
+__global__ void k_swiglu(const float * g, const float * u, float * out, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = act_swiglu(g[i], u[i]);
+}
+
+__global__ void k_swiglu_oai(const float * g, const float * u, float * out, int64_t n, float alpha, float limit) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = act_swiglu_oai(g[i], u[i], alpha, limit);
+}
+
+__global__ void k_expf(const float * x, float * y, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = gx_expf(x[i]);
+}
+
+__global__ void k_combine(const float * y, const float * w, float * out, int64_t H, int k, int64_t T) {
+    const int64_t n = H * T;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / H, h = i - t * H;
+        const float * wt = w + t * k;
+        float acc = __fmul_rn(y[(t * k) * H + h], wt[0]);
+        for (int s = 1; s < k; ++s) acc = __fadd_rn(acc, __fmul_rn(y[(t * k + s) * H + h], wt[s]));
+        out[i] = acc;
+    }
+}
+
+// ----------------------------------------------------------- synthetic data
+// Counter-based generator (splitmix64 finaliser of Steele, Lea & Flood 2014),
+// N(0,1) approximated by the standardised sum of four 16-bit uniforms
+// (Irwin-Hall, n = 4). Restated identically in the oracle.
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ uint64_t synth_bits(uint64_t key, uint64_t i) { return splitmix64(key + i * 0xD1B54A32D192ED03ull); }
+
+__device__ __forceinline__ float synth_normal(uint64_t key, uint64_t i, float sigma) {
+    const uint64_t b = synth_bits(key, i);
+    const int S = (int)(b & 0xffff) + (int)((b >> 16) & 0xffff) + (int)((b >> 32) & 0xffff) + (int)((b >> 48) & 0xffff);
+    const float z = __fmul_rn((float)(S - 131070), 2.642899744e-05f);
+    return __fmul_rn(z, sigma);
+}
+
+__global__ void k_synth_normal(float * dst, int64_t n, uint64_t key, float sigma) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = synth_normal(key, (uint64_t)i, sigma);
+}
+
+__device__ __forceinline__ float clampf(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+// one thread per block / superblock
+__global__ void k_synth_weights(int type, uint8_t * dst, int64_t ne00, int64_t n_rows, uint64_t key, float sigma) {
+    const int be = block_elems(type), bb = block_bytes(type);
+    const int64_t bpr = ne00 / be;
+    const int64_t nblk = bpr * n_rows;
+    for (int64_t bi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; bi < nblk; bi += (int64_t)gridDim.x * blockDim.x) {
+        uint8_t * o = dst + bi * bb;
+        const int64_t row = bi / bpr, col = bi - row * bpr;
+        const uint64_t e0 = (uint64_t)(row * ne00 + col * be);
+        if (type == GX_T_Q8_0) {
+            float x[32];
+            float amax = 0.0f;
+            for (int j = 0; j < 32; ++j) {
+                x[j] = synth_normal(key, e0 + j, sigma);
+                const float a = fabsf(x[j]);
+                if (a > amax) amax = a;
+            }
+            const float d = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            const uint16_t h = f2h(d);
+            o[0] = (uint8_t)(h & 0xff);
+            o[1] = (uint8_t)(h >> 8);
+            for (int j = 0; j < 32; ++j) o[2 + j] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(x[j], id));
+        } else if (type == GX_T_Q4_K) {
+            float x[256];
+            for (int j = 0; j < 256; ++j) x[j] = synth_normal(key, e0 + j, sigma);
+            float scf[8], mnf[8];
+            for (int sb = 0; sb < 8; ++sb) {
+                float mn = x[32 * sb], mx = mn;
+                for (int j = 1; j < 32; ++j) {
+                    const float v = x[32 * sb + j];
+                    if (v < mn) mn = v;
+                    if (v > mx) mx = v;
+                }
+                if (mn > 0.0f) mn = 0.0f;
+                scf[sb] = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+                mnf[sb] = -mn;
+            }
+            float maxsc = 0.0f, maxmn = 0.0f;
+            for (int sb = 0; sb < 8; ++sb) {
+                if (scf[sb] > maxsc) maxsc = scf[sb];
+                if (mnf[sb] > maxmn) maxmn = mnf[sb];
+            }
+            const uint16_t d16 = f2h(__fdiv_rn(maxsc, 63.0f)), dm16 = f2h(__fdiv_rn(maxmn, 63.0f));
+            const float df = h2f(d16), dmf = h2f(dm16);
+            int sc[8], mq[8];
+            uint8_t q[256];
+            for (int sb = 0; sb < 8; ++sb) {
+                sc[sb] = df > 0.0f ? __float2int_rn(clampf(__fdiv_rn(scf[sb], df), 0.0f, 63.0f)) : 0;
+                mq[sb] = dmf > 0.0f ? __float2int_rn(clampf(__fdiv_rn(mnf[sb], dmf), 0.0f, 63.0f)) : 0;
+                const float ds = __fmul_rn(df, (float)sc[sb]), dm = __fmul_rn(dmf, (float)mq[sb]);
+                for (int j = 0; j < 32; ++j) {
+                    q[32 * sb + j] = ds > 0.0f ? (uint8_t)__float2int_rn(clampf(__fdiv_rn(__fadd_rn(x[32 * sb + j], dm), ds), 0.0f, 15.0f)) : 0;
+                }
+            }
+            o[0] = (uint8_t)(d16 & 0xff); o[1] = (uint8_t)(d16 >> 8);
+            o[2] = (uint8_t)(dm16 & 0xff); o[3] = (uint8_t)(dm16 >> 8);
+            uint8_t * s = o + 4;
+            for (int j = 0; j < 4; ++j) {
+                s[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+                s[j + 4] = (uint8_t)((mq[j] & 63) | ((mq[j + 4] >> 4) << 6));
+                s[j + 8] = (uint8_t)((sc[j + 4] & 15) | ((mq[j + 4] & 15) << 4));
+            }
+            for (int j = 0; j < 4; ++j)
+                for (int m = 0; m < 32; ++m) o[16 + 32 * j + m] = (uint8_t)(q[64 * j + m] | (q[64 * j + 32 + m] << 4));
+        } else if (type == GX_T_Q6_K) {
+            float x[256];
+            for (int j = 0; j < 256; ++j) x[j] = synth_normal(key, e0 + j, sigma);
+            float scf[16];
+            float maxs = 0.0f;
+            for (int g = 0; g < 16; ++g) {
+                float amax = 0.0f;
+                for (int j = 0; j < 16; ++j) {
+                    const float a = fabsf(x[16 * g + j]);
+                    if (a > amax) amax = a;
+                }
+                scf[g] = __fdiv_rn(amax, 31.0f);
+                if (scf[g] > maxs) maxs = scf[g];
+            }
+            const uint16_t d16 = f2h(__fdiv_rn(maxs, 127.0f));
+            const float df = h2f(d16);
+            for (int j = 0; j < 208; ++j) o[j] = 0;
+            for (int g = 0; g < 16; ++g) {
+                const int sc = df > 0.0f ? __float2int_rn(clampf(__fdiv_rn(scf[g], df), 0.0f, 127.0f)) : 0;
+                o[192 + g] = (uint8_t)(int8_t)sc;
+                const float ds = __fmul_rn(df, (float)sc);
+                for (int j = 0; j < 16; ++j) {
+                    const int e = 16 * g + j;
+                    const int qv = ds > 0.0f ? __float2int_rn(clampf(__fdiv_rn(x[e], ds), -32.0f, 31.0f)) : 0;
+                    const int code = qv + 32;
+                    const int hh = e / 128, r = e % 128;
+                    o[64 * hh + (r % 64)] |= (uint8_t)((code & 15) << (r < 64 ? 0 : 4));
+                    o[128 + 32 * hh + (r % 32)] |= (uint8_t)((code >> 4) << (2 * (r / 32)));
+                }
+            }
+            o[208] = (uint8_t)(d16 & 0xff);
+            o[209] = (uint8_t)(d16 >> 8);
+        } else if (type == GX_T_MXFP4) {
+            const uint64_t w0 = synth_bits(key, 3 * (uint64_t)bi), w1 = synth_bits(key, 3 * (uint64_t)bi + 1),
+                           w2 = synth_bits(key, 3 * (uint64_t)bi + 2);
+            o[0] = (uint8_t)(118 + (w0 & 7));
+            for (int j = 0; j < 8; ++j) { o[1 + j] = (uint8_t)(w1 >> (8 * j)); o[9 + j] = (uint8_t)(w2 >> (8 * j)); }
+        } else if (type == GX_T_IQ1_S) {
+            uint64_t w[7];
+            for (int j = 0; j < 7; ++j) w[j] = synth_bits(key, 8 * (uint64_t)bi + j);
+            const uint16_t d16 = (uint16_t)(0x1400u | (w[0] & 0x3ffu));
+            o[0] = (uint8_t)(d16 & 0xff); o[1] = (uint8_t)(d16 >> 8);
+            for (int j = 0; j < 32; ++j) o[2 + j] = (uint8_t)(w[1 + j / 8] >> (8 * (j % 8)));
+            for (int j = 0; j < 16; ++j) o[34 + j] = (uint8_t)(w[5 + j / 8] >> (8 * (j % 8)));
+        }
+    }
+}
+
+// -------------------------------------------------------------- launchers
+
+static int grid_1d(int64_t n, int threads) {
+    int64_t b = (n + threads - 1) / threads;
+    if (b > 148 * 32) b = 148 * 32;
+    if (b < 1) b = 1;
+    return (int)b;
+}
+
+uint64_t synth_key(uint64_t seed, uint64_t stream_id) {
+    auto sm = [](uint64_t z) {
+        z += 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    return sm(seed ^ sm(stream_id + 0x632BE59BD9B4E019ull));
+}
+
+template <int TYPE, int MODE>
+static cudaError_t launch_rows_t(const RowsParams & p, dim3 grid, uint32_t smem, cudaStream_t stream) {
+    static int configured_smem = 0;  // per instantiation, single device process
+    if ((int)smem > configured_smem) {
+        cudaError_t e = cudaFuncSetAttribute(k_rows<TYPE, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured_smem = (int)smem;
+    }
+    k_rows<TYPE, MODE><<<grid, kRowsThreads, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <int MODE>
+static cudaError_t launch_rows_mode(int type, const RowsParams & p, dim3 grid, uint32_t smem, cudaStream_t stream) {
+    switch (type) {
+        case GX_T_Q8_0: return launch_rows_t<GX_T_Q8_0, MODE>(p, grid, smem, stream);
+        case GX_T_MXFP4: return launch_rows_t<GX_T_MXFP4, MODE>(p, grid, smem, stream);
+        case GX_T_Q4_K: return launch_rows_t<GX_T_Q4_K, MODE>(p, grid, smem, stream);
+        case GX_T_Q6_K: return launch_rows_t<GX_T_Q6_K, MODE>(p, grid, smem, stream);
+        case GX_T_IQ1_S: return launch_rows_t<GX_T_IQ1_S, MODE>(p, grid, smem, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+static int terms_per_unit(int type) {
+    switch (type) {
+        case GX_T_Q8_0: return Dot<GX_T_Q8_0>::TERMS;
+        case GX_T_MXFP4: return Dot<GX_T_MXFP4>::TERMS;
+        case GX_T_Q4_K: return Dot<GX_T_Q4_K>::TERMS;
+        case GX_T_Q6_K: return Dot<GX_T_Q6_K>::TERMS;
+        case GX_T_IQ1_S: return Dot<GX_T_IQ1_S>::TERMS;
+        default: return 0;
+    }
+}
+
+static uint32_t align_up(uint64_t v, uint64_t a) { return (uint32_t)((v + a - 1) / a * a); }
+
+// Lay out shared memory for a tile of NR rows and n_act activation rows.
+// Returns the byte count, or 0 when it does not fit.
+uint32_t rows_smem_layout(int type, int mode, RowsParams & p) {
+    const int n_exp = mode == MODE_DOWN_COMBINE ? p.k : 1;
+    const int NR = mode == MODE_GATE_UP ? 2 * p.R : n_exp * p.R;
+    const int vdt = vec_dot_type(type);
+    const int U = p.ne00 / 64;
+    p.act_pitch = (int32_t)align_up((uint64_t)row_bytes(vdt, p.ne00), 16);
+    p.n_act = mode == MODE_DOWN_COMBINE ? p.k : 1;
+    uint64_t off = 0;
+    p.bar_off = 0;
+    off = 128;
+    p.tile_off = (uint32_t)off;
+    off = align_up(off + (uint64_t)NR * p.nb01 + 16, 128);
+    p.act_off = (uint32_t)off;
+    off = align_up(off + (uint64_t)p.n_act * p.act_pitch + 16, 128);
+    p.terms_off = (uint32_t)off;
+    off = align_up(off + (uint64_t)NR * U * terms_per_unit(type) * 4, 128);
+    p.dots_off = (uint32_t)off;
+    off = align_up(off + (uint64_t)NR * 4, 128);
+    if (off > kMaxSmem) return 0;
+    return (uint32_t)off;
+}
+
+cudaError_t launch_rows(int type, int mode, RowsParams & p, dim3 grid, cudaStream_t stream) {
+    const uint32_t smem = rows_smem_layout(type, mode, p);
+    if (smem == 0) return cudaErrorInvalidConfiguration;
+    switch (mode) {
+        case MODE_PLAIN: return launch_rows_mode<MODE_PLAIN>(type, p, grid, smem, stream);
+        case MODE_GATE_UP: return launch_rows_mode<MODE_GATE_UP>(type, p, grid, smem, stream);
+        case MODE_DOWN_COMBINE: return launch_rows_mode<MODE_DOWN_COMBINE>(type, p, grid, smem, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_quantize_rows(int vdt, const float * src, int ne0, int64_t nrows, int64_t nb1, uint8_t * dst, int64_t pitch,
+                                 cudaStream_t stream) {
+    if (nrows <= 0) return cudaSuccess;
+    const int nblocks = vdt == GX_T_Q8_0 ? ne0 / 32 : ne0 / 256;
+    const dim3 grid((unsigned)nrows, (unsigned)((nblocks + 3) / 4));
+    if (vdt == GX_T_Q8_0) k_quantize_rows<GX_T_Q8_0><<<grid, 128, 0, stream>>>(src, ne0, nb1, dst, pitch, nblocks);
+    else k_quantize_rows<GX_T_Q8_K><<<grid, 128, 0, stream>>>(src, ne0, nb1, dst, pitch, nblocks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu(const float * g, const float * u, float * out, int64_t n, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    k_swiglu<<<grid_1d(n, 256), 256, 0, stream>>>(g, u, out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_oai(const float * g, const float * u, float * out, int64_t n, float alpha, float limit,
+                              cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    k_swiglu_oai<<<grid_1d(n, 256), 256, 0, stream>>>(g, u, out, n, alpha, limit);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_expf(const float * x, float * y, int64_t n, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    k_expf<<<grid_1d(n, 256), 256, 0, stream>>>(x, y, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const float * y, const float * w, float * out, int64_t H, int k, int64_t T, cudaStream_t stream) {
+    if (H * T <= 0) return cudaSuccess;
+    k_combine<<<grid_1d(H * T, 256), 256, 0, stream>>>(y, w, out, H, k, T);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth_normal(float * dst, int64_t n, uint64_t seed, uint64_t stream_id, float sigma, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    k_synth_normal<<<grid_1d(n, 256), 256, 0, stream>>>(dst, n, synth_key(seed, stream_id), sigma);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth_weights(int type, void * dst, int64_t ne00, int64_t n_rows, uint64_t seed, uint64_t stream_id,
+                                 float sigma, cudaStream_t stream) {
+    const int64_t nblk = (ne00 / block_elems(type)) * n_rows;
+    if (nblk <= 0) return cudaSuccess;
+    const int threads = (type == GX_T_Q4_K || type == GX_T_Q6_K) ? 64 : 256;
+    k_synth_weights<<<grid_1d(nblk, threads), threads, 0, stream>>>(type, (uint8_t *)dst, ne00, n_rows,
+                                                                     synth_key(seed, stream_id), sigma);
+    return cudaGetLastError();
+}
+
+cudaError_t read_and_clear_device_error(int * code) {
+    int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(code, g_dev_error, sizeof(int));
+    if (e != cudaSuccess) return e;
+    return cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(int));
+}
+
+}  // namespace gx

@@ -1,0 +1,245 @@
+"""Python face of the C-ABI: the slot policy, the HBM arena with its host tier,
+the remap node, mul_mat_id and the MoE layer entry point.
+
+Device buffers are passed as raw device addresses (ints) or as objects with a
+``data_ptr()`` method (torch tensors); streams as cudaStream_t handles (ints).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+
+from . import _lib as L
+from .models import ModelShape
+
+
+def _ptr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return int(x.data_ptr())
+    if isinstance(x, np.ndarray):
+        return int(x.ctypes.data)
+    raise TypeError(f"cannot take the address of {type(x)}")
+
+
+def _stream(s) -> int:
+    if s is None:
+        return 0
+    if isinstance(s, int):
+        return s
+    if hasattr(s, "cuda_stream"):
+        return int(s.cuda_stream)
+    raise TypeError(f"not a stream: {type(s)}")
+
+
+@dataclass(frozen=True)
+class LayerShape:
+    hidden: int
+    intermediate: int
+    type_gate: int
+    type_up: int
+    type_down: int
+    act: int = L.ACT_SWIGLU
+    alpha: float = 1.702
+    limit: float = 7.0
+
+    @staticmethod
+    def of(m: ModelShape) -> "LayerShape":
+        return LayerShape(m.hidden, m.intermediate, m.type_gate, m.type_up, m.type_down, m.act, m.alpha, m.limit)
+
+
+def record_layout(m: ModelShape) -> dict:
+    return {"down": (0, m.down_bytes), "gate": (m.off_gate, m.gate_bytes), "up": (m.off_up, m.up_bytes),
+            "raw": m.record_raw, "record": m.record}
+
+
+def _profile(first: int, last: int, experts: int, used: int, record: Sequence[int], raw: Sequence[int]):
+    n = last - first + 1
+    rec = (C.c_uint64 * n)(*record)
+    rraw = (C.c_uint64 * n)(*raw)
+    prof = L.gx_profile(first, last, experts, used, C.cast(rec, C.POINTER(C.c_uint64)),
+                        C.cast(rraw, C.POINTER(C.c_uint64)))
+    return prof, (rec, rraw)
+
+
+class SlotPolicy:
+    """Host-only slot policy and ledger (gx_policy_*)."""
+
+    def __init__(self, first_layer: int, last_layer: int, experts: int, used: int, record_bytes: Sequence[int],
+                 capacity_bytes: int, protected_fraction: float = 0.75, policy: int = L.POLICY_AUTO,
+                 plan_quotas: Sequence[int] | None = None):
+        self._lib = L.lib()
+        prof, self._keep = _profile(first_layer, last_layer, experts, used, record_bytes, record_bytes)
+        plan = None
+        if plan_quotas is not None:
+            plan = (C.c_uint32 * len(plan_quotas))(*plan_quotas)
+        h = C.c_void_p()
+        L.check(self._lib.gx_policy_create(C.byref(prof), capacity_bytes, protected_fraction, policy,
+                                           C.cast(plan, C.POINTER(C.c_uint32)) if plan is not None else None,
+                                           C.byref(h)), "gx_policy_create")
+        self.h = h
+        self.first_layer, self.last_layer, self.experts = first_layer, last_layer, experts
+
+    def close(self):
+        if self.h:
+            self._lib.gx_policy_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def quota(self, layer: int) -> tuple[int, int, int]:
+        q, p, b = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        L.check(self._lib.gx_policy_quota(self.h, layer, C.byref(q), C.byref(p), C.byref(b)), "gx_policy_quota")
+        return q.value, p.value, b.value
+
+    def serve(self, layer: int, experts: Sequence[int]):
+        n = len(experts)
+        ex = (C.c_int32 * max(n, 1))(*experts)
+        slots = (C.c_int32 * max(n, 1))()
+        hits = (C.c_uint8 * max(n, 1))()
+        ev = (C.c_int32 * max(n, 1))()
+        st = L.gx_serve_stats()
+        rc = self._lib.gx_policy_serve(self.h, layer, ex, n, slots, hits, ev, C.byref(st))
+        L.check(rc, "gx_policy_serve")
+        return list(slots[:n]), [bool(h) for h in hits[:n]], list(ev[:n]), st
+
+    def slot_of(self, layer: int, expert: int) -> int:
+        return self._lib.gx_policy_slot_of(self.h, layer, expert)
+
+    def counters(self) -> tuple[int, int, int]:
+        a, b, c = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        L.check(self._lib.gx_policy_counters(self.h, C.byref(a), C.byref(b), C.byref(c)))
+        return a.value, b.value, c.value
+
+
+class Arena:
+    """HBM slot arena + pinned host tier + remap node (gx_arena_*)."""
+
+    def __init__(self, model: ModelShape, capacity_bytes: int, *, protected_fraction: float = 0.75,
+                 policy: int = L.POLICY_AUTO, device: int = 0, host_tier: bool = True, max_tokens: int = 1,
+                 first_layer: int = 0, plan_quotas: Sequence[int] | None = None):
+        self._lib = L.lib()
+        self.model = model
+        self.first_layer = first_layer
+        self.last_layer = first_layer + model.layers - 1
+        prof, self._keep = _profile(first_layer, self.last_layer, model.experts, model.used,
+                                    [model.record] * model.layers, [model.record_raw] * model.layers)
+        cfg = L.gx_arena_config()
+        cfg.profile = prof
+        cfg.capacity_bytes = capacity_bytes
+        cfg.protected_fraction = protected_fraction
+        cfg.policy = policy
+        self._plan = (C.c_uint32 * len(plan_quotas))(*plan_quotas) if plan_quotas is not None else None
+        cfg.plan_quotas = C.cast(self._plan, C.POINTER(C.c_uint32)) if self._plan is not None else None
+        cfg.device = device
+        cfg.host_tier = 1 if host_tier else 0
+        cfg.max_tokens = max_tokens
+        cfg.hidden = model.hidden
+        cfg.intermediate = model.intermediate
+        h = C.c_void_p()
+        L.check(self._lib.gx_arena_create(C.byref(cfg), C.byref(h)), "gx_arena_create")
+        self.h = h
+        self.desc = L.gx_layer_desc(model.type_gate, model.type_up, model.type_down, model.act, model.alpha,
+                                    model.limit, model.hidden, model.intermediate, model.off_gate, model.off_up)
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._lib.gx_arena_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # host tier
+    def host_record(self, layer: int, expert: int) -> np.ndarray:
+        p = self._lib.gx_arena_host_record(self.h, layer, expert)
+        if not p:
+            raise L.GxError(L.GX_ERR_STATE, "gx_arena_host_record")
+        return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_uint8)), shape=(self.model.record,))
+
+    def host_record_ptr(self, layer: int, expert: int) -> int:
+        p = self._lib.gx_arena_host_record(self.h, layer, expert)
+        if not p:
+            raise L.GxError(L.GX_ERR_STATE, "gx_arena_host_record")
+        return int(p)
+
+    def load_record(self, layer: int, expert: int, data: np.ndarray) -> None:
+        data = np.ascontiguousarray(data, dtype=np.uint8)
+        L.check(self._lib.gx_load_record(self.h, layer, expert, data.ctypes.data, data.nbytes), "gx_load_record")
+
+    def layer_view(self, layer: int) -> tuple[int, int, int]:
+        base, rec, slots = C.c_void_p(), C.c_uint64(), C.c_uint32()
+        L.check(self._lib.gx_arena_layer_view(self.h, layer, C.byref(base), C.byref(rec), C.byref(slots)))
+        return int(base.value or 0), rec.value, slots.value
+
+    def read_slot(self, layer: int, slot: int, nbytes: int | None = None) -> np.ndarray:
+        n = nbytes or self.model.record_raw
+        out = np.empty(n, np.uint8)
+        L.check(self._lib.gx_arena_read_slot(self.h, layer, slot, out.ctypes.data, n), "gx_arena_read_slot")
+        return out
+
+    def quota(self, layer: int) -> tuple[int, int, int]:
+        pol = self._lib.gx_arena_policy(self.h)
+        q, p, b = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        L.check(self._lib.gx_policy_quota(pol, layer, C.byref(q), C.byref(p), C.byref(b)))
+        return q.value, p.value, b.value
+
+    def slot_of(self, layer: int, expert: int) -> int:
+        return self._lib.gx_policy_slot_of(self._lib.gx_arena_policy(self.h), layer, expert)
+
+    def remap(self, layer: int, ids: np.ndarray, stream=None, slots: np.ndarray | None = None):
+        """The remap node on a host I32 view [ne1, ne0] (numpy strides honoured)."""
+        assert ids.dtype == np.int32 and ids.ndim == 2
+        ne1, ne0 = ids.shape
+        if slots is None:
+            slots = np.zeros((ne1, ne0), dtype=np.int32)
+        st = L.gx_serve_stats()
+        L.check(self._lib.gx_remap_serve(self.h, layer, ids.ctypes.data, ne0, ne1, ids.strides[1], ids.strides[0],
+                                         slots.ctypes.data, slots.strides[1], slots.strides[0], _stream(stream),
+                                         C.byref(st)), "gx_remap_serve")
+        return slots, st
+
+    def warm_all(self, stream=None) -> None:
+        L.check(self._lib.gx_arena_warm_all(self.h, _stream(stream)), "gx_arena_warm_all")
+
+    def stats(self) -> dict:
+        s = L.gx_arena_stats()
+        L.check(self._lib.gx_stats(self.h, C.byref(s)))
+        return {k: getattr(s, k) for k, _ in s._fields_}
+
+    def layer_forward(self, layer: int, x, ids: np.ndarray, w, out, stream=None) -> L.gx_serve_stats:
+        """One MoE layer: x [T, H] f32 device, ids [T, k] int32 HOST, w [T, k] f32 device, out [T, H] device."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        T, k = ids.shape
+        st = L.gx_serve_stats()
+        L.check(self._lib.gx_moe_layer_forward(self.h, layer, C.byref(self.desc), _ptr(x), ids.ctypes.data, _ptr(w),
+                                               k, T, _ptr(out), _stream(stream), C.byref(st)),
+                "gx_moe_layer_forward")
+        return st
+
+
+def mul_mat_id(type_: int, as_, ne00: int, ne01: int, nb01: int, nb02: int, n_as: int,
+               b, ne11: int, ne12: int, nb11: int, nb12: int,
+               ids, ne20: int, ne21: int, nbi1: int, dst, stream=None) -> None:
+    """ggml_mul_mat_id with ggml's tensor conventions (all device addresses)."""
+    L.check(L.lib().gx_mul_mat_id(type_, _ptr(as_), ne00, ne01, nb01, nb02, n_as, _ptr(b), ne11, ne12, nb11, nb12,
+                                  _ptr(ids), ne20, ne21, nbi1, _ptr(dst), _stream(stream)), "gx_mul_mat_id")
+
+
+def device_error() -> int:
+    code = C.c_int32()
+    L.check(L.lib().gx_device_error(C.byref(code)))
+    return code.value

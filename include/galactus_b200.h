@@ -1,0 +1,256 @@
+/*
+ * galactus_b200 -- C-ABI of the B200 routed-expert FFN.
+ *
+ * This is the boundary a patched llama.cpp graph binds. Every entry point takes
+ * plain pointers and sizes; device pointers are CUDA device addresses, streams
+ * are cudaStream_t passed as void*. No entry point throws: each returns a
+ * GX_* status code (0 = success).
+ *
+ * The op surface it replaces, in the reference's patched llama.cpp
+ * (patches/galactus-h4-llamacpp.diff, cited by the diff's own line numbers):
+ *   galactus_h4::init / create_exps / remap_ids      diff:2147-2150, 2260-2264, 2293-2296
+ *   ggml_mul_mat_id on the expert tensors            diff:2161, 2170, 2179, 2188
+ *   ggml_swiglu_split / GGML_GLU_OP_SWIGLU_OAI       diff:1461-1465
+ * and, underneath the glue, the H4 engine:
+ *   galactus::h4::ModelProfile                       src/h4/h4-profile.hpp:19-39
+ *   galactus::h4::ExpertCache                        src/h4/h4-expert-cache.hpp:66-196
+ *   galactus::h4::ExpertStore                        src/h4/h4-expert-store.hpp:27-117
+ */
+#ifndef GALACTUS_B200_H
+#define GALACTUS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define GX_OK              0
+#define GX_ERR_INVALID    -1  /* null pointer, bad size or stride */
+#define GX_ERR_TYPE       -2  /* weight type without a bit-exact kernel (reference: decline, diff:53-96) */
+#define GX_ERR_ALIGN      -3  /* ne00 not a multiple of 64 (Q8_0 family) or 256 (Q8_K family), or a
+                                 tensor base/stride the kernels cannot stage (diff:181-187) */
+#define GX_ERR_DOMAIN     -4  /* expert id outside [0, n_expert) */
+#define GX_ERR_BATCH      -5  /* a micro-batch holds more distinct experts than the probation segment */
+#define GX_ERR_SLOTS      -6  /* free list exhausted or a served key has no slot
+                                 (src/h4/h4-expert-store.cpp:127-141; scripts/derive-remap-strides.py:70) */
+#define GX_ERR_CUDA       -7  /* a CUDA runtime call failed */
+#define GX_ERR_TIMEOUT    -8  /* a bounded device-side wait ran out */
+#define GX_ERR_NOMEM      -9  /* device or pinned host allocation failed */
+#define GX_ERR_COPY      -10  /* a host->HBM miss copy failed */
+#define GX_ERR_STATE     -11  /* call out of order (e.g. no host tier) */
+#define GX_ERR_DEVICE    -12  /* a kernel reported an error (see gx_device_error) */
+
+/* ggml type ids (ggml.h numbering) of the formats this library computes on */
+#define GX_TYPE_Q8_0   8
+#define GX_TYPE_Q4_K  12
+#define GX_TYPE_Q6_K  14
+#define GX_TYPE_Q8_K  15
+#define GX_TYPE_IQ1_S 19
+#define GX_TYPE_MXFP4 39
+
+/* slot policies: GALACTUS_H4_CACHE_POLICY values (src/h4/h4-cache-plan.hpp:83-97) plus pure LRU */
+#define GX_POLICY_AUTO      0  /* plan (when given) + frequency victim: the reference default */
+#define GX_POLICY_UNIFORM   1  /* equal quota, SLRU with LRU victim (the shipped policy) */
+#define GX_POLICY_PLAN      2  /* plan only, LRU victim */
+#define GX_POLICY_FREQUENCY 3  /* equal quota, frequency victim */
+#define GX_POLICY_LRU       4  /* one segment, least recently used victim (no reference counterpart) */
+
+/* activations of the expert FFN */
+#define GX_ACT_SWIGLU     0
+#define GX_ACT_SWIGLU_OAI 1
+
+const char * gx_status_string(int status);
+
+/* Library build identity (kernel generation, target arch). */
+const char * gx_version(void);
+
+/* Select the CUDA device for the calling thread and load the device tables.
+ * Returns GX_ERR_CUDA when no device is present. */
+int gx_device_init(int device);
+
+/* First error code recorded by a kernel on the current device since the last
+ * call (0 if none), and clear it. Kernels record instead of trapping: an
+ * out-of-domain expert id, or a bounded wait that ran out. */
+int gx_device_error(int32_t * code_out);
+
+/* ----------------------------------------------------------------- profile
+ * MoE geometry of the routed layers (ModelProfile, src/h4/h4-profile.hpp:19-39).
+ * record_bytes[i] is the 16 KiB-padded record of layer first_layer+i
+ * (down | gate | up), record_bytes_raw[i] its useful bytes. */
+typedef struct gx_profile {
+    uint32_t first_layer;
+    uint32_t last_layer;
+    uint32_t experts;   /* experts per layer (<= 1024, the key encoding capacity) */
+    uint32_t used;      /* experts selected per token */
+    const uint64_t * record_bytes;
+    const uint64_t * record_bytes_raw;
+} gx_profile;
+
+/* ------------------------------------------------------------ slot policy
+ * The per-layer slot cache and slot ledger, host only: ExpertCache plus the
+ * slot tables of ExpertStore (warm path, src/h4/h4-expert-store.cpp:197-211).
+ * No device memory is touched; usable on any host. */
+typedef struct gx_policy gx_policy;
+
+typedef struct gx_serve_stats {
+    uint32_t hits;
+    uint32_t misses;
+    uint32_t evictions;
+    uint32_t distinct;
+    uint64_t bytes_copied;   /* host->HBM bytes issued by this call */
+} gx_serve_stats;
+
+/* capacity_bytes: the whole cache budget; quota = capacity / sum of one record
+ * per layer, capped at `experts` (src/h4/h4-expert-cache.cpp:68-135).
+ * plan_quotas: optional per-layer quotas (NULL = uniform), validated against
+ * the budget the uniform quota buys. */
+int gx_policy_create(const gx_profile * profile, uint64_t capacity_bytes, double protected_fraction,
+                     int policy, const uint32_t * plan_quotas, gx_policy ** out);
+void gx_policy_destroy(gx_policy * policy);
+int gx_policy_quota(const gx_policy * policy, uint32_t layer, uint32_t * quota,
+                    uint32_t * protected_quota, uint32_t * probation_quota);
+/* One micro-batch of one layer through the policy: begin_batch, then one
+ * access per expert in order, slot release before slot allocation. On return
+ * slots_out[i] is the slot of experts[i]; hit_out[i] (optional) its hit bit,
+ * evicted_out[i] (optional) the expert evicted by that access or -1. */
+int gx_policy_serve(gx_policy * policy, uint32_t layer, const int32_t * experts, uint32_t count,
+                    int32_t * slots_out, uint8_t * hit_out, int32_t * evicted_out, gx_serve_stats * stats);
+/* Slot of a resident expert, -1 otherwise (ExpertStore::slot_of). */
+int32_t gx_policy_slot_of(const gx_policy * policy, uint32_t layer, uint32_t expert);
+/* Cumulative counters (ExpertCache::hits/accesses/cold_bytes). */
+int gx_policy_counters(const gx_policy * policy, uint64_t * hits, uint64_t * accesses, uint64_t * cold_bytes);
+
+/* ------------------------------------------------------------------ arena
+ * The slot arena in HBM (one slab per layer, quota x record bytes, 16 KiB
+ * aligned) and the pinned host tier that backs it (every record of every
+ * layer, record layout down | gate | up). Replaces ExpertStore's arena and
+ * DualVolumeReader's SSD reads (src/h4/h4-expert-store.cpp:29-90,
+ * src/h4/h4-reader.cpp:284-305). */
+typedef struct gx_arena gx_arena;
+
+typedef struct gx_arena_config {
+    gx_profile profile;
+    uint64_t capacity_bytes;
+    double protected_fraction;   /* GALACTUS_H4_PROTECTED; 0.75 in the reference */
+    int policy;                  /* GX_POLICY_* */
+    const uint32_t * plan_quotas;/* optional */
+    int device;
+    int host_tier;               /* 1: allocate the pinned host tier (all records) */
+    int64_t max_tokens;          /* largest micro-batch the layer entry point will see */
+    int64_t hidden;              /* H, for the layer entry point's scratch */
+    int64_t intermediate;        /* I */
+} gx_arena_config;
+
+int gx_arena_create(const gx_arena_config * config, gx_arena ** out);
+int gx_arena_destroy(gx_arena * arena);
+/* Pinned host copy of record (layer, expert): fill it before the first serve. */
+void * gx_arena_host_record(gx_arena * arena, uint32_t layer, uint32_t expert);
+/* Copy one record into the host tier (the pack reader's job in the reference). */
+int gx_load_record(gx_arena * arena, uint32_t layer, uint32_t expert, const void * src, uint64_t bytes);
+/* Device base of a layer's slab, its record stride and slot count: the three
+ * expert tensors of the layer are views at base + role offset with
+ * nb[2] = record (create_exps, diff:2293-2296). */
+int gx_arena_layer_view(gx_arena * arena, uint32_t layer, void ** base, uint64_t * record_bytes, uint32_t * slots);
+gx_policy * gx_arena_policy(gx_arena * arena);
+/* Number of keys currently resident with valid bytes in HBM for a layer. */
+
+/* The remap node (galactus_h4::remap_ids, diff:2146-2150; strided read and
+ * write of scripts/derive-remap-strides.py:30-75). Reads expert ids from a
+ * host I32 tensor [ne0, ne1] with byte strides nb0, nb1, serves the layer
+ * (policy, then one host->HBM copy per miss on the arena's copy stream), and
+ * writes slot ids into a host I32 tensor with byte strides dnb0, dnb1.
+ * `stream` (the consumer's stream) is made to wait for the copies, and the
+ * copies wait for everything already queued on `stream`. */
+int gx_remap_serve(gx_arena * arena, uint32_t layer,
+                   const int32_t * ids, int64_t ne0, int64_t ne1, int64_t nb0, int64_t nb1,
+                   int32_t * slots, int64_t dnb0, int64_t dnb1,
+                   void * stream, gx_serve_stats * stats);
+
+/* Copy the bytes of one slot back to host memory, after every copy queued so
+ * far has landed (the slot-content audit of src/h4/h4-serve-check.cpp:63-91). */
+int gx_arena_read_slot(gx_arena * arena, uint32_t layer, uint32_t slot, void * dst, uint64_t bytes);
+
+/* Serve every expert of every layer once (full-residency warm-up), copies included. */
+int gx_arena_warm_all(gx_arena * arena, void * stream);
+
+typedef struct gx_arena_stats {
+    uint64_t serves;
+    uint64_t hits;
+    uint64_t misses;
+    uint64_t evictions;
+    uint64_t bytes_h2d;
+    uint64_t copies;
+} gx_arena_stats;
+int gx_stats(gx_arena * arena, gx_arena_stats * stats);
+
+/* ---------------------------------------------------------------- kernels
+ * ggml_mul_mat_id with ggml's tensor conventions (all device pointers):
+ *   as   expert weights, row r of expert e at as + e*nb02 + r*nb01, ne00 x ne01 per expert
+ *   b    f32 [ne00, ne11, ne12] with byte strides nb11, nb12 (ne11 is 1 or k)
+ *   ids  i32 [ne20 = k, ne21 = T] with byte stride nbi1 between tokens
+ *   dst  f32 [ne01, k, T] contiguous
+ * The f32 activations are quantized to the weight type's vec_dot_type inside
+ * the kernel (Q8_0 for Q8_0/MXFP4, Q8_K otherwise) and every output is the
+ * CPU's vec_dot of the quantized row, bit for bit (diff:335-345, 1049-1054,
+ * 1167-1174, 1254-1259, 1366-1370). Requires ne00 % 64 == 0 (Q8_0 family)
+ * or % 256 == 0 (Q8_K family), 16-byte aligned as/nb01*tile/nb02. */
+int gx_mul_mat_id(int type, const void * as, int64_t ne00, int64_t ne01, int64_t nb01, int64_t nb02, int64_t n_as,
+                  const float * b, int64_t ne11, int64_t ne12, int64_t nb11, int64_t nb12,
+                  const int32_t * ids, int64_t ne20, int64_t ne21, int64_t nbi1,
+                  float * dst, void * stream);
+
+/* Activation quantization alone (quantize_row_q8_0 / quantize_row_q8_K):
+ * rows of ne0 f32 at src + i*nb1 -> blocks at dst + i*dst_row_stride. */
+int gx_quantize_rows(int vec_dot_type, const float * src, int64_t ne0, int64_t nrows, int64_t nb1,
+                     void * dst, int64_t dst_row_stride, void * stream);
+
+/* out = silu(g) * u, silu(x) = x / (1 + exp(-x)) */
+int gx_swiglu(const float * g, const float * u, float * out, int64_t n, void * stream);
+/* out = min(g,limit) / (1 + exp(alpha * -min(g,limit))) * (clamp(u,-limit,limit) + 1) */
+int gx_swiglu_oai(const float * g, const float * u, float * out, int64_t n, float alpha, float limit, void * stream);
+/* out[h,t] = sum over s = 0..k-1, in order, of w[s,t] * y[h,s,t] (one rounding per product and per add) */
+int gx_combine(const float * y, const float * w, float * out, int64_t H, int64_t k, int64_t T, void * stream);
+/* The library's exp, elementwise (the one SiLU uses) */
+int gx_expf(const float * x, float * y, int64_t n, void * stream);
+
+/* ------------------------------------------------------------- MoE layer
+ * One routed-expert FFN layer, end to end on the device:
+ *   remap (policy + miss copies) -> gate/up mul_mat_id + activation
+ *   -> down mul_mat_id -> weighted combine in slot order.
+ * x: device f32 [H, T]; ids: HOST i32 [k, T] (contiguous); w: device f32 [k, T];
+ * out: device f32 [H, T]. Record layout down | gate | up (offsets below). */
+typedef struct gx_layer_desc {
+    int32_t type_gate;
+    int32_t type_up;
+    int32_t type_down;
+    int32_t act;        /* GX_ACT_* */
+    float alpha;        /* SWIGLU_OAI */
+    float limit;        /* SWIGLU_OAI */
+    int64_t hidden;     /* H */
+    int64_t intermediate; /* I */
+    uint64_t off_gate;  /* byte offset of gate inside a record (down at 0) */
+    uint64_t off_up;
+} gx_layer_desc;
+
+int gx_moe_layer_forward(gx_arena * arena, uint32_t layer, const gx_layer_desc * desc,
+                         const float * x, const int32_t * ids, const float * w, int64_t k, int64_t T,
+                         float * out, void * stream, gx_serve_stats * stats);
+
+/* ------------------------------------------------------------- synthetic
+ * Seeded synthetic data written straight into device memory (test and bench
+ * inputs; the same generator is restated in the oracle):
+ *   gx_synth_normal: f32 ~ N(0, sigma) (4-term Irwin-Hall), element i of stream (seed, stream_id)
+ *   gx_synth_weights: n_rows rows of ne00 elements of `type`, quantized from
+ *     N(0, sigma) (Q8_0, Q4_K, Q6_K) or uniform over codes (MXFP4, IQ1_S) */
+int gx_synth_normal(float * dst, int64_t n, uint64_t seed, uint64_t stream_id, float sigma, void * stream);
+int gx_synth_weights(int type, void * dst, int64_t ne00, int64_t n_rows, uint64_t seed, uint64_t stream_id,
+                     float sigma, void * stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GALACTUS_B200_H */

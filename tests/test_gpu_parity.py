@@ -1,0 +1,262 @@
+"""Parity of the CUDA path (called through the C-ABI) with the CPU oracle:
+bit-identical outputs on the same seeded inputs, for every weight format of
+the benchmark models, token counts 1..512, both src1 shapes (ne11 = 1 and
+ne11 = k), strided id views, slot churn, and the error paths."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+Q8_0, Q4_K, Q6_K, Q8_K, IQ1_S, MXFP4 = 8, 12, 14, 15, 19, 39
+# (type, ne00, ne01) of the expert matrices of the benchmark models
+SHAPES = {
+    "q8_0-gate": (Q8_0, 2048, 768), "q8_0-down": (Q8_0, 768, 2048),
+    "q4_K-gate": (Q4_K, 2048, 1024), "q6_K-down": (Q6_K, 1024, 2048),
+    "q4_K-gate-4096": (Q4_K, 4096, 1536), "q6_K-down-1536": (Q6_K, 1536, 4096),
+    "mxfp4": (MXFP4, 2880, 2880), "iq1_s-gate": (IQ1_S, 7168, 2048), "iq1_s-down": (IQ1_S, 2048, 7168),
+}
+
+
+@pytest.fixture(scope="module")
+def dev(gxlib):
+    gxlib.check(gxlib.lib().gx_device_init(0), "gx_device_init")
+    return torch.device("cuda:0")
+
+
+def D(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to("cuda")
+
+
+def H(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+def no_device_error(gxlib):
+    from galactus_b200.moe import device_error
+    assert device_error() == 0
+
+
+@pytest.mark.parametrize("t", [Q8_0, Q4_K, Q6_K, MXFP4, IQ1_S])
+def test_synth_weights_bytes(gxlib, orc, dev, t):
+    ne00 = 2880 if t == MXFP4 else 2048
+    rows = 12
+    want = orc.synth_weights(t, ne00, rows, seed=3, stream_id=99)
+    buf = torch.zeros(want.size, dtype=torch.uint8, device=dev)
+    gxlib.check(gxlib.lib().gx_synth_weights(t, buf.data_ptr(), ne00, rows, 3, 99, 0.02, None))
+    np.testing.assert_array_equal(H(buf), want)
+    x = torch.zeros(10000, dtype=torch.float32, device=dev)
+    gxlib.check(gxlib.lib().gx_synth_normal(x.data_ptr(), 10000, 7, 5, 1.0, None))
+    np.testing.assert_array_equal(bits(H(x)), bits(orc.synth_normal(10000, 7, 5, 1.0)))
+
+
+def test_expf_bitwise(gxlib, orc, dev):
+    rng = np.random.default_rng(1)
+    xs = np.concatenate([
+        rng.uniform(-110, 95, 1 << 21), rng.uniform(-2, 2, 1 << 20),
+        np.arange(-(1 << 16), 1 << 16, dtype=np.int64).astype(np.float32) * np.float32(1 / 512),
+        np.array([0, -0.0, np.inf, -np.inf, np.nan, 88.72283935546875, 88.7228317, -103.972084, -87.33655], np.float32),
+    ]).astype(np.float32)
+    xd = D(xs)
+    yd = torch.empty_like(xd)
+    gxlib.check(gxlib.lib().gx_expf(xd.data_ptr(), yd.data_ptr(), xs.size, None))
+    got, want = H(yd), orc.expf(xs)
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    np.testing.assert_array_equal(bits(got)[~nan], bits(want)[~nan])
+
+
+@pytest.mark.parametrize("vdt,n", [(Q8_0, 2048), (Q8_0, 2880), (Q8_K, 2048), (Q8_K, 7168)])
+def test_quantize_rows_bitwise(gxlib, orc, dev, vdt, n):
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((9, n)).astype(np.float32)
+    x[1] = 0.0
+    x[2, :64] = np.float32(0.5)          # ties in |x|
+    x[3] *= np.float32(1e-30)            # tiny magnitudes
+    want = orc.quantize(vdt, x)
+    pitch = (want.shape[1] + 15) // 16 * 16
+    out = torch.zeros(9 * pitch, dtype=torch.uint8, device=dev)
+    gxlib.check(gxlib.lib().gx_quantize_rows(vdt, D(x).data_ptr(), n, 9, n * 4, out.data_ptr(), pitch, None))
+    got = H(out).reshape(9, pitch)[:, :want.shape[1]]
+    np.testing.assert_array_equal(got, want)
+
+
+def test_activations_and_combine_bitwise(gxlib, orc, dev):
+    rng = np.random.default_rng(3)
+    g = (rng.standard_normal(1 << 18) * 6).astype(np.float32)
+    u = (rng.standard_normal(1 << 18) * 6).astype(np.float32)
+    g[:4] = [np.nan, 100.0, -100.0, 7.0]
+    gd, ud = D(g), D(u)
+    out = torch.empty_like(gd)
+    gxlib.check(gxlib.lib().gx_swiglu(gd.data_ptr(), ud.data_ptr(), out.data_ptr(), g.size, None))
+    w = orc.swiglu(g, u)
+    np.testing.assert_array_equal(bits(H(out))[4:], bits(w)[4:])
+    gxlib.check(gxlib.lib().gx_swiglu_oai(gd.data_ptr(), ud.data_ptr(), out.data_ptr(), g.size, 1.702, 7.0, None))
+    w = orc.swiglu_oai(g, u, 1.702, 7.0)
+    got = H(out)
+    assert np.array_equal(np.isnan(got), np.isnan(w))
+    np.testing.assert_array_equal(bits(got)[~np.isnan(w)], bits(w)[~np.isnan(w)])
+    y = rng.standard_normal((5, 8, 2048)).astype(np.float32)
+    wt = rng.random((5, 8)).astype(np.float32)
+    o = torch.empty((5, 2048), dtype=torch.float32, device=dev)
+    gxlib.check(gxlib.lib().gx_combine(D(y).data_ptr(), D(wt).data_ptr(), o.data_ptr(), 2048, 8, 5, None))
+    np.testing.assert_array_equal(bits(H(o)), bits(orc.combine(y, wt)))
+
+
+def _experts(orc, t, ne00, ne01, n_as, seed):
+    rb = orc.row_bytes(t, ne00)
+    nb02 = (rb * ne01 + 16383) // 16384 * 16384 + 16384   # a record stride wider than the matrix
+    ex = np.zeros((n_as, nb02), np.uint8)
+    for e in range(n_as):
+        ex[e, :rb * ne01] = orc.synth_weights(t, ne00, ne01, seed, 1000 + e)
+    return ex, rb, nb02
+
+
+def _run_mmid(gxlib, t, ex, ne00, ne01, rb, nb02, b, ids_full, k):
+    T, ne11, _ = b.shape
+    dst = torch.zeros((T, k, ne01), dtype=torch.float32, device="cuda")
+    exd, bd, idd = D(ex), D(b), D(ids_full)
+    gxlib.mul_mat_id(t, exd, ne00, ne01, rb, nb02, ex.shape[0], bd, ne11, T, ne00 * 4, ne11 * ne00 * 4,
+                     idd, k, T, ids_full.shape[1] * 4, dst)
+    return H(dst)
+
+
+@pytest.mark.parametrize("shape", list(SHAPES))
+@pytest.mark.parametrize("T", [1, 2, 3, 8, 32])
+def test_mul_mat_id_bitwise(gxlib, orc, dev, shape, T):
+    t, ne00, ne01 = SHAPES[shape]
+    k, n_as, n_exp_row = 4, 6, 16
+    rng = np.random.default_rng(T * 31 + ne00)
+    ex, rb, nb02 = _experts(orc, t, ne00, ne01, n_as, seed=T)
+    # ids as a view into a wider argsort row (nb1 = 16 ints), the case the
+    # reference's stride fix is about
+    ids_full = np.full((T, n_exp_row), -7, np.int32)
+    for i in range(T):
+        ids_full[i, :k] = rng.choice(n_as, k, replace=False)
+    ids = ids_full[:, :k]
+    for ne11 in (1, k):
+        b = rng.standard_normal((T, ne11, ne00)).astype(np.float32)
+        got = _run_mmid(gxlib, t, ex, ne00, ne01, rb, nb02, b, ids_full, k)
+        want = orc.mul_mat_id(t, ex, ne00, ne01, b, ids, nb01=rb)
+        np.testing.assert_array_equal(bits(got), bits(want), err_msg=f"{shape} T={T} ne11={ne11}")
+    no_device_error(gxlib)
+
+
+def test_mul_mat_id_512_tokens(gxlib, orc, dev):
+    t, ne00, ne01 = SHAPES["q8_0-gate"]
+    k, n_as, T = 8, 16, 512
+    rng = np.random.default_rng(512)
+    ex, rb, nb02 = _experts(orc, t, ne00, ne01, n_as, seed=9)
+    ids = np.stack([rng.choice(n_as, k, replace=False) for _ in range(T)]).astype(np.int32)
+    b = rng.standard_normal((T, 1, ne00)).astype(np.float32)
+    got = _run_mmid(gxlib, t, ex, ne00, ne01, rb, nb02, b, ids, k)
+    want = orc.mul_mat_id(t, ex, ne00, ne01, b, ids, nb01=rb)
+    np.testing.assert_array_equal(bits(got), bits(want))
+
+
+def test_out_of_domain_id_is_reported_not_read(gxlib, orc, dev):
+    from galactus_b200.moe import device_error
+    device_error()
+    t, ne00, ne01 = SHAPES["q8_0-down"]
+    k, n_as, T = 2, 3, 2
+    ex, rb, nb02 = _experts(orc, t, ne00, ne01, n_as, seed=1)
+    ids = np.array([[0, 1], [2, 3]], np.int32)      # 3 is outside [0, 3)
+    b = np.random.default_rng(0).standard_normal((T, 1, ne00)).astype(np.float32)
+    got = _run_mmid(gxlib, t, ex, ne00, ne01, rb, nb02, b, ids, k)
+    assert np.isnan(got[1, 1]).all()
+    want = orc.mul_mat_id(t, ex, ne00, ne01, b, np.array([[0, 1], [2, 0]], np.int32), nb01=rb)
+    np.testing.assert_array_equal(bits(got[:, 0]), bits(want[:, 0]))
+    assert device_error() == 1
+    assert device_error() == 0
+
+
+def _small_model(gxlib, name, experts=12, layers=2):
+    m = gxlib.MODELS[name]
+    from galactus_b200.models import ModelShape
+    return ModelShape(**{**m.__dict__, "experts": experts, "layers": layers})
+
+
+def _zipf_routes(rng, T, experts, k):
+    p = 1.0 / np.arange(1, experts + 1) ** 1.1
+    p /= p.sum()
+    ids = np.stack([rng.choice(experts, k, replace=False, p=p) for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, k)).astype(np.float32)
+    w /= w.sum(axis=1, keepdims=True)
+    return ids, w.astype(np.float32)
+
+
+@pytest.mark.parametrize("name", ["qwen3-30b", "olmoe", "gpt-oss-120b", "qwen3-235b", "deepseek-v3"])
+def test_layer_forward_bitwise_with_churn(gxlib, orc, dev, name):
+    """remap (policy + host->HBM miss copies) + fused gate/up/act + fused
+    down/combine, against the oracle layer on expert-indexed records, with a
+    cache small enough that slots are evicted and reused."""
+    m = _small_model(gxlib, name)
+    k = m.used
+    rng = np.random.default_rng(sum(map(ord, name)))
+    cap_slots = k + 2 if k + 2 < m.experts else m.experts
+    arena = gxlib.Arena(m, capacity_bytes=cap_slots * m.record * m.layers, policy=gxlib.POLICY_AUTO,
+                        max_tokens=16)
+    records = np.stack([orc.synth_record(m, m.seed, 0, e) for e in range(m.experts)])
+    records2 = np.stack([orc.synth_record(m, m.seed, 1, e) for e in range(m.experts)])
+    for e in range(m.experts):
+        arena.load_record(0, e, records[e])
+        arena.load_record(1, e, records2[e])
+    q, prot, prob = arena.quota(0)
+    bound = min(q, prob)
+    stream = torch.cuda.current_stream()
+    for step, T in enumerate([1, 1, 2, 1, 4, 1, 16, 1, 3]):
+        layer = step % 2
+        recs = records if layer == 0 else records2
+        ids, w = _zipf_routes(rng, T, m.experts, k)
+        # keep the micro-batch inside the engine's probation bound
+        if len(set(ids.ravel().tolist())) > bound:
+            ids = np.stack([ids[0]] * T)
+        x = rng.standard_normal((T, m.hidden)).astype(np.float32)
+        out = torch.zeros((T, m.hidden), dtype=torch.float32, device=dev)
+        arena.layer_forward(layer, D(x), ids, D(w), out, stream=stream)
+        got = H(out)
+        want = orc.moe_layer(m, recs, x, ids, w)
+        np.testing.assert_array_equal(bits(got), bits(want), err_msg=f"{name} step {step} T={T}")
+    st = arena.stats()
+    assert st["misses"] > 0 and st["hits"] > 0
+    no_device_error(gxlib)
+    arena.close()
+
+
+def test_remap_serve_strided_and_slot_bytes(gxlib, orc, dev):
+    """The remap node reads and writes through strides, and every served slot
+    holds exactly its record's bytes after churn (the serve-check pattern)."""
+    m = _small_model(gxlib, "qwen3-30b", experts=16, layers=1)
+    arena = gxlib.Arena(m, capacity_bytes=10 * m.record, policy=gxlib.POLICY_AUTO, max_tokens=4)
+    recs = [orc.synth_record(m, 11, 0, e) for e in range(m.experts)]
+    for e in range(m.experts):
+        arena.load_record(0, e, recs[e])
+    rng = np.random.default_rng(4)
+    stream = torch.cuda.current_stream()
+    q, _, prob = arena.quota(0)
+    for _ in range(30):
+        full = np.full((2, 16), -1, np.int32)            # argsort rows of 16, top-k view of 4
+        full[0, :4] = rng.choice(16, 4, replace=False)
+        full[1, :4] = full[0, :4][::-1]
+        view = full[:, :4]
+        slots_full = np.full((2, 8), -5, np.int32)
+        slots = slots_full[:, ::2]                        # strided destination
+        arena.remap(0, view, stream=stream, slots=slots)
+        assert (slots_full[:, 1::2] == -5).all()
+        for i in range(2):
+            for j in range(4):
+                assert slots[i, j] == arena.slot_of(0, int(view[i, j]))
+    torch.cuda.synchronize()
+    seen = 0
+    for e in range(m.experts):
+        s = arena.slot_of(0, e)
+        if s >= 0:
+            np.testing.assert_array_equal(arena.read_slot(0, s), recs[e][:m.record_raw])
+            seen += 1
+    assert seen > 0
+    arena.close()

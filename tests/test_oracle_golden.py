@@ -1,0 +1,176 @@
+"""The oracle pinned before it is trusted: block decoding against gguf-py's
+dequantizers, binary16 conversion against numpy, Q8_0 quantization against
+gguf-py, the integer dot pipeline against a float64 evaluation of the same
+quantized values, and the shared expf against the host libm."""
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+GOLD = Path(__file__).resolve().parent / "golden"
+TYPES = {"q8_0": 8, "q4_K": 12, "q6_K": 14, "mxfp4": 39, "iq1_s": 19}
+ELEMS = {8: 32, 12: 256, 14: 256, 39: 32, 19: 256}
+
+
+@pytest.mark.parametrize("name", list(TYPES))
+def test_dequant_matches_gguf(orc, name):
+    t = TYPES[name]
+    z = np.load(GOLD / f"dequant_{name}.npz")
+    blocks, expected = z["blocks"], z["expected"]
+    assert blocks.shape[0] > 0, "an empty comparison is not a pass"
+    for i in range(blocks.shape[0]):
+        got = orc.dequantize_row(t, blocks[i], ELEMS[t])
+        np.testing.assert_array_equal(got.view(np.uint32), expected[i].view(np.uint32), err_msg=f"{name} block {i}")
+
+
+def test_iq1s_grid_fixture_shape(orc):
+    g = orc.iq1s_grid()
+    assert g.shape == (2048, 8)
+    assert set(np.unique(g).tolist()) <= {-1, 0, 1}
+    assert (g[0] == -1).all()
+
+
+def test_fp16_conversion_matches_numpy(orc):
+    rng = np.random.default_rng(1)
+    vals = np.concatenate([
+        rng.standard_normal(20000).astype(np.float32) * np.float32(10.0) ** rng.integers(-9, 5, 20000),
+        np.array([0.0, -0.0, 65504.0, 65519.99, 65520.0, 1e6, -1e6, 6.0e-8, 2.9802322e-08, 2.98023259e-08,
+                  5.96e-08, 6.1035156e-05, 6.1e-05, 1.0, 0.5, np.inf, -np.inf], dtype=np.float32),
+    ]).astype(np.float32)
+    want = vals.astype(np.float16).view(np.uint16)
+    got = np.array([orc.fp32_to_fp16(float(v)) for v in vals], dtype=np.uint16)
+    np.testing.assert_array_equal(got, want)
+    # widening is exact for every binary16 value
+    allh = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    finite = ~np.isnan(allh.view(np.float16))
+    wid = np.array([orc.lib().orc_fp16_to_fp32(int(h)) for h in allh[finite]], dtype=np.float32)
+    np.testing.assert_array_equal(wid.view(np.uint32), allh[finite].view(np.float16).astype(np.float32).view(np.uint32))
+
+
+def test_q8_0_quantize_matches_gguf_except_ties(orc):
+    z = np.load(GOLD / "q8_0_quant.npz")
+    x, want = z["x"], z["q"]
+    got = orc.quantize(8, x.reshape(1, -1)).reshape(-1, 34)
+    assert got.shape == want.shape
+    np.testing.assert_array_equal(got[:, :2], want[:, :2])  # fp16 scales identical
+    # gguf-py rounds half away from zero (the scalar reference); the NEON path
+    # rounds to nearest even: the two may only differ where x*id is an exact tie
+    diff = np.argwhere(got[:, 2:] != want[:, 2:])
+    for b, j in diff:
+        d = np.float32(np.abs(x[b]).max()) / np.float32(127)
+        idv = np.float32(1) / d
+        p = np.float32(x[b, j]) * idv
+        assert abs(abs(float(p)) % 1.0 - 0.5) == 0.0, f"block {b} elem {j}: not a tie"
+
+
+def test_q8_K_quantize_rules(orc):
+    # first strict max wins: two equal magnitudes of opposite sign, the first is negative
+    x = np.zeros(256, np.float32)
+    x[10] = -2.0
+    x[200] = 2.0
+    x[5] = 1.0
+    q = orc.quantize(15, x)[0]
+    d = q[:4].view(np.float32)[0]
+    qs = q[4:260].view(np.int8)
+    bs = q[260:].view(np.int16)
+    assert d == np.float32(1.0) / (np.float32(-127.0) / np.float32(-2.0))
+    assert qs[10] == -127 and qs[200] == 127 and qs[5] == 64  # iscale = 63.5 -> RNE(63.5) = 64
+    assert all(bs[g] == qs[16 * g:16 * g + 16].astype(int).sum() for g in range(16))
+    # all zero -> zeros
+    z = orc.quantize(15, np.zeros(256, np.float32))[0]
+    assert not z.any()
+    # iscale*x never exceeds 127 after the clamp
+    rng = np.random.default_rng(3)
+    for _ in range(50):
+        v = rng.standard_normal(256).astype(np.float32)
+        qq = orc.quantize(15, v)[0][4:260].view(np.int8)
+        assert qq.max() <= 127 and qq.min() >= -127
+
+
+def _dequant_q8(vdt, q, n):
+    if vdt == 8:
+        b = q.reshape(-1, 34)
+        d = b[:, :2].copy().view(np.float16).astype(np.float64)
+        return (b[:, 2:].view(np.int8).astype(np.float64) * d).reshape(-1)[:n]
+    b = q.reshape(-1, 292)
+    d = b[:, :4].copy().view(np.float32).astype(np.float64)
+    return (b[:, 4:260].view(np.int8).astype(np.float64) * d).reshape(-1)[:n]
+
+
+@pytest.mark.parametrize("name,n", [("q8_0", 2048), ("q4_K", 2048), ("q6_K", 1024), ("mxfp4", 2880), ("iq1_s", 7168)])
+def test_integer_dot_equals_float_dot_of_same_values(orc, name, n):
+    """The integer pipeline computes sum(w_i * y_i) over the dequantized weights
+    and the dequantized Q8 activations; only float rounding may differ."""
+    t = TYPES[name]
+    rng = np.random.default_rng(11)
+    w = orc.synth_weights(t, n, 4, seed=5, stream_id=17)
+    rb = orc.row_bytes(t, n)
+    vdt = 8 if t in (8, 39) else 15
+    for r in range(4):
+        x = rng.standard_normal(n).astype(np.float32)
+        y = orc.quantize(vdt, x)[0]
+        got = orc.vec_dot(t, n, w[r * rb:(r + 1) * rb], y)
+        wf = orc.dequantize_row(t, w[r * rb:(r + 1) * rb], n).astype(np.float64)
+        ref = float(np.dot(wf, _dequant_q8(vdt, y, n)))
+        scale = float(np.sum(np.abs(wf) * np.abs(_dequant_q8(vdt, y, n)))) + 1e-30
+        assert abs(got - ref) <= 2e-6 * scale, (name, r, got, ref)
+
+
+def test_expf_against_libm(orc):
+    rng = np.random.default_rng(5)
+    xs = np.concatenate([rng.uniform(-87, 88, 200000), rng.uniform(-5, 5, 200000),
+                         rng.uniform(-103.9, -87.4, 20000)]).astype(np.float32)
+    got = orc.expf(xs).astype(np.float64)
+    ref = np.exp(xs.astype(np.float64))
+    normal = ref > np.finfo(np.float32).tiny
+    ulp = np.spacing(ref[normal].astype(np.float32)).astype(np.float64)
+    err = np.abs(got[normal] - ref[normal]) / ulp
+    assert err.max() <= 1.5, err.max()
+    # the subnormal range stays within one subnormal unit of the true value
+    sub = ~normal
+    assert np.all(np.abs(got[sub] - ref[sub]) <= 2 ** -149 * 1.01)
+    spec = orc.expf(np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 88.72283, 88.7229, -103.98, -200.0, 1.0],
+                             np.float32))
+    assert spec[0] == 1.0 and spec[1] == 1.0 and np.isposinf(spec[2]) and spec[3] == 0.0 and np.isnan(spec[4])
+    assert np.isfinite(spec[5]) and np.isposinf(spec[6]) and spec[7] == 0.0 and spec[8] == 0.0
+    assert abs(float(spec[9]) - math.e) <= float(np.spacing(np.float32(math.e)))
+
+
+def test_swiglu_oai_semantics(orc):
+    g = np.array([8.0, -8.0, 7.0, np.nan, 0.5], np.float32)
+    u = np.array([9.0, -9.0, 0.0, 1.0, np.nan], np.float32)
+    out = orc.swiglu_oai(g, u, 1.702, 7.0)
+    # x = min(g, 7) keeps NaN (ordered comparison), y = clamp(u) keeps NaN
+    x0 = np.float32(7.0)
+    want0 = (x0 / (np.float32(1) + orc.expf(np.array([np.float32(1.702) * -x0]))[0])) * np.float32(8.0)
+    assert out[0] == want0
+    assert np.isnan(out[3]) and np.isnan(out[4])
+
+
+def test_combine_is_ordered_chain(orc):
+    rng = np.random.default_rng(9)
+    y = rng.standard_normal((3, 8, 64)).astype(np.float32)
+    w = rng.random((3, 8)).astype(np.float32)
+    out = orc.combine(y, w)
+    for t in range(3):
+        acc = y[t, 0] * w[t, 0]
+        for s in range(1, 8):
+            acc = (acc + y[t, s] * w[t, s]).astype(np.float32)
+        np.testing.assert_array_equal(out[t], acc)
+
+
+def test_mul_mat_id_src1_shapes(orc):
+    """ne11 = 1 broadcasts one activation row to every slot; ne11 = k uses row s."""
+    rng = np.random.default_rng(2)
+    t, ne00, ne01, n_as, k, T = 8, 128, 16, 5, 3, 4
+    experts = np.stack([orc.synth_weights(t, ne00, ne01, 1, e) for e in range(n_as)])
+    ids = rng.integers(0, n_as, (T, k)).astype(np.int32)
+    b1 = rng.standard_normal((T, 1, ne00)).astype(np.float32)
+    bk = np.repeat(b1, k, axis=1)
+    o1 = orc.mul_mat_id(t, experts, ne00, ne01, b1, ids)
+    ok = orc.mul_mat_id(t, experts, ne00, ne01, bk, ids)
+    np.testing.assert_array_equal(o1, ok)
+    assert o1.shape == (T, k, ne01)
+    with pytest.raises(ValueError):
+        orc.mul_mat_id(t, experts, ne00, ne01, b1, np.full((T, k), n_as, np.int32))
