@@ -52,7 +52,7 @@ class gx_arena_config(C.Structure):
     _fields_ = [("profile", gx_profile), ("capacity_bytes", C.c_uint64), ("protected_fraction", C.c_double),
                 ("policy", C.c_int), ("plan_quotas", C.POINTER(C.c_uint32)), ("device", C.c_int),
                 ("host_tier", C.c_int), ("max_tokens", C.c_int64), ("hidden", C.c_int64),
-                ("intermediate", C.c_int64)]
+                ("intermediate", C.c_int64), ("host_tier_base", C.c_void_p)]
 
 
 class gx_arena_stats(C.Structure):
@@ -93,6 +93,8 @@ _SIGS = {
     "gx_arena_read_slot": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P, C.c_uint64]),
     "gx_arena_warm_all": (C.c_int, [_P, _P]),
     "gx_stats": (C.c_int, [_P, C.POINTER(gx_arena_stats)]),
+    "gx_arena_timing": (C.c_int, [_P, C.c_int]),
+    "gx_arena_timing_read": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "gx_mul_mat_id": (C.c_int, [C.c_int, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64,
                                 _I64, _I64, _P, _P]),
     "gx_quantize_rows": (C.c_int, [C.c_int, _P, _I64, _I64, _I64, _P, _I64, _P]),
@@ -102,6 +104,8 @@ _SIGS = {
     "gx_expf": (C.c_int, [_P, _P, _I64, _P]),
     "gx_moe_layer_forward": (C.c_int, [_P, C.c_uint32, C.POINTER(gx_layer_desc), _P, _P, _P, _I64, _I64, _P, _P,
                                        C.POINTER(gx_serve_stats)]),
+    "gx_moe_stack_forward": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.POINTER(gx_layer_desc), C.POINTER(_P), _P,
+                                       C.POINTER(_P), _I64, _I64, C.POINTER(_P), _P, C.POINTER(gx_serve_stats)]),
     "gx_synth_normal": (C.c_int, [_P, _I64, C.c_uint64, C.c_uint64, C.c_float, _P]),
     "gx_synth_weights": (C.c_int, [C.c_int, _P, _I64, _I64, C.c_uint64, C.c_uint64, C.c_float, _P]),
 }

@@ -127,6 +127,11 @@ struct gx_arena {
     cudaEvent_t ev_stage[kStageRing] = {};
     int stage_next = 0;
     gx_arena_stats stats{};
+    bool own_tier = false;
+    // kernel timing (gx_arena_timing)
+    bool timing = false;
+    std::vector<cudaEvent_t> tev;   // 3 per timed call
+    size_t tev_used = 0;
     std::mutex mu;
 
     uint32_t L(uint32_t layer) const { return layer - policy->impl.first_layer(); }
@@ -237,7 +242,8 @@ int gx_arena_destroy(gx_arena * a) {
     if (a->d_act) cudaFree(a->d_act);
     if (a->d_ids) cudaFree(a->d_ids);
     if (a->h_ids) cudaFreeHost(a->h_ids);
-    if (a->h_tier) cudaFreeHost(a->h_tier);
+    for (auto e : a->tev) if (e) cudaEventDestroy(e);
+    if (a->h_tier && a->own_tier) cudaFreeHost(a->h_tier);
     delete a->policy;
     delete a;
     return GX_OK;
@@ -272,7 +278,14 @@ int gx_arena_create(const gx_arena_config * c, gx_arena ** out) {
         a->arena_bytes = off;
         a->tier_bytes = hoff;
         ck(cudaMalloc(&a->d_arena, a->arena_bytes));
-        if (c->host_tier) ck(cudaHostAlloc(&a->h_tier, a->tier_bytes, cudaHostAllocDefault));
+        if (c->host_tier) {
+            if (c->host_tier_base != nullptr) {
+                a->h_tier = static_cast<uint8_t *>(c->host_tier_base);
+            } else {
+                ck(cudaHostAlloc(&a->h_tier, a->tier_bytes, cudaHostAllocDefault));
+                a->own_tier = true;
+            }
+        }
         ck(cudaStreamCreateWithFlags(&a->copy_stream, cudaStreamNonBlocking));
         a->ev_done.resize(n);
         a->ev_copy.resize(n);
@@ -335,6 +348,35 @@ int gx_stats(gx_arena * a, gx_arena_stats * s) {
     if (a == nullptr || s == nullptr) return GX_ERR_INVALID;
     *s = a->stats;
     return GX_OK;
+}
+
+int gx_arena_timing(gx_arena * a, int enable) {
+    if (a == nullptr) return GX_ERR_INVALID;
+    std::lock_guard<std::mutex> lock(a->mu);
+    a->timing = enable != 0;
+    a->tev_used = 0;
+    return GX_OK;
+}
+
+int gx_arena_timing_read(gx_arena * a, double * gate_up_ms, double * down_ms, uint64_t * calls) {
+    if (a == nullptr) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        double gu = 0.0, dn = 0.0;
+        if (a->tev_used > 0) ck(cudaEventSynchronize(a->tev[a->tev_used - 1]));
+        for (size_t i = 0; i + 3 <= a->tev_used; i += 3) {
+            float m1 = 0.f, m2 = 0.f;
+            ck(cudaEventElapsedTime(&m1, a->tev[i], a->tev[i + 1]));
+            ck(cudaEventElapsedTime(&m2, a->tev[i + 1], a->tev[i + 2]));
+            gu += m1;
+            dn += m2;
+        }
+        if (gate_up_ms) *gate_up_ms = gu;
+        if (down_ms) *down_ms = dn;
+        if (calls) *calls = a->tev_used / 3;
+        a->tev_used = 0;
+        return GX_OK;
+    });
 }
 
 }  // extern "C"
@@ -539,8 +581,47 @@ int gx_expf(const float * x, float * y, int64_t n, void * stream) {
 
 // --------------------------------------------------------------- MoE layer
 
+static int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x,
+                                const int32_t * ids, const float * w, int64_t k, int64_t T, float * out,
+                                cudaStream_t s, gx_serve_stats * stats);
+
 int gx_moe_layer_forward(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x, const int32_t * ids,
                          const float * w, int64_t k, int64_t T, float * out, void * stream, gx_serve_stats * stats) {
+    if (a == nullptr) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        ck(cudaSetDevice(a->device));
+        return layer_forward_locked(a, layer, d, x, ids, w, k, T, out, reinterpret_cast<cudaStream_t>(stream), stats);
+    });
+}
+
+int gx_moe_stack_forward(gx_arena * a, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * d,
+                         const float * const * x, const int32_t * ids, const float * const * w, int64_t k, int64_t T,
+                         float * const * out, void * stream, gx_serve_stats * stats) {
+    if (a == nullptr || x == nullptr || ids == nullptr || w == nullptr || out == nullptr) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        ck(cudaSetDevice(a->device));
+        gx_serve_stats sum{};
+        for (uint32_t i = 0; i < n_layers; ++i) {
+            gx_serve_stats st{};
+            const int rc = layer_forward_locked(a, first_layer + i, d, x[i], ids + (size_t)i * k * T, w[i], k, T, out[i],
+                                                reinterpret_cast<cudaStream_t>(stream), &st);
+            if (rc != GX_OK) return rc;
+            sum.hits += st.hits;
+            sum.misses += st.misses;
+            sum.evictions += st.evictions;
+            sum.distinct += st.distinct;
+            sum.bytes_copied += st.bytes_copied;
+        }
+        if (stats) *stats = sum;
+        return GX_OK;
+    });
+}
+
+static int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x,
+                                const int32_t * ids, const float * w, int64_t k, int64_t T, float * out,
+                                cudaStream_t s, gx_serve_stats * stats) {
     if (a == nullptr || d == nullptr || x == nullptr || ids == nullptr || w == nullptr || out == nullptr) return GX_ERR_INVALID;
     if (!gx::supported_weight_type(d->type_gate) || !gx::supported_weight_type(d->type_down)) return GX_ERR_TYPE;
     if (d->type_up != d->type_gate) return GX_ERR_TYPE;
@@ -552,16 +633,13 @@ int gx_moe_layer_forward(gx_arena * a, uint32_t layer, const gx_layer_desc * d, 
     if (H % gx::row_align(d->type_gate) != 0 || I % gx::row_align(d->type_down) != 0) return GX_ERR_ALIGN;
     if (d->off_gate % 16 || d->off_up % 16) return GX_ERR_ALIGN;
     if (T == 0) return GX_OK;
-    return guarded([&] {
-        std::lock_guard<std::mutex> lock(a->mu);
-        ck(cudaSetDevice(a->device));
+    {
         const SlotPolicy & P = a->policy->impl;
         if (layer < P.first_layer() || layer > P.last_layer()) return GX_ERR_INVALID;
         const uint32_t li = a->L(layer);
         if (d->off_up + gx::row_bytes(d->type_up, H) * I > a->record_raw[li] ||
             (uint64_t)gx::row_bytes(d->type_down, I) * H > d->off_gate)
             return GX_ERR_INVALID;
-        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         const int64_t n = k * T;
         std::vector<int32_t> slots((size_t)n);
         int rc = arena_serve(a, layer, ids, (uint32_t)n, slots.data(), a->ev_done[li], s, stats);
@@ -593,6 +671,18 @@ int gx_moe_layer_forward(gx_arena * a, uint32_t layer, const gx_layer_desc * d, 
             p.nbi1 = k * 4;
         }
 
+        cudaEvent_t tv[3] = {nullptr, nullptr, nullptr};
+        if (a->timing) {
+            while (a->tev.size() < a->tev_used + 3) {
+                cudaEvent_t e;
+                ck(cudaEventCreate(&e));
+                a->tev.push_back(e);
+            }
+            for (int j = 0; j < 3; ++j) tv[j] = a->tev[a->tev_used + j];
+            a->tev_used += 3;
+        }
+        if (tv[0]) ck(cudaEventRecord(tv[0], s));
+
         // gate + up + activation -> act [I, k, T]
         gx::RowsParams g = p;
         g.w0 = base + d->off_gate;
@@ -611,6 +701,7 @@ int gx_moe_layer_forward(gx_arena * a, uint32_t layer, const gx_layer_desc * d, 
         static const int cands_gu[] = {8, 4, 2, 1};
         if (pick_rows(d->type_gate, gx::kModeGateUp, g, n, cands_gu, 4) == 0) return GX_ERR_ALIGN;
         ck(gx::launch_rows(d->type_gate, gx::kModeGateUp, g, dim3((unsigned)(I / g.R), (unsigned)n), s));
+        if (tv[1]) ck(cudaEventRecord(tv[1], s));
 
         // down + weighted combine in slot order -> out [H, T]
         gx::RowsParams dn = p;
@@ -627,9 +718,10 @@ int gx_moe_layer_forward(gx_arena * a, uint32_t layer, const gx_layer_desc * d, 
         static const int cands_dn[] = {8, 4, 2, 1};
         if (pick_rows(d->type_down, gx::kModeDownCombine, dn, T, cands_dn, 4) == 0) return GX_ERR_ALIGN;
         ck(gx::launch_rows(d->type_down, gx::kModeDownCombine, dn, dim3((unsigned)(H / dn.R), (unsigned)T), s));
+        if (tv[2]) ck(cudaEventRecord(tv[2], s));
         ck(cudaEventRecord(a->ev_done[li], s));
         return GX_OK;
-    });
+    }
 }
 
 // --------------------------------------------------------------- synthetic

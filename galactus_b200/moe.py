@@ -127,7 +127,7 @@ class Arena:
 
     def __init__(self, model: ModelShape, capacity_bytes: int, *, protected_fraction: float = 0.75,
                  policy: int = L.POLICY_AUTO, device: int = 0, host_tier: bool = True, max_tokens: int = 1,
-                 first_layer: int = 0, plan_quotas: Sequence[int] | None = None):
+                 first_layer: int = 0, plan_quotas: Sequence[int] | None = None, host_tier_base: int = 0):
         self._lib = L.lib()
         self.model = model
         self.first_layer = first_layer
@@ -146,6 +146,7 @@ class Arena:
         cfg.max_tokens = max_tokens
         cfg.hidden = model.hidden
         cfg.intermediate = model.intermediate
+        cfg.host_tier_base = host_tier_base or None
         h = C.c_void_p()
         L.check(self._lib.gx_arena_create(C.byref(cfg), C.byref(h)), "gx_arena_create")
         self.h = h
@@ -215,6 +216,14 @@ class Arena:
     def warm_all(self, stream=None) -> None:
         L.check(self._lib.gx_arena_warm_all(self.h, _stream(stream)), "gx_arena_warm_all")
 
+    def timing(self, enable: bool) -> None:
+        L.check(self._lib.gx_arena_timing(self.h, 1 if enable else 0))
+
+    def timing_read(self) -> tuple[float, float, int]:
+        a, b, n = C.c_double(), C.c_double(), C.c_uint64()
+        L.check(self._lib.gx_arena_timing_read(self.h, C.byref(a), C.byref(b), C.byref(n)), "gx_arena_timing_read")
+        return a.value, b.value, n.value
+
     def stats(self) -> dict:
         s = L.gx_arena_stats()
         L.check(self._lib.gx_stats(self.h, C.byref(s)))
@@ -229,6 +238,33 @@ class Arena:
                                                k, T, _ptr(out), _stream(stream), C.byref(st)),
                 "gx_moe_layer_forward")
         return st
+
+
+class StackCall:
+    """A prepared gx_moe_stack_forward call: fixed device pointers per layer,
+    host routes swapped in per call (no per-layer Python work)."""
+
+    def __init__(self, arena: "Arena", first_layer: int, n_layers: int, x_ptrs, w_ptrs, out_ptrs, k: int, T: int):
+        self.arena, self.first, self.n, self.k, self.T = arena, first_layer, n_layers, k, T
+        self.x = (C.c_void_p * n_layers)(*x_ptrs)
+        self.w = (C.c_void_p * n_layers)(*w_ptrs)
+        self.out = (C.c_void_p * n_layers)(*out_ptrs)
+        self.st = L.gx_serve_stats()
+        self.fn = arena._lib.gx_moe_stack_forward
+
+    def set_pointers(self, x_ptrs=None, w_ptrs=None, out_ptrs=None):
+        for arr, ptrs in ((self.x, x_ptrs), (self.w, w_ptrs), (self.out, out_ptrs)):
+            if ptrs is not None:
+                for i, p in enumerate(ptrs):
+                    arr[i] = p
+
+    def __call__(self, ids: np.ndarray, stream=None) -> L.gx_serve_stats:
+        """ids: int32 C-contiguous [n_layers, T, k] on the host."""
+        rc = self.fn(self.arena.h, self.first, self.n, C.byref(self.arena.desc), self.x, ids.ctypes.data, self.w,
+                     self.k, self.T, self.out, _stream(stream), C.byref(self.st))
+        if rc != L.GX_OK:
+            raise L.GxError(rc, "gx_moe_stack_forward")
+        return self.st
 
 
 def mul_mat_id(type_: int, as_, ne00: int, ne01: int, nb01: int, nb02: int, n_as: int,

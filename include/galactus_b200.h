@@ -142,6 +142,8 @@ typedef struct gx_arena_config {
     int64_t max_tokens;          /* largest micro-batch the layer entry point will see */
     int64_t hidden;              /* H, for the layer entry point's scratch */
     int64_t intermediate;        /* I */
+    void * host_tier_base;       /* optional caller-owned PINNED tier (layer-major, expert-minor records,
+                                    record_bytes apart); used instead of allocating one when host_tier = 1 */
 } gx_arena_config;
 
 int gx_arena_create(const gx_arena_config * config, gx_arena ** out);
@@ -185,6 +187,13 @@ typedef struct gx_arena_stats {
     uint64_t copies;
 } gx_arena_stats;
 int gx_stats(gx_arena * arena, gx_arena_stats * stats);
+
+/* Kernel timing of the layer entry point: when enabled, every call records
+ * CUDA events around its two kernels on the caller's stream; read returns the
+ * summed device milliseconds of the gate/up and down kernels and the number of
+ * calls since the last read (waiting for the last event). */
+int gx_arena_timing(gx_arena * arena, int enable);
+int gx_arena_timing_read(gx_arena * arena, double * gate_up_ms, double * down_ms, uint64_t * calls);
 
 /* ---------------------------------------------------------------- kernels
  * ggml_mul_mat_id with ggml's tensor conventions (all device pointers):
@@ -238,6 +247,15 @@ typedef struct gx_layer_desc {
 int gx_moe_layer_forward(gx_arena * arena, uint32_t layer, const gx_layer_desc * desc,
                          const float * x, const int32_t * ids, const float * w, int64_t k, int64_t T,
                          float * out, void * stream, gx_serve_stats * stats);
+
+/* A stack of consecutive MoE layers for one micro-batch whose routes are all
+ * known (the reference's "token" serving regime, src/h4/h4-expert-store.hpp:
+ * 13-16): for each layer i, layer first_layer+i runs as gx_moe_layer_forward
+ * on x[i], ids + i*k*T, w[i] -> out[i]. x, w, out are arrays of n_layers
+ * device pointers; ids is HOST i32 [n_layers, T, k]. Stats are summed. */
+int gx_moe_stack_forward(gx_arena * arena, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * desc,
+                         const float * const * x, const int32_t * ids, const float * const * w, int64_t k, int64_t T,
+                         float * const * out, void * stream, gx_serve_stats * stats);
 
 /* ------------------------------------------------------------- synthetic
  * Seeded synthetic data written straight into device memory (test and bench

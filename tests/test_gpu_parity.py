@@ -42,6 +42,20 @@ def no_device_error(gxlib):
     assert device_error() == 0
 
 
+@pytest.fixture(autouse=True)
+def clear_device_error(gxlib):
+    """Each test starts with the device error word cleared."""
+    try:
+        import torch as _t
+        if _t.cuda.is_available():
+            from galactus_b200.moe import device_error
+            gxlib.lib().gx_device_init(0)
+            device_error()
+    except Exception:
+        pass
+    yield
+
+
 @pytest.mark.parametrize("t", [Q8_0, Q4_K, Q6_K, MXFP4, IQ1_S])
 def test_synth_weights_bytes(gxlib, orc, dev, t):
     ne00 = 2880 if t == MXFP4 else 2048
@@ -81,7 +95,8 @@ def test_quantize_rows_bitwise(gxlib, orc, dev, vdt, n):
     want = orc.quantize(vdt, x)
     pitch = (want.shape[1] + 15) // 16 * 16
     out = torch.zeros(9 * pitch, dtype=torch.uint8, device=dev)
-    gxlib.check(gxlib.lib().gx_quantize_rows(vdt, D(x).data_ptr(), n, 9, n * 4, out.data_ptr(), pitch, None))
+    xd = D(x)
+    gxlib.check(gxlib.lib().gx_quantize_rows(vdt, xd.data_ptr(), n, 9, n * 4, out.data_ptr(), pitch, None))
     got = H(out).reshape(9, pitch)[:, :want.shape[1]]
     np.testing.assert_array_equal(got, want)
 
@@ -104,7 +119,8 @@ def test_activations_and_combine_bitwise(gxlib, orc, dev):
     y = rng.standard_normal((5, 8, 2048)).astype(np.float32)
     wt = rng.random((5, 8)).astype(np.float32)
     o = torch.empty((5, 2048), dtype=torch.float32, device=dev)
-    gxlib.check(gxlib.lib().gx_combine(D(y).data_ptr(), D(wt).data_ptr(), o.data_ptr(), 2048, 8, 5, None))
+    yd, wd = D(y), D(wt)          # keep the device copies alive until the kernel has run
+    gxlib.check(gxlib.lib().gx_combine(yd.data_ptr(), wd.data_ptr(), o.data_ptr(), 2048, 8, 5, None))
     np.testing.assert_array_equal(bits(H(o)), bits(orc.combine(y, wt)))
 
 
