@@ -122,6 +122,9 @@ struct gx_arena {
     int64_t max_tokens = 0, hidden = 0, intermediate = 0;
     uint32_t used = 0;
     float * d_act = nullptr;            // [I, k, T] activations between gate/up and down
+    uint8_t * d_xq = nullptr;           // quantized layer inputs, split layout, one row per token
+    uint8_t * d_actq = nullptr;         // quantized activations of the down projection, one row per (token, slot)
+    int32_t * d_cnt = nullptr;          // per (token, slot, Q8 block) completion counters, zero between calls
     int32_t * d_ids = nullptr;          // kStageRing x (used * max_tokens) slot ids
     int32_t * h_ids = nullptr;          // pinned staging of the same
     cudaEvent_t ev_stage[kStageRing] = {};
@@ -241,6 +244,9 @@ int gx_arena_destroy(gx_arena * a) {
     if (a->d_arena) cudaFree(a->d_arena);
     if (a->d_act) cudaFree(a->d_act);
     if (a->d_ids) cudaFree(a->d_ids);
+    if (a->d_xq) cudaFree(a->d_xq);
+    if (a->d_actq) cudaFree(a->d_actq);
+    if (a->d_cnt) cudaFree(a->d_cnt);
     if (a->h_ids) cudaFreeHost(a->h_ids);
     for (auto e : a->tev) if (e) cudaEventDestroy(e);
     if (a->h_tier && a->own_tier) cudaFreeHost(a->h_tier);
@@ -301,6 +307,14 @@ int gx_arena_create(const gx_arena_config * c, gx_arena ** out) {
         if (c->max_tokens > 0 && c->intermediate > 0) {
             const int64_t pairs = (int64_t)c->profile.used * c->max_tokens;
             ck(cudaMalloc(&a->d_act, (size_t)(pairs * c->intermediate * sizeof(float))));
+            const int64_t px = std::max(gx::act_layout(gx::GX_T_Q8_0, (int)c->hidden).pitch,
+                                        gx::act_layout(gx::GX_T_Q8_K, (int)c->hidden).pitch);
+            const int64_t pa = std::max(gx::act_layout(gx::GX_T_Q8_0, (int)c->intermediate).pitch,
+                                        gx::act_layout(gx::GX_T_Q8_K, (int)c->intermediate).pitch);
+            ck(cudaMalloc(&a->d_xq, (size_t)(c->max_tokens * px)));
+            ck(cudaMalloc(&a->d_actq, (size_t)(pairs * pa)));
+            ck(cudaMalloc(&a->d_cnt, (size_t)(pairs * (c->intermediate / 32 + 1) * sizeof(int32_t))));
+            ck(cudaMemset(a->d_cnt, 0, (size_t)(pairs * (c->intermediate / 32 + 1) * sizeof(int32_t))));
             ck(cudaMalloc(&a->d_ids, (size_t)(kStageRing * pairs * sizeof(int32_t))));
             ck(cudaHostAlloc(&a->h_ids, (size_t)(kStageRing * pairs * sizeof(int32_t)), cudaHostAllocDefault));
             for (int i = 0; i < kStageRing; ++i) ck(cudaEventCreateWithFlags(&a->ev_stage[i], cudaEventDisableTiming));
@@ -642,8 +656,11 @@ static int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_des
             return GX_ERR_INVALID;
         const int64_t n = k * T;
         std::vector<int32_t> slots((size_t)n);
-        int rc = arena_serve(a, layer, ids, (uint32_t)n, slots.data(), a->ev_done[li], s, stats);
+        gx_serve_stats sst{};
+        int rc = arena_serve(a, layer, ids, (uint32_t)n, slots.data(), a->ev_done[li], s, &sst);
         if (rc != GX_OK) return rc;
+        if (stats) *stats = sst;
+        const uint32_t last_misses = sst.misses;
 
         uint8_t * base = a->d_arena + a->slab_base[li];
         gx::RowsParams p{};
@@ -681,43 +698,87 @@ static int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_des
             for (int j = 0; j < 3; ++j) tv[j] = a->tev[a->tev_used + j];
             a->tev_used += 3;
         }
+
+        const int vdt_g = gx::vec_dot_type(d->type_gate), vdt_d = gx::vec_dot_type(d->type_down);
+        // without misses nothing but kernels precede: let each kernel start
+        // streaming its weights while the previous one finishes
+        // (kernel timing measures each kernel alone, without the overlap)
+        const bool pdl = !a->timing;
+        const bool had_misses = last_misses > 0;
+        ck(gx::launch_quant_split(vdt_g, x, (int)H, T, H * 4, a->d_xq, s, pdl && !had_misses));
         if (tv[0]) ck(cudaEventRecord(tv[0], s));
 
-        // gate + up + activation -> act [I, k, T]
-        gx::RowsParams g = p;
+        // gate + up + activation -> quantized down input
+        gx::DecodeParams g{};
         g.w0 = base + d->off_gate;
         g.w1 = base + d->off_up;
         g.nb01 = gx::row_bytes(d->type_gate, H);
+        g.nb02 = (int64_t)a->record[li];
         g.ne00 = (int32_t)H;
         g.ne01 = (int32_t)I;
-        g.src = x;
-        g.nb11 = H * 4;
-        g.nb12 = H * 4;
-        g.ne11 = 1;
-        g.dst = a->d_act;
+        g.n_as = p.n_as;
+        g.k = p.k;
+        g.T = p.T;
+        g.ids = p.ids;
+        g.use_inline = p.use_inline;
+        std::memcpy(g.inline_ids, p.inline_ids, sizeof(g.inline_ids));
+        g.aq = a->d_xq;
+        g.al = gx::act_layout(vdt_g, (int)H);
+        g.a_rows = 1;
+        g.act_f32 = a->d_act;
+        g.act_q = a->d_actq;
+        g.al2 = gx::act_layout(vdt_d, (int)I);
+        g.vdt2 = vdt_d;
+        g.qblk = vdt_d == gx::GX_T_Q8_0 ? 32 : 256;
+        g.counters = a->d_cnt;
         g.act = d->act;
         g.alpha = d->alpha;
         g.limit = d->limit;
-        static const int cands_gu[] = {8, 4, 2, 1};
-        if (pick_rows(d->type_gate, gx::kModeGateUp, g, n, cands_gu, 4) == 0) return GX_ERR_ALIGN;
-        ck(gx::launch_rows(d->type_gate, gx::kModeGateUp, g, dim3((unsigned)(I / g.R), (unsigned)n), s));
+        {
+            static const int cands[] = {8, 16, 4, 2};
+            int threads = 0;
+            g.R = 0;
+            for (int R : cands) {
+                if (I % R || g.qblk % R) continue;
+                gx::DecodeParams t = g;
+                t.R = R;
+                if (gx::decode_layout(1, t, threads) == 0) continue;
+                g.R = R;
+                break;
+            }
+            if (g.R == 0) return GX_ERR_ALIGN;
+            g.n_units = (int32_t)(n * (I / g.R));
+        }
+        ck(gx::launch_decode(d->type_gate, 1, g, s, pdl));
         if (tv[1]) ck(cudaEventRecord(tv[1], s));
 
         // down + weighted combine in slot order -> out [H, T]
-        gx::RowsParams dn = p;
+        gx::DecodeParams dn = g;
         dn.w0 = base;
+        dn.w1 = nullptr;
         dn.nb01 = gx::row_bytes(d->type_down, I);
         dn.ne00 = (int32_t)I;
         dn.ne01 = (int32_t)H;
-        dn.src = a->d_act;
-        dn.nb11 = I * 4;
-        dn.nb12 = I * k * 4;
-        dn.ne11 = (int32_t)k;
+        dn.aq = a->d_actq;
+        dn.al = gx::act_layout(vdt_d, (int)I);
+        dn.a_rows = (int32_t)k;
         dn.rw = w;
-        dn.dst = out;
-        static const int cands_dn[] = {8, 4, 2, 1};
-        if (pick_rows(d->type_down, gx::kModeDownCombine, dn, T, cands_dn, 4) == 0) return GX_ERR_ALIGN;
-        ck(gx::launch_rows(d->type_down, gx::kModeDownCombine, dn, dim3((unsigned)(H / dn.R), (unsigned)T), s));
+        dn.out = out;
+        {
+            int threads = 0;
+            dn.R = 0;
+            for (int R = (int)(32 / k); R >= 1; R /= 2) {
+                if (R < 1 || H % R) continue;
+                gx::DecodeParams t = dn;
+                t.R = R;
+                if (gx::decode_layout(2, t, threads) == 0) continue;
+                dn.R = R;
+                break;
+            }
+            if (dn.R == 0) return GX_ERR_ALIGN;
+            dn.n_units = (int32_t)(T * (H / dn.R));
+        }
+        ck(gx::launch_decode(d->type_down, 2, dn, s, pdl));
         if (tv[2]) ck(cudaEventRecord(tv[2], s));
         ck(cudaEventRecord(a->ev_done[li], s));
         return GX_OK;

@@ -18,59 +18,10 @@
 
 #include "gx_device.cuh"
 #include "gx_kernels.h"
+#include "gx_moe.cuh"
 
 namespace gx {
 
-__device__ int g_dev_error = 0;
-
-__device__ __forceinline__ void record_error(int code) { atomicCAS(&g_dev_error, 0, code); }
-
-// --------------------------------------------------------- TMA / mbarrier
-
-__device__ __forceinline__ uint32_t smem_u32(const void * p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_fence_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-// bulk copy global -> shared, completion counted on the mbarrier (no multicast)
-__device__ __forceinline__ void bulk_g2s(void * dst_smem, const void * src_gmem, uint32_t bytes, uint64_t * bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst_smem)),
-        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-
-// Every wait is bounded: after the limit the kernel records a timeout and
-// gives up instead of spinning forever.
-constexpr uint32_t kWaitLimit = 1u << 24;
-
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t * bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-    }
-    return false;
-}
 
 // ------------------------------------------------------------ row kernel
 
@@ -528,6 +479,110 @@ cudaError_t launch_synth_weights(int type, void * dst, int64_t ne00, int64_t n_r
                                                                      synth_key(seed, stream_id), sigma);
     return cudaGetLastError();
 }
+
+// ------------------------------------------------------- decode launchers
+
+template <int TYPE, int MODE>
+static cudaError_t launch_decode_t(DecodeParams & p, int threads, uint32_t smem, cudaStream_t stream, bool pdl) {
+    static int configured = 0;
+    if ((int)smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(k_decode<TYPE, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = (int)smem;
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<TYPE, MODE>, threads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    int sms = 148;
+    {
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const int grid = p.n_units < per_sm * sms ? p.n_units : per_sm * sms;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, k_decode<TYPE, MODE>, p);
+    return e;
+}
+
+// Shared-memory layout and tiling of a decode launch; 0 when it cannot fit.
+uint32_t decode_layout(int mode, DecodeParams & p, int & threads) {
+    const int nexp = mode == 1 ? 2 : p.k;
+    threads = 4 * nexp * p.R;
+    if (threads > 128 || threads < 32 || threads % 32 != 0) return 0;
+    if (p.nb01 % 16 == 0) {
+        p.row_copy = 1;
+        p.pitch_w = (int32_t)(p.nb01 % 128 == 0 ? p.nb01 + 16 : p.nb01);
+    } else {
+        if ((p.R * p.nb01) % 16 != 0) return 0;
+        p.row_copy = 0;
+        p.pitch_w = (int32_t)p.nb01;
+    }
+    p.stage_bytes = (int32_t)align_up((uint64_t)nexp * p.R * p.pitch_w + 16, 128);
+    const uint32_t act_bytes = align_up((uint64_t)p.a_rows * p.al.pitch + 16, 128);
+    const uint32_t fixed = 128 + act_bytes + 128 + 128;
+    const uint32_t budget = 110 * 1024;
+    int S = (int)((budget > fixed ? budget - fixed : 0) / (uint32_t)p.stage_bytes);
+    if (S > 4) S = 4;
+    if (S < 2) S = 2;
+    p.S = S;
+    p.act_off = 128;
+    p.stage_off = p.act_off + act_bytes;
+    p.dots_off = p.stage_off + (uint32_t)S * p.stage_bytes;
+    p.flag_off = p.dots_off + 128 * 4;
+    const uint32_t total = p.flag_off + 128;
+    if (total > kMaxSmem) return 0;
+    return total;
+}
+
+template <int MODE>
+static cudaError_t launch_decode_mode(int type, DecodeParams & p, int threads, uint32_t smem, cudaStream_t stream, bool pdl) {
+    switch (type) {
+        case GX_T_Q8_0: return launch_decode_t<GX_T_Q8_0, MODE>(p, threads, smem, stream, pdl);
+        case GX_T_MXFP4: return launch_decode_t<GX_T_MXFP4, MODE>(p, threads, smem, stream, pdl);
+        case GX_T_Q4_K: return launch_decode_t<GX_T_Q4_K, MODE>(p, threads, smem, stream, pdl);
+        case GX_T_Q6_K: return launch_decode_t<GX_T_Q6_K, MODE>(p, threads, smem, stream, pdl);
+        case GX_T_IQ1_S: return launch_decode_t<GX_T_IQ1_S, MODE>(p, threads, smem, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_decode(int type, int mode, DecodeParams & p, cudaStream_t stream, bool pdl) {
+    int threads = 0;
+    const uint32_t smem = decode_layout(mode, p, threads);
+    if (smem == 0) return cudaErrorInvalidConfiguration;
+    return mode == 1 ? launch_decode_mode<1>(type, p, threads, smem, stream, pdl)
+                     : launch_decode_mode<2>(type, p, threads, smem, stream, pdl);
+}
+
+cudaError_t launch_quant_split(int vdt, const float * src, int ne0, int64_t nrows, int64_t nb1, uint8_t * dst,
+                               cudaStream_t stream, bool pdl) {
+    const ActLayout L = act_layout(vdt, ne0);
+    const int64_t warps = nrows * (ne0 / (vdt == GX_T_Q8_0 ? 32 : 256));
+    if (warps <= 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((warps + 3) / 4));
+    cfg.blockDim = dim3(128);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (vdt == GX_T_Q8_0) return cudaLaunchKernelEx(&cfg, k_quant_split<GX_T_Q8_0>, src, ne0, nrows, nb1, dst, L);
+    return cudaLaunchKernelEx(&cfg, k_quant_split<GX_T_Q8_K>, src, ne0, nrows, nb1, dst, L);
+}
+
+ActLayout act_layout_host(int vdt, int n) { return act_layout(vdt, n); }
 
 cudaError_t read_and_clear_device_error(int * code) {
     int zero = 0;

@@ -4,6 +4,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "gx_formats.h"
+
 namespace gx {
 
 constexpr int kRowsThreads = 128;
@@ -35,6 +37,69 @@ struct RowsParams {
 };
 
 enum { kModePlain = 0, kModeGateUp = 1, kModeDownCombine = 2 };
+
+// ------------------------------------------------------------ split layout
+
+struct ActLayout {
+    int32_t d_off;    // byte offset of the scales (fp16 for Q8_0, f32 for Q8_K)
+    int32_t bs_off;   // byte offset of the Q8_K block sums (int16 per 16 elements)
+    int32_t pitch;    // bytes per row, multiple of 16
+};
+
+GX_HD int32_t align16i(int64_t v) { return (int32_t)((v + 15) / 16 * 16); }
+
+GX_HD ActLayout act_layout(int vdt, int n) {
+    ActLayout a;
+    a.d_off = n;
+    if (vdt == GX_T_Q8_0) {
+        a.bs_off = n + (n / 32) * 2;
+        a.pitch = align16i(a.bs_off);
+    } else {
+        a.bs_off = n + (n / 256) * 4;
+        a.pitch = align16i(a.bs_off + (n / 16) * 2);
+    }
+    return a;
+}
+
+struct DecodeParams {
+    const uint8_t * w0;        // gate (GATE_UP) or down (DOWN) role base of slot 0
+    const uint8_t * w1;        // up role base (GATE_UP)
+    int64_t nb01, nb02;        // row bytes, record stride
+    int32_t ne00, ne01;        // input length, output rows per expert
+    int32_t n_as;              // slots of the layer
+    int32_t k, T;
+    int32_t R;                 // rows per expert per stage
+    int32_t S;                 // pipeline stages
+    int32_t row_copy;          // 1: one bulk copy per row (pitch_w), 0: one per R-row tile
+    int32_t pitch_w;           // shared-memory bytes between rows of a stage
+    int32_t stage_bytes;
+    int32_t n_units;
+    const int32_t * ids;       // slot ids [T, k] (device) unless use_inline
+    int32_t use_inline;
+    int32_t inline_ids[kInlineIds];
+    const uint8_t * aq;        // quantized input rows (split layout)
+    ActLayout al;              // layout of aq rows
+    int32_t a_rows;            // aq rows loaded per token (1 for GATE_UP, k for DOWN)
+    // GATE_UP outputs
+    float * act_f32;           // [T*k, ne01]
+    uint8_t * act_q;           // [T*k, al2.pitch] split-layout quantized activations for the down projection
+    ActLayout al2;
+    int32_t vdt2, qblk;        // down input quant type and its block rows
+    int32_t * counters;        // [T*k, ne01/qblk], zero between calls
+    int32_t act;
+    float alpha, limit;
+    // DOWN outputs
+    const float * rw;          // router weights [T, k]
+    float * out;               // [T, ne01]
+    uint32_t act_off, stage_off, dots_off, flag_off;
+};
+
+
+
+uint32_t decode_layout(int mode, DecodeParams & p, int & threads);
+cudaError_t launch_decode(int type, int mode, DecodeParams & p, cudaStream_t stream, bool pdl);
+cudaError_t launch_quant_split(int vdt, const float * src, int ne0, int64_t nrows, int64_t nb1, uint8_t * dst,
+                               cudaStream_t stream, bool pdl);
 
 uint32_t rows_smem_layout(int type, int mode, RowsParams & p);
 cudaError_t launch_rows(int type, int mode, RowsParams & p, dim3 grid, cudaStream_t stream);

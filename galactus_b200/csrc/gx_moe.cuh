@@ -1,0 +1,473 @@
+// Decode-path kernels of the routed-expert FFN (sm_100a): persistent CTAs,
+// multi-stage bulk-TMA pipelines, four lanes per weight row.
+//
+// Activations are quantized once into an internal "split" layout (all int8
+// quants of a row contiguous, then the block scales, then the Q8_K block
+// sums), so the dot loops read them with aligned 32-bit loads. The values are
+// exactly those of ggml's Q8_0 / Q8_K blocks; only the byte layout differs.
+//
+// A weight row is processed by a quad of lanes: lane l owns one quarter of
+// every 64- or 256-element unit. Integer partial sums are exact, so the quad
+// adds them with shuffles in any order; the float tail is then evaluated in
+// the reference's order (diff:1049-1054, 1167-1174, 1254-1259, 1366-1370,
+// 335-345) in registers, identically in the four lanes (or, for Q8_0, one
+// accumulator chain per lane, reduced by the NEON faddp tree).
+#pragma once
+
+#include <cstdint>
+
+#include "gx_device.cuh"
+#include "gx_kernels.h"
+
+namespace gx {
+
+// quantize block ib of an f32 row into the split layout, one warp
+template <int VDT, bool COHERENT>
+__device__ __forceinline__ void quant_block_split(const float * x, uint8_t * row, const ActLayout & L, int ib, int lane) {
+    if (VDT == GX_T_Q8_0) {
+        const float v = COHERENT ? __ldcg(x + 32 * ib + lane) : __ldg(x + 32 * ib + lane);
+        float a = fabsf(v);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+        const float d = __fdiv_rn(a, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        row[32 * ib + lane] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v, id));
+        if (lane == 0) *reinterpret_cast<uint16_t *>(row + L.d_off + 2 * ib) = f2h(d);
+    } else {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = COHERENT ? __ldcg(x + 256 * ib + 8 * lane + j) : __ldg(x + 256 * ib + 8 * lane + j);
+        float amax = 0.0f, vmax = 0.0f;
+        int imax = 8 * lane;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float av = fabsf(v[j]);
+            if (av > amax) { amax = av; vmax = v[j]; imax = 8 * lane + j; }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+            const float ov = __shfl_xor_sync(0xffffffffu, vmax, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, imax, off);
+            if (oa > amax || (oa == amax && oi < imax)) { amax = oa; vmax = ov; imax = oi; }
+        }
+        int8_t * qs = reinterpret_cast<int8_t *>(row + 256 * ib);
+        int16_t * bs = reinterpret_cast<int16_t *>(row + L.bs_off) + 16 * ib;
+        float * dp = reinterpret_cast<float *>(row + L.d_off) + ib;
+        if (amax == 0.0f) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) qs[8 * lane + j] = 0;
+            if (lane < 16) bs[lane] = 0;
+            if (lane == 0) *dp = 0.0f;
+            return;
+        }
+        const float iscale = __fdiv_rn(-127.0f, vmax);
+        int lsum = 0;
+        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int q = min(127, __float2int_rn(__fmul_rn(iscale, v[j])));
+            lsum += q;
+            if (j < 4) w0 |= ((uint32_t)(q & 0xff)) << (8 * j); else w1 |= ((uint32_t)(q & 0xff)) << (8 * (j - 4));
+        }
+        *reinterpret_cast<uint2 *>(qs + 8 * lane) = make_uint2(w0, w1);
+        const int pair = lsum + __shfl_xor_sync(0xffffffffu, lsum, 1);
+        if ((lane & 1) == 0) bs[lane >> 1] = (int16_t)pair;
+        if (lane == 0) *dp = __fdiv_rn(1.0f, iscale);
+    }
+}
+
+// ----------------------------------------------------------- quad dots
+
+__device__ __forceinline__ int quad_sum(int v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    return v;
+}
+
+template <int TYPE> struct Quad;
+
+template <> struct Quad<GX_T_Q8_0> {
+    static constexpr int VDT = GX_T_Q8_0;
+    static constexpr int UNIT = 64;   // a pair of 32-element blocks
+    struct St { float e = 0.0f, o = 0.0f; };
+    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int u,
+                                                int l, St & st) {
+        const int pe = wo + 68 * u;
+        const uint32_t w0 = lds32(wb + pe + 4 * l), w1 = lds32(wb + pe + 4 * l + 4);
+        const uint32_t w4 = lds32(wb + pe + 16 + 4 * l), w5 = lds32(wb + pe + 20 + 4 * l);
+        const uint32_t xea = __funnelshift_r(w0, w1, 16), xeb = __funnelshift_r(w4, w5, 16);
+        const uint32_t xoa = lds32(wb + pe + 36 + 4 * l), xob = lds32(wb + pe + 52 + 4 * l);
+        const float dxe = h2f(ld_u16(wb, pe)), dxo = h2f(ld_u16(wb, pe + 34));
+        const uint8_t * aq = ar + 64 * u;
+        const uint32_t yea = lds32(aq + 4 * l), yeb = lds32(aq + 16 + 4 * l);
+        const uint32_t yoa = lds32(aq + 32 + 4 * l), yob = lds32(aq + 48 + 4 * l);
+        const uint32_t dd = lds32(ar + L.d_off + 4 * u);
+        const int ie = dp4a(xeb, yeb, dp4a(xea, yea, 0));
+        const int io = dp4a(xob, yob, dp4a(xoa, yoa, 0));
+        st.e = __fmaf_rn((float)ie, __fmul_rn(dxe, h2f((uint16_t)(dd & 0xffffu))), st.e);
+        st.o = __fmaf_rn((float)io, __fmul_rn(dxo, h2f((uint16_t)(dd >> 16))), st.o);
+    }
+    // ((e0+e1)+(e2+e3)) + ((o0+o1)+(o2+o3)), the NEON faddp trees
+    __device__ __forceinline__ static float finish(St & st) {
+        float e = st.e, o = st.o;
+        e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, 1));
+        o = __fadd_rn(o, __shfl_xor_sync(0xffffffffu, o, 1));
+        e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, 2));
+        o = __fadd_rn(o, __shfl_xor_sync(0xffffffffu, o, 2));
+        return __fadd_rn(e, o);
+    }
+};
+
+template <> struct Quad<GX_T_MXFP4> {
+    static constexpr int VDT = GX_T_Q8_0;
+    static constexpr int UNIT = 64;
+    struct St { float s = 0.0f; };
+    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int u,
+                                                int l, St & st) {
+        const int pe = wo + 34 * u;
+        uint32_t qe[1], qo[1];
+        ld_words<1>(wb, pe + 1 + 4 * l, qe);
+        ld_words<1>(wb, pe + 18 + 4 * l, qo);
+        const uint8_t * aq = ar + 64 * u;
+        int ie = dp4a(mxfp4_lut(qe[0] & 0x0f0f0f0fu), lds32(aq + 4 * l), 0);
+        ie = dp4a(mxfp4_lut((qe[0] >> 4) & 0x0f0f0f0fu), lds32(aq + 16 + 4 * l), ie);
+        int io = dp4a(mxfp4_lut(qo[0] & 0x0f0f0f0fu), lds32(aq + 32 + 4 * l), 0);
+        io = dp4a(mxfp4_lut((qo[0] >> 4) & 0x0f0f0f0fu), lds32(aq + 48 + 4 * l), io);
+        ie = quad_sum(ie);
+        io = quad_sum(io);
+        const uint32_t dd = lds32(ar + L.d_off + 4 * u);
+        const float sce = __fmul_rn(h2f((uint16_t)(dd & 0xffffu)), e8m0_half(wb[pe]));
+        const float sco = __fmul_rn(h2f((uint16_t)(dd >> 16)), e8m0_half(wb[pe + 17]));
+        st.s = __fadd_rn(st.s, __fmaf_rn(sce, (float)ie, __fmul_rn(sco, (float)io)));
+    }
+    __device__ __forceinline__ static float finish(St & st) { return st.s; }
+};
+
+template <> struct Quad<GX_T_Q4_K> {
+    static constexpr int VDT = GX_T_Q8_K;
+    static constexpr int UNIT = 256;
+    struct St { float s = 0.0f; };
+    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int i,
+                                                int l, St & st) {
+        const int xo = wo + 144 * i;
+        uint32_t q[8];
+        ld_words<8>(wb, xo + 16 + 32 * l, q);
+        uint32_t sw[3];
+        ld_words<3>(wb, xo + 4, sw);
+        uint32_t dw[1];
+        ld_words<1>(wb, xo, dw);
+        const uint8_t * aq = ar + 256 * i + 64 * l;
+        int p1 = 0, p2 = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            p1 = dp4a(q[w] & 0x0f0f0f0fu, lds32(aq + 4 * w), p1);
+            p2 = dp4a((q[w] >> 4) & 0x0f0f0f0fu, lds32(aq + 32 + 4 * w), p2);
+        }
+        // 6-bit scale and min of sub-blocks a = 2l and 2l+1 (12-byte packing)
+        int sc[2], mn[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int a = 2 * l + h;
+            if (a < 4) {
+                sc[h] = (sw[0] >> (8 * a)) & 63;
+                mn[h] = (sw[1] >> (8 * a)) & 63;
+            } else {
+                const int b = a - 4;
+                sc[h] = ((sw[2] >> (8 * b)) & 0x0f) | (((sw[0] >> (8 * b + 6)) & 3) << 4);
+                mn[h] = ((sw[2] >> (8 * b + 4)) & 0x0f) | (((sw[1] >> (8 * b + 6)) & 3) << 4);
+            }
+        }
+        const uint2 bsw = *reinterpret_cast<const uint2 *>(ar + L.bs_off + 32 * i + 8 * l);
+        const int q8s0 = (int16_t)((int16_t)(bsw.x & 0xffff) + (int16_t)(bsw.x >> 16));
+        const int q8s1 = (int16_t)((int16_t)(bsw.y & 0xffff) + (int16_t)(bsw.y >> 16));
+        const int sumi = quad_sum(p1 * sc[0] + p2 * sc[1]);
+        const int prod = quad_sum(q8s0 * mn[0] + q8s1 * mn[1]);
+        const float yd = *reinterpret_cast<const float *>(ar + L.d_off + 4 * i);
+        st.s = __fmaf_rn(-__fmul_rn(yd, h2f((uint16_t)(dw[0] >> 16))), (float)prod, st.s);
+        st.s = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dw[0] & 0xffffu))), (float)sumi, st.s);
+    }
+    __device__ __forceinline__ static float finish(St & st) { return st.s; }
+};
+
+template <> struct Quad<GX_T_Q6_K> {
+    static constexpr int VDT = GX_T_Q8_K;
+    static constexpr int UNIT = 256;
+    struct St { float s = 0.0f; };
+    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int i,
+                                                int l, St & st) {
+        const int xo = wo + 210 * i;
+        const int h = l >> 1, odd = l & 1;
+        uint32_t ql[16], qh[8], scw[1];
+        ld_words<16>(wb, xo + 64 * h, ql);
+        ld_words<8>(wb, xo + 128 + 32 * h, qh);
+        ld_words<1>(wb, xo + 192 + 4 * l, scw);
+        const uint8_t * aq = ar + 256 * i + 64 * l;
+        const uint2 bsw = *reinterpret_cast<const uint2 *>(ar + L.bs_off + 32 * i + 8 * l);
+        const int bs4[4] = {(int16_t)(bsw.x & 0xffff), (int16_t)(bsw.x >> 16), (int16_t)(bsw.y & 0xffff),
+                            (int16_t)(bsw.y >> 16)};
+        int isum = 0, mins = 0;
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg) {
+            int pg = 0;
+#pragma unroll
+            for (int ww = 0; ww < 4; ++ww) {
+                const int w = 4 * gg + ww;
+                const uint32_t nib = (odd ? (ql[w] >> 4) : ql[w]) & 0x0f0f0f0fu;
+                const uint32_t sh = 4u * (uint32_t)odd + (w >= 8 ? 2u : 0u);
+                const uint32_t hb = (qh[w & 7] >> sh) & 0x03030303u;
+                pg = dp4a(nib | (hb << 4), lds32(aq + 4 * w), pg);
+            }
+            const int scg = (int)(int8_t)(scw[0] >> (8 * gg));
+            isum += pg * scg;
+            mins += bs4[gg] * scg;
+        }
+        isum = quad_sum(isum);
+        mins = quad_sum(mins);
+        const float yd = *reinterpret_cast<const float *>(ar + L.d_off + 4 * i);
+        st.s = __fmaf_rn(__fmul_rn(yd, h2f(ld_u16(wb, xo + 208))), (float)(isum - 32 * mins), st.s);
+    }
+    __device__ __forceinline__ static float finish(St & st) { return st.s; }
+};
+
+template <> struct Quad<GX_T_IQ1_S> {
+    static constexpr int VDT = GX_T_Q8_K;
+    static constexpr int UNIT = 256;
+    struct St { float s = 0.0f; };
+    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int i,
+                                                int l, St & st) {
+        const int xo = wo + 50 * i;
+        uint32_t qsw[2], qhw[1];
+        ld_words<2>(wb, xo + 2 + 8 * l, qsw);
+        ld_words<1>(wb, xo + 34 + 4 * l, qhw);
+        const uint8_t * aq = ar + 256 * i + 64 * l;
+        int p[2] = {0, 0}, ls[2], sg[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const uint32_t qh = (qhw[0] >> (16 * hh)) & 0xffffu;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t gi = ((qsw[hh] >> (8 * j)) & 0xffu) | (((qh >> (3 * j)) & 7u) << 8);
+                const uint2 g = g_iq1s_grid[gi];
+                p[hh] = dp4a(g.x, lds32(aq + 32 * hh + 8 * j), p[hh]);
+                p[hh] = dp4a(g.y, lds32(aq + 32 * hh + 8 * j + 4), p[hh]);
+            }
+            ls[hh] = 2 * (int)((qh >> 12) & 7u) + 1;
+            sg[hh] = (qh & 0x8000u) ? -1 : 1;
+        }
+        const uint2 bsw = *reinterpret_cast<const uint2 *>(ar + L.bs_off + 32 * i + 8 * l);
+        const int b0 = (int16_t)(bsw.x & 0xffff), b1 = (int16_t)(bsw.x >> 16);
+        const int b2 = (int16_t)(bsw.y & 0xffff), b3 = (int16_t)(bsw.y >> 16);
+        const int s1 = quad_sum(p[0] * ls[0]);
+        const int s2 = quad_sum(p[1] * ls[1]);
+        const int s3 = quad_sum((b0 + b1) * ls[0] * sg[0] + (b2 + b3) * ls[1] * sg[1]);
+        const float yd = *reinterpret_cast<const float *>(ar + L.d_off + 4 * i);
+        const float expr = __fmaf_rn((float)s3, 0.125f, (float)(s1 + s2));
+        st.s = __fmaf_rn(__fmul_rn(yd, h2f(ld_u16(wb, xo))), expr, st.s);
+    }
+    __device__ __forceinline__ static float finish(St & st) { return st.s; }
+};
+
+// --------------------------------------------------------- PDL and TMA
+
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ------------------------------------------------------ decode kernels
+
+__device__ __forceinline__ int32_t dec_id(const DecodeParams & p, int t, int s) {
+    return p.use_inline ? p.inline_ids[t * p.k + s] : p.ids[t * p.k + s];
+}
+
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t * bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 24); ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"((uint32_t)__cvta_generic_to_shared(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma_expect(uint64_t * bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            (uint32_t)__cvta_generic_to_shared(dst)),
+        "l"(src), "r"(bytes), "r"((uint32_t)__cvta_generic_to_shared(bar))
+        : "memory");
+}
+
+// Issue the weight copies of one unit into a stage. GATE_UP: R gate rows then
+// R up rows of the pair's expert; DOWN: R rows of each of the token's k experts.
+template <int MODE>
+__device__ __forceinline__ void issue_unit(const DecodeParams & p, int u, uint8_t * stage, uint64_t * bar) {
+    const int tiles = p.ne01 / p.R;
+    const int r0 = (u % tiles) * p.R;
+    const int nexp = MODE == 1 ? 2 : p.k;
+    tma_expect(bar, (uint32_t)(nexp * p.R) * (uint32_t)p.nb01);
+    for (int m = 0; m < nexp; ++m) {
+        const uint8_t * src;
+        if (MODE == 1) {
+            const int pair = u / tiles;
+            const int32_t e = dec_id(p, pair / p.k, pair % p.k);
+            src = (m == 0 ? p.w0 : p.w1) + (int64_t)e * p.nb02 + (int64_t)r0 * p.nb01;
+        } else {
+            const int t = u / tiles;
+            src = p.w0 + (int64_t)dec_id(p, t, m) * p.nb02 + (int64_t)r0 * p.nb01;
+        }
+        uint8_t * dst = stage + m * p.R * p.pitch_w;
+        if (p.row_copy) {
+            for (int r = 0; r < p.R; ++r) tma_load(dst + r * p.pitch_w, src + (int64_t)r * p.nb01, (uint32_t)p.nb01, bar);
+        } else {
+            tma_load(dst, src, (uint32_t)(p.R * p.nb01), bar);
+        }
+    }
+}
+
+// MODE 1: gate/up + activation, one (token, slot) pair per unit, then the
+//         quantization of each completed Q8 block of the activation row by the
+//         last CTA that contributed to it (no CTA ever waits for another).
+// MODE 2: down + weighted combine, one token per unit (all k slots).
+template <int TYPE, int MODE>
+__global__ void __launch_bounds__(128) k_decode(const DecodeParams p) {
+    using Q = Quad<TYPE>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t * full = reinterpret_cast<uint64_t *>(smem);   // S stage barriers, then the activation barrier
+    uint64_t * abar = full + p.S;
+    uint8_t * act = smem + p.act_off;
+    uint8_t * stages = smem + p.stage_off;
+    float * dots = reinterpret_cast<float *>(smem + p.dots_off);
+    int * flag = reinterpret_cast<int *>(smem + p.flag_off);
+    const int tid = threadIdx.x, lane = tid & 31, l = tid & 3, row = tid >> 2;
+    const int G = gridDim.x;
+    const int tiles = p.ne01 / p.R;
+    const int U = p.ne00 / Q::UNIT;
+
+    // every slot id of the call is checked before any load
+    {
+        int bad = 0;
+        for (int j = tid; j < p.T * p.k; j += blockDim.x) {
+            const int32_t e = p.use_inline ? p.inline_ids[j] : p.ids[j];
+            if (e < 0 || e >= p.n_as) bad = 1;
+        }
+        if (__syncthreads_or(bad)) {
+            if (tid == 0) record_error(GX_DEVERR_DOMAIN);
+            return;
+        }
+    }
+
+    if (tid == 0) {
+        for (int s = 0; s <= p.S; ++s) mbar_init(full + s, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    // weights do not depend on the previous kernel: start streaming them now
+    if (tid == 0) {
+        for (int i = 0; i < p.S; ++i) {
+            const int u = blockIdx.x + i * G;
+            if (u < p.n_units) issue_unit<MODE>(p, u, stages + i * p.stage_bytes, full + i);
+        }
+    }
+    griddep_launch_dependents();
+    griddep_wait();   // the quantized activations come from the previous kernel
+
+    int cur_t = -1;
+    uint32_t aphase = 0;
+    for (int i = 0;; ++i) {
+        const int u = blockIdx.x + i * G;
+        if (u >= p.n_units) break;
+        const int s = i % p.S;
+        const int t = MODE == 1 ? (u / tiles) / p.k : u / tiles;
+        const int r0 = (u % tiles) * p.R;
+        if (t != cur_t) {
+            if (tid == 0) {
+                tma_expect(abar, (uint32_t)(p.a_rows * p.al.pitch));
+                const int arow0 = MODE == 1 ? t : t * p.k;
+                tma_load(act, p.aq + (int64_t)arow0 * p.al.pitch, (uint32_t)(p.a_rows * p.al.pitch), abar);
+            }
+            if (!mbar_wait_limit(abar, aphase)) {
+                if (tid == 0) record_error(GX_DEVERR_TIMEOUT);
+                mbar_wait_limit(abar, aphase);
+                return;
+            }
+            aphase ^= 1u;
+            cur_t = t;
+        }
+        if (!mbar_wait_limit(full + s, (uint32_t)((i / p.S) & 1))) {
+            if (tid == 0) record_error(GX_DEVERR_TIMEOUT);
+            mbar_wait_limit(full + s, (uint32_t)((i / p.S) & 1));
+            return;
+        }
+        const uint8_t * st_base = stages + s * p.stage_bytes;
+        const uint8_t * arow = MODE == 1 ? act : act + (row / p.R) * p.al.pitch;
+        typename Q::St acc;
+#pragma unroll 2
+        for (int v = 0; v < U; ++v) Q::unit(st_base, row * p.pitch_w, arow, p.al, v, l, acc);
+        const float dot = Q::finish(acc);
+        if (l == 0) dots[row] = dot;
+        __syncthreads();
+        // the stage is free: stream the unit S steps ahead into it
+        if (tid == 0) {
+            const int un = u + p.S * G;
+            if (un < p.n_units) issue_unit<MODE>(p, un, stages + s * p.stage_bytes, full + s);
+        }
+        if (MODE == 1) {
+            const int pair = u / tiles;
+            if (tid < p.R) {
+                const float g = dots[tid], up = dots[p.R + tid];
+                const float a = p.act == 1 ? act_swiglu_oai(g, up, p.alpha, p.limit) : act_swiglu(g, up);
+                p.act_f32[(int64_t)pair * p.ne01 + r0 + tid] = a;
+                __threadfence();
+            }
+            __syncthreads();
+            const int nblk = p.ne01 / p.qblk;
+            const int blk = r0 / p.qblk;
+            if (tid == 0) {
+                const int old = atomicAdd(p.counters + pair * nblk + blk, 1);
+                *flag = old == p.qblk / p.R - 1;
+            }
+            __syncthreads();
+            if (*flag && tid < 32) {
+                __threadfence();
+                const float * src = p.act_f32 + (int64_t)pair * p.ne01;
+                uint8_t * dst = p.act_q + (int64_t)pair * p.al2.pitch;
+                if (p.vdt2 == GX_T_Q8_0) quant_block_split<GX_T_Q8_0, true>(src, dst, p.al2, blk, lane);
+                else quant_block_split<GX_T_Q8_K, true>(src, dst, p.al2, blk, lane);
+                if (lane == 0) atomicExch(p.counters + pair * nblk + blk, 0);
+            }
+        } else {
+            if (tid < p.R) {
+                const float * w = p.rw + (int64_t)t * p.k;
+                float accf = __fmul_rn(dots[tid], w[0]);
+                for (int m = 1; m < p.k; ++m) accf = __fadd_rn(accf, __fmul_rn(dots[m * p.R + tid], w[m]));
+                p.out[(int64_t)t * p.ne01 + r0 + tid] = accf;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// f32 rows -> split-layout Q8 rows, one warp per block
+template <int VDT>
+__global__ void k_quant_split(const float * src, int ne0, int64_t nrows, int64_t nb1, uint8_t * dst, ActLayout L) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int nblk = ne0 / (VDT == GX_T_Q8_0 ? 32 : 256);
+    const int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (wid >= nrows * nblk) return;
+    const int64_t r = wid / nblk;
+    const int ib = (int)(wid - r * nblk);
+    const float * x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(src) + r * nb1);
+    quant_block_split<VDT, false>(x, dst + r * L.pitch, L, ib, threadIdx.x & 31);
+}
+
+}  // namespace gx
