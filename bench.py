@@ -175,7 +175,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import galactus_b200 as gx
-    from galactus_b200.moe import StackCall, device_error
+    from galactus_b200.moe import StackCall, StackPlan, device_error
     from galactus_b200.routing import routes
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -286,21 +286,47 @@ def run_ours(args):
         return st_h, st_m
 
     results = {}
-    # ---------------- headline: full residency
+    # fixed per-layer input / weight / output buffers the captured plan reads;
+    # each step copies its token's hidden states and router weights into them
+    x_fix = torch.empty((NL, H), dtype=torch.float32, device=dev)
+    w_fix = torch.empty((NL, k), dtype=torch.float32, device=dev)
+
+    def plan_for(a, timing=False):
+        return StackPlan(a, 0, NL, [x_fix[L].data_ptr() for L in range(NL)], [w_fix[L].data_ptr() for L in range(NL)],
+                         [out_dev[L].data_ptr() for L in range(NL)], k, 1, timing=timing)
+
+    def run_plan(plan, t_first, n, e2e=None):
+        st_h = st_m = 0
+        for i in range(n):
+            t = t_first + i
+            if e2e is None:
+                x_fix.copy_(x_dev[t % P], non_blocking=True)
+                w_fix.copy_(w_dev[t % P], non_blocking=True)
+            else:
+                h_x, h_w, h_out = e2e
+                x_fix.copy_(h_x[t % P], non_blocking=True)
+                w_fix.copy_(h_w[t % P], non_blocking=True)
+            st = plan(ids_c[t], stream)
+            st_h += st.hits
+            st_m += st.misses
+            if e2e is not None:
+                e2e[2][t % P].copy_(out_dev, non_blocking=True)
+        return st_h, st_m
+
+    # ---------------- headline: full residency, captured decode step
     arena = make_arena(1.0)
     with torch.cuda.stream(stream):
         arena.warm_all(stream)
         torch.cuda.synchronize()
-        call = stack_for(arena)
-        tabs = ptr_tables(call)
-        run_steps(call, tabs, 0, args.warmup)
+        plan = plan_for(arena)
+        run_plan(plan, 0, args.warmup)
         torch.cuda.synchronize()
         barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clk:
             torch.cuda.synchronize()
             ev0.record(stream)
-            h, m = run_steps(call, tabs, args.warmup, args.steps)
+            h, m = run_plan(plan, args.warmup, args.steps)
             ev1.record(stream)
             torch.cuda.synchronize()
         ms = ev0.elapsed_time(ev1)
@@ -315,11 +341,11 @@ def run_ours(args):
         h_x = torch.from_numpy(xs).pin_memory()
         h_w = torch.from_numpy(np.ascontiguousarray(w_all[:P])).pin_memory()
         h_out = torch.empty((P, NL, H), dtype=torch.float32).pin_memory()
-        run_steps(call, tabs, 0, args.warmup, e2e=(h_x, h_w, h_out))
+        run_plan(plan, 0, args.warmup, e2e=(h_x, h_w, h_out))
         torch.cuda.synchronize()
         barrier()
         ev0.record(stream)
-        run_steps(call, tabs, args.warmup, args.steps, e2e=(h_x, h_w, h_out))
+        run_plan(plan, args.warmup, args.steps, e2e=(h_x, h_w, h_out))
         ev1.record(stream)
         torch.cuda.synchronize()
         ms_e2e = max_over_ranks(ev0.elapsed_time(ev1))
@@ -327,11 +353,28 @@ def run_ours(args):
         results["e2e"] = {"value": world * args.steps / (ms_e2e / 1e3), "unit": "tok/s",
                           "h2d_bytes_per_step": NL * H * 4 + NL * k * 4, "d2h_bytes_per_step": NL * H * 4}
 
-        # ---------------- per-kernel timing (CUDA events around each launch)
-        arena.timing(True)
+        # ---------------- the same step through the per-layer C-ABI calls (no graph)
+        call = stack_for(arena)
+        tabs = ptr_tables(call)
+        run_steps(call, tabs, 0, args.warmup)
+        torch.cuda.synchronize()
+        ev0.record(stream)
         run_steps(call, tabs, args.warmup, args.steps)
-        gu_ms, dn_ms, calls = arena.timing_read()
-        arena.timing(False)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        results["layer_path_tok_s"] = world * args.steps / (max_over_ranks(ev0.elapsed_time(ev1)) / 1e3)
+
+        # ---------------- per-kernel timing: a graph with events around each kernel
+        tplan = plan_for(arena, timing=True)
+        gu_ms = dn_ms = 0.0
+        calls = 0
+        for i in range(args.steps):
+            run_plan(tplan, args.warmup + i, 1)
+            a_, b_ = tplan.timing()
+            gu_ms += a_
+            dn_ms += b_
+            calls += NL
+        tplan.close()
         err = device_error()
         if err:
             raise RuntimeError(f"device error {err}")
@@ -357,6 +400,7 @@ def run_ours(args):
             pms = max_over_ranks(ev0.elapsed_time(ev1)) / reps
             results["prefill"] = {"tokens": Tp, "tok_s": world * Tp / (pms / 1e3), "ms": pms}
             del px, pwd, pout
+    plan.close()
     arena.close()
 
     # ---------------- residency sweep (misses stream from the host tier)
@@ -364,16 +408,16 @@ def run_ours(args):
     for frac in [float(f) for f in args.sweep.split(",") if f.strip()]:
         a = make_arena(frac)
         with torch.cuda.stream(stream):
-            c = stack_for(a)
-            tb = ptr_tables(c)
-            run_steps(c, tb, 0, args.warmup)
+            sp = plan_for(a)
+            run_plan(sp, 0, args.warmup)
             torch.cuda.synchronize()
             s0 = a.stats()
             ev0.record(stream)
-            hh, mm = run_steps(c, tb, args.warmup, args.sweep_steps)
+            hh, mm = run_plan(sp, args.warmup, args.sweep_steps)
             ev1.record(stream)
             torch.cuda.synchronize()
             s1 = a.stats()
+            sp.close()
         sms = max_over_ranks(ev0.elapsed_time(ev1))
         moved = s1["bytes_h2d"] - s0["bytes_h2d"]
         sweep.append({"fraction": frac, "slots_per_layer": a.quota(0)[0], "tok_s": world * args.sweep_steps / (sms / 1e3),
@@ -389,9 +433,9 @@ def run_ours(args):
     dn_bytes = k * H * rb_i + k * I * 4 + k * 4 + H * 4
     gu_avg, dn_avg = gu_ms / max(1, calls), dn_ms / max(1, calls)
     if gu_ms >= dn_ms:
-        dom, dbytes, dms = "k_rows<GATE_UP> (fused gate/up/SwiGLU)", gu_bytes, gu_avg
+        dom, dbytes, dms = "k_decode<GATE_UP> (fused gate/up/activation)", gu_bytes, gu_avg
     else:
-        dom, dbytes, dms = "k_rows<DOWN_COMBINE> (fused down/combine)", dn_bytes, dn_avg
+        dom, dbytes, dms = "k_decode<DOWN> (fused down/combine)", dn_bytes, dn_avg
     achieved = dbytes / (dms / 1e3) / 1e9
     traffic = None
     tp = ROOT / "profiles" / "traffic.json"
@@ -410,7 +454,8 @@ def run_ours(args):
                    "l2": f"inputs larger than L2: ~{NL * k * model.record_raw / 1e9:.2f} GB of expert weights read "
                          f"per step vs 126 MB L2, no flush"},
         "e2e": results["e2e"],
-        "gpu_launches": 2 * NL * args.steps,
+        "gpu_launches": 3 * NL * args.steps,
+        "layer_path_tok_s": results["layer_path_tok_s"],
         "hit_rate": results["hit_rate"],
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,

@@ -70,7 +70,8 @@ int serve_policy(SlotPolicy & P, uint32_t layer, const int32_t * experts, uint32
     if (layer < P.first_layer() || layer > P.last_layer()) return GX_ERR_INVALID;
     for (uint32_t i = 0; i < count; ++i)
         if (experts[i] < 0 || (uint32_t)experts[i] >= P.experts()) return GX_ERR_DOMAIN;
-    std::vector<uint8_t> seen(P.experts(), 0);
+    thread_local std::vector<uint8_t> seen;
+    seen.assign(P.experts(), 0);
     uint32_t distinct = 0;
     for (uint32_t i = 0; i < count; ++i)
         if (!seen[experts[i]]) { seen[experts[i]] = 1; ++distinct; }
@@ -117,6 +118,8 @@ struct gx_arena {
     uint64_t tier_bytes = 0;
     cudaStream_t copy_stream = nullptr;
     std::vector<cudaEvent_t> ev_done, ev_copy;
+    std::vector<cudaEvent_t> last_ev;   // last event after which nothing reads a layer's slab
+    std::vector<int32_t> slot_scratch;  // slot ids of one micro-batch
     cudaEvent_t ev_snapshot = nullptr;
     // layer entry point scratch
     int64_t max_tokens = 0, hidden = 0, intermediate = 0;
@@ -300,6 +303,8 @@ int gx_arena_create(const gx_arena_config * c, gx_arena ** out) {
             ck(cudaEventCreateWithFlags(&a->ev_copy[i], cudaEventDisableTiming));
         }
         ck(cudaEventCreateWithFlags(&a->ev_snapshot, cudaEventDisableTiming));
+        a->last_ev = a->ev_done;
+        a->slot_scratch.resize((size_t)std::max<int64_t>(1, (int64_t)c->profile.used * std::max<int64_t>(1, c->max_tokens)));
         a->max_tokens = c->max_tokens;
         a->used = c->profile.used;
         a->hidden = c->hidden;
@@ -402,7 +407,8 @@ namespace {
 // slots) and `consumer` waits for them.
 int arena_serve(gx_arena * a, uint32_t layer, const int32_t * experts, uint32_t count, int32_t * slots,
                 cudaEvent_t after, cudaStream_t consumer, gx_serve_stats * st_out) {
-    std::vector<std::pair<int32_t, int32_t>> misses;
+    thread_local std::vector<std::pair<int32_t, int32_t>> misses;
+    misses.clear();
     gx_serve_stats st{};
     const int rc = serve_policy(a->policy->impl, layer, experts, count, slots, nullptr, nullptr, &misses, &st);
     if (rc != GX_OK) return rc;
@@ -595,9 +601,212 @@ int gx_expf(const float * x, float * y, int64_t n, void * stream) {
 
 // --------------------------------------------------------------- MoE layer
 
-static int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x,
-                                const int32_t * ids, const float * w, int64_t k, int64_t T, float * out,
-                                cudaStream_t s, gx_serve_stats * stats);
+}  // extern "C"
+
+namespace {
+
+// Launch configuration of one routed-expert layer: everything the three
+// kernels need except the per-call pointers and slot ids.
+struct LayerPlan {
+    uint32_t layer = 0, li = 0;
+    int64_t H = 0, I = 0, k = 0, T = 0;
+    int vdt_g = 0, vdt_d = 0;
+    int type_gate = 0, type_down = 0;
+    gx::DecodeParams g{}, dn{};
+};
+
+int plan_layer(gx_arena * a, uint32_t layer, const gx_layer_desc * d, int64_t k, int64_t T, LayerPlan & lp) {
+    if (d == nullptr) return GX_ERR_INVALID;
+    if (!gx::supported_weight_type(d->type_gate) || !gx::supported_weight_type(d->type_down)) return GX_ERR_TYPE;
+    if (d->type_up != d->type_gate) return GX_ERR_TYPE;
+    if (d->act != GX_ACT_SWIGLU && d->act != GX_ACT_SWIGLU_OAI) return GX_ERR_INVALID;
+    if (T < 1 || k <= 0 || T > a->max_tokens || d->hidden != a->hidden || d->intermediate != a->intermediate)
+        return GX_ERR_INVALID;
+    if (k > (int64_t)a->used || k * T > 65535) return GX_ERR_INVALID;
+    const int64_t H = d->hidden, I = d->intermediate;
+    if (H % gx::row_align(d->type_gate) != 0 || I % gx::row_align(d->type_down) != 0) return GX_ERR_ALIGN;
+    if (d->off_gate % 16 || d->off_up % 16) return GX_ERR_ALIGN;
+    const SlotPolicy & P = a->policy->impl;
+    if (layer < P.first_layer() || layer > P.last_layer()) return GX_ERR_INVALID;
+    const uint32_t li = a->L(layer);
+    if (d->off_up + gx::row_bytes(d->type_up, H) * I > a->record_raw[li] ||
+        (uint64_t)gx::row_bytes(d->type_down, I) * H > d->off_gate)
+        return GX_ERR_INVALID;
+    lp.layer = layer;
+    lp.li = li;
+    lp.H = H;
+    lp.I = I;
+    lp.k = k;
+    lp.T = T;
+    lp.type_gate = d->type_gate;
+    lp.type_down = d->type_down;
+    lp.vdt_g = gx::vec_dot_type(d->type_gate);
+    lp.vdt_d = gx::vec_dot_type(d->type_down);
+    uint8_t * base = a->d_arena + a->slab_base[li];
+    const int64_t n = k * T;
+
+    gx::DecodeParams & g = lp.g;
+    g = gx::DecodeParams{};
+    g.w0 = base + d->off_gate;
+    g.w1 = base + d->off_up;
+    g.nb01 = gx::row_bytes(d->type_gate, H);
+    g.nb02 = (int64_t)a->record[li];
+    g.ne00 = (int32_t)H;
+    g.ne01 = (int32_t)I;
+    g.n_as = (int32_t)P.quota_of(layer);
+    g.k = (int32_t)k;
+    g.T = (int32_t)T;
+    g.aq = a->d_xq;
+    g.al = gx::act_layout(lp.vdt_g, (int)H);
+    g.a_rows = 1;
+    g.act_f32 = a->d_act;
+    g.act_q = a->d_actq;
+    g.al2 = gx::act_layout(lp.vdt_d, (int)I);
+    g.vdt2 = lp.vdt_d;
+    g.qblk = lp.vdt_d == gx::GX_T_Q8_0 ? 32 : 256;
+    g.counters = a->d_cnt;
+    g.act = d->act;
+    g.alpha = d->alpha;
+    g.limit = d->limit;
+    {
+        static const int cands[] = {8, 16, 4, 2, 1};
+        int threads = 0;
+        g.R = 0;
+        for (int R : cands) {
+            if (I % R || g.qblk % R) continue;
+            gx::DecodeParams t = g;
+            t.R = R;
+            if (gx::decode_layout(1, t, threads) == 0) continue;
+            g.R = R;
+            break;
+        }
+        if (g.R == 0) return GX_ERR_ALIGN;
+        g.n_units = (int32_t)(n * (I / g.R));
+    }
+
+    gx::DecodeParams & dn = lp.dn;
+    dn = g;
+    dn.w0 = base;
+    dn.w1 = nullptr;
+    dn.nb01 = gx::row_bytes(d->type_down, I);
+    dn.ne00 = (int32_t)I;
+    dn.ne01 = (int32_t)H;
+    dn.aq = a->d_actq;
+    dn.al = gx::act_layout(lp.vdt_d, (int)I);
+    dn.a_rows = (int32_t)k;
+    {
+        // 16 rows per stage (128 threads) when the tile keeps 16-byte alignment,
+        // else larger or smaller tiles
+        const int base_r = (int)(16 / k) > 0 ? (int)(16 / k) : 1;
+        const int cands[] = {base_r, 2 * base_r, base_r / 2, base_r / 4, 1};
+        int threads = 0;
+        dn.R = 0;
+        for (int R : cands) {
+            if (R < 1 || H % R) continue;
+            gx::DecodeParams t = dn;
+            t.R = R;
+            if (gx::decode_layout(2, t, threads) == 0) continue;
+            dn.R = R;
+            break;
+        }
+        if (dn.R == 0) return GX_ERR_ALIGN;
+        dn.n_units = (int32_t)(T * (H / dn.R));
+    }
+    return GX_OK;
+}
+
+// Enqueue the three kernels of a planned layer. Slot ids come either inline
+// (n <= kInlineIds) or from a device array [T, k].
+void enqueue_layer(const LayerPlan & lp, const float * x, const float * w, float * out, const int32_t * ids_dev,
+                   const int32_t * inline_slots, cudaStream_t s, bool pdl_first, bool pdl, cudaEvent_t tv[3]) {
+    gx::DecodeParams g = lp.g, dn = lp.dn;
+    const int64_t n = lp.k * lp.T;
+    if (ids_dev == nullptr) {
+        g.use_inline = dn.use_inline = 1;
+        for (int64_t j = 0; j < n; ++j) g.inline_ids[j] = dn.inline_ids[j] = inline_slots[j];
+    } else {
+        g.use_inline = dn.use_inline = 0;
+        g.ids = dn.ids = ids_dev;
+    }
+    dn.rw = w;
+    dn.out = out;
+    ck(gx::launch_quant_split(lp.vdt_g, x, (int)lp.H, lp.T, lp.H * 4, const_cast<uint8_t *>(g.aq), s, pdl_first));
+    // external records: inside a stream capture they become event nodes of the graph
+    if (tv && tv[0]) ck(cudaEventRecordWithFlags(tv[0], s, cudaEventRecordExternal));
+    ck(gx::launch_decode(lp.type_gate, 1, g, s, pdl));
+    if (tv && tv[1]) ck(cudaEventRecordWithFlags(tv[1], s, cudaEventRecordExternal));
+    ck(gx::launch_decode(lp.type_down, 2, dn, s, pdl));
+    if (tv && tv[2]) ck(cudaEventRecordWithFlags(tv[2], s, cudaEventRecordExternal));
+}
+
+int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x, const int32_t * ids,
+                         const float * w, int64_t k, int64_t T, float * out, cudaStream_t s, gx_serve_stats * stats) {
+    if (x == nullptr || ids == nullptr || w == nullptr || out == nullptr) return GX_ERR_INVALID;
+    if (T == 0) return GX_OK;
+    LayerPlan lp;
+    int rc = plan_layer(a, layer, d, k, T, lp);
+    if (rc != GX_OK) return rc;
+    const int64_t n = k * T;
+    int32_t * slots = a->slot_scratch.data();
+    gx_serve_stats sst{};
+    rc = arena_serve(a, layer, ids, (uint32_t)n, slots, a->last_ev[lp.li], s, &sst);
+    if (rc != GX_OK) return rc;
+    if (stats) *stats = sst;
+
+    const int32_t * ids_dev = nullptr;
+    if (n > gx::kInlineIds) {
+        // stage the slot ids through a pinned ring; a ring entry is reused
+        // only after the copy that read it has run
+        const int st = a->stage_next;
+        a->stage_next = (st + 1) % kStageRing;
+        const int64_t stride = (int64_t)a->used * a->max_tokens;
+        ck(cudaEventSynchronize(a->ev_stage[st]));
+        int32_t * h = a->h_ids + (size_t)st * stride;
+        int32_t * dd = a->d_ids + (size_t)st * stride;
+        std::memcpy(h, slots, (size_t)n * sizeof(int32_t));
+        ck(cudaMemcpyAsync(dd, h, (size_t)n * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+        ck(cudaEventRecord(a->ev_stage[st], s));
+        ids_dev = dd;
+    }
+    cudaEvent_t tv[3] = {nullptr, nullptr, nullptr};
+    if (a->timing) {
+        while (a->tev.size() < a->tev_used + 3) {
+            cudaEvent_t e;
+            ck(cudaEventCreate(&e));
+            a->tev.push_back(e);
+        }
+        for (int j = 0; j < 3; ++j) tv[j] = a->tev[a->tev_used + j];
+        a->tev_used += 3;
+    }
+    // programmatic overlap between the kernels, except right after a miss
+    // copy wait or while timing the kernels one by one
+    const bool pdl = !a->timing;
+    enqueue_layer(lp, x, w, out, ids_dev, slots, s, pdl && sst.misses == 0 && ids_dev == nullptr, pdl, tv);
+    ck(cudaEventRecord(a->ev_done[lp.li], s));
+    a->last_ev[lp.li] = a->ev_done[lp.li];
+    return GX_OK;
+}
+
+}  // namespace
+
+struct gx_stack_plan {
+    gx_arena * a = nullptr;
+    uint32_t first = 0, n = 0;
+    int64_t k = 0, T = 0;
+    gx_layer_desc desc{};
+    std::vector<LayerPlan> lps;
+    int32_t * d_slots = nullptr;
+    int32_t * h_slots[2] = {nullptr, nullptr};
+    cudaEvent_t ev_h[2] = {nullptr, nullptr};
+    int cur = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaEvent_t ev_graph = nullptr;
+    int timing = 0;
+    std::vector<cudaEvent_t> tev;
+};
+
+extern "C" {
 
 int gx_moe_layer_forward(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x, const int32_t * ids,
                          const float * w, int64_t k, int64_t T, float * out, void * stream, gx_serve_stats * stats) {
@@ -633,156 +842,135 @@ int gx_moe_stack_forward(gx_arena * a, uint32_t first_layer, uint32_t n_layers, 
     });
 }
 
-static int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x,
-                                const int32_t * ids, const float * w, int64_t k, int64_t T, float * out,
-                                cudaStream_t s, gx_serve_stats * stats) {
-    if (a == nullptr || d == nullptr || x == nullptr || ids == nullptr || w == nullptr || out == nullptr) return GX_ERR_INVALID;
-    if (!gx::supported_weight_type(d->type_gate) || !gx::supported_weight_type(d->type_down)) return GX_ERR_TYPE;
-    if (d->type_up != d->type_gate) return GX_ERR_TYPE;
-    if (d->act != GX_ACT_SWIGLU && d->act != GX_ACT_SWIGLU_OAI) return GX_ERR_INVALID;
-    if (T < 0 || k <= 0 || T > a->max_tokens || d->hidden != a->hidden || d->intermediate != a->intermediate)
+int gx_stack_plan_destroy(gx_stack_plan * p) {
+    if (p == nullptr) return GX_OK;
+    if (p->a) cudaSetDevice(p->a->device);
+    if (p->ev_graph) cudaEventSynchronize(p->ev_graph);
+    if (p->exec) cudaGraphExecDestroy(p->exec);
+    if (p->graph) cudaGraphDestroy(p->graph);
+    for (auto e : p->tev) if (e) cudaEventDestroy(e);
+    for (auto e : p->ev_h) if (e) cudaEventDestroy(e);
+    if (p->ev_graph) cudaEventDestroy(p->ev_graph);
+    if (p->d_slots) cudaFree(p->d_slots);
+    for (auto h : p->h_slots) if (h) cudaFreeHost(h);
+    delete p;
+    return GX_OK;
+}
+
+int gx_stack_plan_create(gx_arena * a, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * d,
+                         const float * const * x, const float * const * w, float * const * out, int64_t k, int64_t T,
+                         int timing, gx_stack_plan ** out_plan) {
+    if (a == nullptr || d == nullptr || x == nullptr || w == nullptr || out == nullptr || out_plan == nullptr ||
+        n_layers == 0)
         return GX_ERR_INVALID;
-    if (k > (int64_t)a->used) return GX_ERR_INVALID;
-    const int64_t H = d->hidden, I = d->intermediate;
-    if (H % gx::row_align(d->type_gate) != 0 || I % gx::row_align(d->type_down) != 0) return GX_ERR_ALIGN;
-    if (d->off_gate % 16 || d->off_up % 16) return GX_ERR_ALIGN;
-    if (T == 0) return GX_OK;
-    {
-        const SlotPolicy & P = a->policy->impl;
-        if (layer < P.first_layer() || layer > P.last_layer()) return GX_ERR_INVALID;
-        const uint32_t li = a->L(layer);
-        if (d->off_up + gx::row_bytes(d->type_up, H) * I > a->record_raw[li] ||
-            (uint64_t)gx::row_bytes(d->type_down, I) * H > d->off_gate)
-            return GX_ERR_INVALID;
-        const int64_t n = k * T;
-        std::vector<int32_t> slots((size_t)n);
-        gx_serve_stats sst{};
-        int rc = arena_serve(a, layer, ids, (uint32_t)n, slots.data(), a->ev_done[li], s, &sst);
-        if (rc != GX_OK) return rc;
-        if (stats) *stats = sst;
-        const uint32_t last_misses = sst.misses;
-
-        uint8_t * base = a->d_arena + a->slab_base[li];
-        gx::RowsParams p{};
-        p.k = (int32_t)k;
-        p.T = (int32_t)T;
-        p.n_as = (int32_t)P.quota_of(layer);
-        p.nb02 = (int64_t)a->record[li];
-        if (n <= gx::kInlineIds) {
-            p.use_inline = 1;
-            for (int64_t j = 0; j < n; ++j) p.inline_ids[j] = slots[(size_t)j];
-        } else {
-            // stage the slot ids through a pinned ring; a ring entry is reused
-            // only after the copy that read it has run
-            const int st = a->stage_next;
-            a->stage_next = (st + 1) % kStageRing;
-            const int64_t stride = (int64_t)a->used * a->max_tokens;
-            if (n > stride) return GX_ERR_INVALID;
-            ck(cudaEventSynchronize(a->ev_stage[st]));
-            int32_t * h = a->h_ids + (size_t)st * stride;
-            int32_t * dd = a->d_ids + (size_t)st * stride;
-            std::memcpy(h, slots.data(), (size_t)n * sizeof(int32_t));
-            ck(cudaMemcpyAsync(dd, h, (size_t)n * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-            ck(cudaEventRecord(a->ev_stage[st], s));
-            p.ids = dd;
-            p.nbi1 = k * 4;
+    *out_plan = nullptr;
+    gx_stack_plan * p = new (std::nothrow) gx_stack_plan();
+    if (p == nullptr) return GX_ERR_NOMEM;
+    const int rc = guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        ck(cudaSetDevice(a->device));
+        p->a = a;
+        p->first = first_layer;
+        p->n = n_layers;
+        p->k = k;
+        p->T = T;
+        p->desc = *d;
+        p->timing = timing;
+        p->lps.resize(n_layers);
+        for (uint32_t i = 0; i < n_layers; ++i) {
+            const int r = plan_layer(a, first_layer + i, d, k, T, p->lps[i]);
+            if (r != GX_OK) return r;
         }
-
-        cudaEvent_t tv[3] = {nullptr, nullptr, nullptr};
-        if (a->timing) {
-            while (a->tev.size() < a->tev_used + 3) {
-                cudaEvent_t e;
-                ck(cudaEventCreate(&e));
-                a->tev.push_back(e);
-            }
-            for (int j = 0; j < 3; ++j) tv[j] = a->tev[a->tev_used + j];
-            a->tev_used += 3;
+        const size_t bytes = (size_t)n_layers * k * T * sizeof(int32_t);
+        ck(cudaMalloc(&p->d_slots, bytes));
+        ck(cudaMemset(p->d_slots, 0, bytes));
+        for (int j = 0; j < 2; ++j) {
+            ck(cudaHostAlloc(&p->h_slots[j], bytes, cudaHostAllocDefault));
+            ck(cudaEventCreateWithFlags(&p->ev_h[j], cudaEventDisableTiming));
         }
-
-        const int vdt_g = gx::vec_dot_type(d->type_gate), vdt_d = gx::vec_dot_type(d->type_down);
-        // without misses nothing but kernels precede: let each kernel start
-        // streaming its weights while the previous one finishes
-        // (kernel timing measures each kernel alone, without the overlap)
-        const bool pdl = !a->timing;
-        const bool had_misses = last_misses > 0;
-        ck(gx::launch_quant_split(vdt_g, x, (int)H, T, H * 4, a->d_xq, s, pdl && !had_misses));
-        if (tv[0]) ck(cudaEventRecord(tv[0], s));
-
-        // gate + up + activation -> quantized down input
-        gx::DecodeParams g{};
-        g.w0 = base + d->off_gate;
-        g.w1 = base + d->off_up;
-        g.nb01 = gx::row_bytes(d->type_gate, H);
-        g.nb02 = (int64_t)a->record[li];
-        g.ne00 = (int32_t)H;
-        g.ne01 = (int32_t)I;
-        g.n_as = p.n_as;
-        g.k = p.k;
-        g.T = p.T;
-        g.ids = p.ids;
-        g.use_inline = p.use_inline;
-        std::memcpy(g.inline_ids, p.inline_ids, sizeof(g.inline_ids));
-        g.aq = a->d_xq;
-        g.al = gx::act_layout(vdt_g, (int)H);
-        g.a_rows = 1;
-        g.act_f32 = a->d_act;
-        g.act_q = a->d_actq;
-        g.al2 = gx::act_layout(vdt_d, (int)I);
-        g.vdt2 = vdt_d;
-        g.qblk = vdt_d == gx::GX_T_Q8_0 ? 32 : 256;
-        g.counters = a->d_cnt;
-        g.act = d->act;
-        g.alpha = d->alpha;
-        g.limit = d->limit;
-        {
-            static const int cands[] = {8, 16, 4, 2};
-            int threads = 0;
-            g.R = 0;
-            for (int R : cands) {
-                if (I % R || g.qblk % R) continue;
-                gx::DecodeParams t = g;
-                t.R = R;
-                if (gx::decode_layout(1, t, threads) == 0) continue;
-                g.R = R;
-                break;
-            }
-            if (g.R == 0) return GX_ERR_ALIGN;
-            g.n_units = (int32_t)(n * (I / g.R));
+        ck(cudaEventCreateWithFlags(&p->ev_graph, cudaEventDisableTiming));
+        if (timing) {
+            p->tev.resize((size_t)3 * n_layers);
+            for (auto & e : p->tev) ck(cudaEventCreate(&e));
         }
-        ck(gx::launch_decode(d->type_gate, 1, g, s, pdl));
-        if (tv[1]) ck(cudaEventRecord(tv[1], s));
-
-        // down + weighted combine in slot order -> out [H, T]
-        gx::DecodeParams dn = g;
-        dn.w0 = base;
-        dn.w1 = nullptr;
-        dn.nb01 = gx::row_bytes(d->type_down, I);
-        dn.ne00 = (int32_t)I;
-        dn.ne01 = (int32_t)H;
-        dn.aq = a->d_actq;
-        dn.al = gx::act_layout(vdt_d, (int)I);
-        dn.a_rows = (int32_t)k;
-        dn.rw = w;
-        dn.out = out;
-        {
-            int threads = 0;
-            dn.R = 0;
-            for (int R = (int)(32 / k); R >= 1; R /= 2) {
-                if (R < 1 || H % R) continue;
-                gx::DecodeParams t = dn;
-                t.R = R;
-                if (gx::decode_layout(2, t, threads) == 0) continue;
-                dn.R = R;
-                break;
-            }
-            if (dn.R == 0) return GX_ERR_ALIGN;
-            dn.n_units = (int32_t)(T * (H / dn.R));
+        // warm every kernel configuration (attributes, occupancy) outside the capture
+        cudaStream_t cap;
+        ck(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+        for (uint32_t i = 0; i < n_layers; ++i) {
+            ck(gx::prepare_decode(p->lps[i].type_gate, 1, p->lps[i].g));
+            ck(gx::prepare_decode(p->lps[i].type_down, 2, p->lps[i].dn));
         }
-        ck(gx::launch_decode(d->type_down, 2, dn, s, pdl));
-        if (tv[2]) ck(cudaEventRecord(tv[2], s));
-        ck(cudaEventRecord(a->ev_done[li], s));
+        ck(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));
+        for (uint32_t i = 0; i < n_layers; ++i) {
+            cudaEvent_t * tv = timing ? &p->tev[(size_t)3 * i] : nullptr;
+            enqueue_layer(p->lps[i], x[i], w[i], out[i], p->d_slots + (size_t)i * k * T, nullptr, cap, !timing, !timing, tv);
+        }
+        cudaGraph_t graph = nullptr;
+        const cudaError_t ce = cudaStreamEndCapture(cap, &graph);
+        cudaStreamDestroy(cap);
+        ck(ce);
+        p->graph = graph;
+        ck(cudaGraphInstantiate(&p->exec, p->graph, 0));
         return GX_OK;
+    });
+    if (rc != GX_OK) {
+        gx_stack_plan_destroy(p);
+        return rc;
     }
+    *out_plan = p;
+    return GX_OK;
+}
+
+int gx_stack_plan_run(gx_stack_plan * p, const int32_t * ids, void * stream, gx_serve_stats * stats) {
+    if (p == nullptr || ids == nullptr) return GX_ERR_INVALID;
+    gx_arena * a = p->a;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        ck(cudaSetDevice(a->device));
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        const int64_t per = p->k * p->T;
+        int32_t * h = p->h_slots[p->cur];
+        ck(cudaEventSynchronize(p->ev_h[p->cur]));     // the previous copy out of this buffer has run
+        gx_serve_stats sum{};
+        for (uint32_t i = 0; i < p->n; ++i) {
+            gx_serve_stats st{};
+            const uint32_t li = p->lps[i].li;
+            const int rc = arena_serve(a, p->first + i, ids + (size_t)i * per, (uint32_t)per, h + (size_t)i * per,
+                                       a->last_ev[li], s, &st);
+            if (rc != GX_OK) return rc;
+            sum.hits += st.hits;
+            sum.misses += st.misses;
+            sum.evictions += st.evictions;
+            sum.distinct += st.distinct;
+            sum.bytes_copied += st.bytes_copied;
+        }
+        ck(cudaMemcpyAsync(p->d_slots, h, (size_t)p->n * per * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+        ck(cudaEventRecord(p->ev_h[p->cur], s));
+        p->cur ^= 1;
+        ck(cudaGraphLaunch(p->exec, s));
+        ck(cudaEventRecord(p->ev_graph, s));
+        for (uint32_t i = 0; i < p->n; ++i) a->last_ev[p->lps[i].li] = p->ev_graph;
+        if (stats) *stats = sum;
+        return GX_OK;
+    });
+}
+
+int gx_stack_plan_timing(gx_stack_plan * p, double * gate_up_ms, double * down_ms) {
+    if (p == nullptr || !p->timing) return GX_ERR_STATE;
+    return guarded([&] {
+        ck(cudaEventSynchronize(p->ev_graph));
+        double gu = 0.0, dn = 0.0;
+        for (uint32_t i = 0; i < p->n; ++i) {
+            float m1 = 0.f, m2 = 0.f;
+            ck(cudaEventElapsedTime(&m1, p->tev[3 * i], p->tev[3 * i + 1]));
+            ck(cudaEventElapsedTime(&m2, p->tev[3 * i + 1], p->tev[3 * i + 2]));
+            gu += m1;
+            dn += m2;
+        }
+        if (gate_up_ms) *gate_up_ms = gu;
+        if (down_ms) *down_ms = dn;
+        return GX_OK;
+    });
 }
 
 // --------------------------------------------------------------- synthetic

@@ -14,6 +14,8 @@
 //   DOWN_COMBINE  the k down tiles of one token, then the weighted sum in slot order
 #include <cstdint>
 #include <cstdio>
+#include <map>
+#include <mutex>
 #include <cuda_runtime.h>
 
 #include "gx_device.cuh"
@@ -482,24 +484,55 @@ cudaError_t launch_synth_weights(int type, void * dst, int64_t ne00, int64_t n_r
 
 // ------------------------------------------------------- decode launchers
 
-template <int TYPE, int MODE>
-static cudaError_t launch_decode_t(DecodeParams & p, int threads, uint32_t smem, cudaStream_t stream, bool pdl) {
-    static int configured = 0;
-    if ((int)smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(k_decode<TYPE, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        configured = (int)smem;
+static int device_sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+        cached[dev] = sms;
     }
-    int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode<TYPE, MODE>, threads, smem);
+    return cached[dev];
+}
+
+// Resident CTAs per SM of one kernel configuration, computed once (the
+// occupancy query and the shared-memory attribute stay off the launch path).
+template <typename K>
+static cudaError_t resident_per_sm(K kernel, int threads, uint32_t smem, int & per_sm) {
+    // keyed by the kernel's address: every instantiation has its own
+    // shared-memory attribute and occupancy
+    static std::mutex mu;
+    static std::map<std::pair<const void *, uint64_t>, int> cache;
+    static std::map<const void *, int> configured;
+    const void * fn = reinterpret_cast<const void *>(kernel);
+    const auto key = std::make_pair(fn, ((uint64_t)threads << 32) | smem);
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        per_sm = it->second;
+        return cudaSuccess;
+    }
+    int & conf = configured[fn];
+    if ((int)smem > conf) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        conf = (int)smem;
+    }
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    int sms = 148;
-    {
-        int dev = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    }
-    const int grid = p.n_units < per_sm * sms ? p.n_units : per_sm * sms;
+    cache[key] = per_sm;
+    return cudaSuccess;
+}
+
+template <int TYPE, int MODE>
+static cudaError_t launch_decode_t(DecodeParams & p, int threads, uint32_t smem, cudaStream_t stream, bool pdl) {
+    int per_sm = 0;
+    cudaError_t e = resident_per_sm(k_decode<TYPE, MODE>, threads, smem, per_sm);
+    if (e != cudaSuccess) return e;
+    const int cap = per_sm * device_sm_count();
+    const int grid = p.n_units < cap ? p.n_units : cap;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3((unsigned)threads);
@@ -510,15 +543,14 @@ static cudaError_t launch_decode_t(DecodeParams & p, int threads, uint32_t smem,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, k_decode<TYPE, MODE>, p);
-    return e;
+    return cudaLaunchKernelEx(&cfg, k_decode<TYPE, MODE>, p);
 }
 
 // Shared-memory layout and tiling of a decode launch; 0 when it cannot fit.
 uint32_t decode_layout(int mode, DecodeParams & p, int & threads) {
     const int nexp = mode == 1 ? 2 : p.k;
-    threads = 4 * nexp * p.R;
-    if (threads > 128 || threads < 32 || threads % 32 != 0) return 0;
+    threads = 8 * nexp * p.R;
+    if (threads > kDecodeMaxThreads || threads < 32 || threads % 32 != 0) return 0;
     if (p.nb01 % 16 == 0) {
         p.row_copy = 1;
         p.pitch_w = (int32_t)(p.nb01 % 128 == 0 ? p.nb01 + 16 : p.nb01);
@@ -530,7 +562,7 @@ uint32_t decode_layout(int mode, DecodeParams & p, int & threads) {
     p.stage_bytes = (int32_t)align_up((uint64_t)nexp * p.R * p.pitch_w + 16, 128);
     const uint32_t act_bytes = align_up((uint64_t)p.a_rows * p.al.pitch + 16, 128);
     const uint32_t fixed = 128 + act_bytes + 128 + 128;
-    const uint32_t budget = 110 * 1024;
+    const uint32_t budget = 72 * 1024;   // three CTAs per SM
     int S = (int)((budget > fixed ? budget - fixed : 0) / (uint32_t)p.stage_bytes);
     if (S > 4) S = 4;
     if (S < 2) S = 2;
@@ -538,7 +570,7 @@ uint32_t decode_layout(int mode, DecodeParams & p, int & threads) {
     p.act_off = 128;
     p.stage_off = p.act_off + act_bytes;
     p.dots_off = p.stage_off + (uint32_t)S * p.stage_bytes;
-    p.flag_off = p.dots_off + 128 * 4;
+    p.flag_off = p.dots_off + (uint32_t)kDecodeMaxThreads / 8 * 4;
     const uint32_t total = p.flag_off + 128;
     if (total > kMaxSmem) return 0;
     return total;
@@ -554,6 +586,26 @@ static cudaError_t launch_decode_mode(int type, DecodeParams & p, int threads, u
         case GX_T_IQ1_S: return launch_decode_t<GX_T_IQ1_S, MODE>(p, threads, smem, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
+}
+
+template <int MODE>
+static cudaError_t prepare_decode_mode(int type, int threads, uint32_t smem) {
+    int per_sm = 0;
+    switch (type) {
+        case GX_T_Q8_0: return resident_per_sm(k_decode<GX_T_Q8_0, MODE>, threads, smem, per_sm);
+        case GX_T_MXFP4: return resident_per_sm(k_decode<GX_T_MXFP4, MODE>, threads, smem, per_sm);
+        case GX_T_Q4_K: return resident_per_sm(k_decode<GX_T_Q4_K, MODE>, threads, smem, per_sm);
+        case GX_T_Q6_K: return resident_per_sm(k_decode<GX_T_Q6_K, MODE>, threads, smem, per_sm);
+        case GX_T_IQ1_S: return resident_per_sm(k_decode<GX_T_IQ1_S, MODE>, threads, smem, per_sm);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t prepare_decode(int type, int mode, DecodeParams p) {
+    int threads = 0;
+    const uint32_t smem = decode_layout(mode, p, threads);
+    if (smem == 0) return cudaErrorInvalidConfiguration;
+    return mode == 1 ? prepare_decode_mode<1>(type, threads, smem) : prepare_decode_mode<2>(type, threads, smem);
 }
 
 cudaError_t launch_decode(int type, int mode, DecodeParams & p, cudaStream_t stream, bool pdl) {

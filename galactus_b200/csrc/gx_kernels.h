@@ -11,6 +11,7 @@ namespace gx {
 constexpr int kRowsThreads = 128;
 constexpr uint32_t kMaxSmem = 227 * 1024;
 constexpr int kInlineIds = 64;
+constexpr int kDecodeMaxThreads = 256;
 
 // Parameters of the row-tile kernel (all three modes). Byte offsets of the
 // shared-memory regions are filled by rows_smem_layout().
@@ -98,6 +99,7 @@ struct DecodeParams {
 
 uint32_t decode_layout(int mode, DecodeParams & p, int & threads);
 cudaError_t launch_decode(int type, int mode, DecodeParams & p, cudaStream_t stream, bool pdl);
+cudaError_t prepare_decode(int type, int mode, DecodeParams p);
 cudaError_t launch_quant_split(int vdt, const float * src, int ne0, int64_t nrows, int64_t nb1, uint8_t * dst,
                                cudaStream_t stream, bool pdl);
 

@@ -6,12 +6,12 @@
 // sums), so the dot loops read them with aligned 32-bit loads. The values are
 // exactly those of ggml's Q8_0 / Q8_K blocks; only the byte layout differs.
 //
-// A weight row is processed by a quad of lanes: lane l owns one quarter of
-// every 64- or 256-element unit. Integer partial sums are exact, so the quad
-// adds them with shuffles in any order; the float tail is then evaluated in
-// the reference's order (diff:1049-1054, 1167-1174, 1254-1259, 1366-1370,
-// 335-345) in registers, identically in the four lanes (or, for Q8_0, one
-// accumulator chain per lane, reduced by the NEON faddp tree).
+// A weight row is processed by eight lanes: lane o owns one eighth of every
+// 64- or 256-element unit. Integer partial sums are exact, so the lanes add
+// them with shuffles in any order; the float tail is then evaluated in the
+// reference's order (diff:1049-1054, 1167-1174, 1254-1259, 1366-1370,
+// 335-345) in registers, identically in the eight lanes (or, for Q8_0, as the
+// NEON loop's per-lane accumulator chains, reduced by its faddp trees).
 #pragma once
 
 #include <cstdint>
@@ -77,7 +77,18 @@ __device__ __forceinline__ void quant_block_split(const float * x, uint8_t * row
     }
 }
 
-// ----------------------------------------------------------- quad dots
+// ---------------------------------------------------------- octet dots
+//
+// Eight lanes per weight row; lane o owns one eighth of every unit (one
+// 32-element block of a Q8_0/MXFP4 pair split in quarters, or one 32-element
+// sub-block of a 256-element superblock).
+
+__device__ __forceinline__ int oct_sum(int v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    return v;
+}
 
 __device__ __forceinline__ int quad_sum(int v) {
     v += __shfl_xor_sync(0xffffffffu, v, 1);
@@ -85,184 +96,164 @@ __device__ __forceinline__ int quad_sum(int v) {
     return v;
 }
 
-template <int TYPE> struct Quad;
+// 16-bit value at an even byte offset of a shared-memory buffer whose base is 4-byte aligned
+__device__ __forceinline__ uint32_t lds_u16_even(const uint8_t * base, int off) {
+    return (lds32(base + (off & ~3)) >> ((off & 2) * 8)) & 0xffffu;
+}
 
-template <> struct Quad<GX_T_Q8_0> {
+template <int TYPE> struct Oct;
+
+// Q8_0: lane o -> block b = o>>2 of the pair, NEON lane l = o&3; one
+// accumulator chain per lane, reduced by the faddp trees at the end.
+template <> struct Oct<GX_T_Q8_0> {
     static constexpr int VDT = GX_T_Q8_0;
-    static constexpr int UNIT = 64;   // a pair of 32-element blocks
-    struct St { float e = 0.0f, o = 0.0f; };
+    static constexpr int UNIT = 64;
+    struct St { float a = 0.0f; };
     __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int u,
-                                                int l, St & st) {
-        const int pe = wo + 68 * u;
-        const uint32_t w0 = lds32(wb + pe + 4 * l), w1 = lds32(wb + pe + 4 * l + 4);
-        const uint32_t w4 = lds32(wb + pe + 16 + 4 * l), w5 = lds32(wb + pe + 20 + 4 * l);
-        const uint32_t xea = __funnelshift_r(w0, w1, 16), xeb = __funnelshift_r(w4, w5, 16);
-        const uint32_t xoa = lds32(wb + pe + 36 + 4 * l), xob = lds32(wb + pe + 52 + 4 * l);
-        const float dxe = h2f(ld_u16(wb, pe)), dxo = h2f(ld_u16(wb, pe + 34));
-        const uint8_t * aq = ar + 64 * u;
-        const uint32_t yea = lds32(aq + 4 * l), yeb = lds32(aq + 16 + 4 * l);
-        const uint32_t yoa = lds32(aq + 32 + 4 * l), yob = lds32(aq + 48 + 4 * l);
-        const uint32_t dd = lds32(ar + L.d_off + 4 * u);
-        const int ie = dp4a(xeb, yeb, dp4a(xea, yea, 0));
-        const int io = dp4a(xob, yob, dp4a(xoa, yoa, 0));
-        st.e = __fmaf_rn((float)ie, __fmul_rn(dxe, h2f((uint16_t)(dd & 0xffffu))), st.e);
-        st.o = __fmaf_rn((float)io, __fmul_rn(dxo, h2f((uint16_t)(dd >> 16))), st.o);
+                                                int o, St & st) {
+        const int b = o >> 2, l = o & 3;
+        const int pb = wo + 68 * u + 34 * b;
+        uint32_t x0[1], x1[1];
+        ld_words<1>(wb, pb + 2 + 4 * l, x0);
+        ld_words<1>(wb, pb + 18 + 4 * l, x1);
+        const float dx = h2f((uint16_t)lds_u16_even(wb, pb));
+        const uint8_t * aq = ar + 64 * u + 32 * b;
+        const float dy = h2f((uint16_t)lds_u16_even(ar, L.d_off + 4 * u + 2 * b));
+        const int ip = dp4a(x1[0], lds32(aq + 16 + 4 * l), dp4a(x0[0], lds32(aq + 4 * l), 0));
+        st.a = __fmaf_rn((float)ip, __fmul_rn(dx, dy), st.a);
     }
     // ((e0+e1)+(e2+e3)) + ((o0+o1)+(o2+o3)), the NEON faddp trees
     __device__ __forceinline__ static float finish(St & st) {
-        float e = st.e, o = st.o;
-        e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, 1));
-        o = __fadd_rn(o, __shfl_xor_sync(0xffffffffu, o, 1));
-        e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, 2));
-        o = __fadd_rn(o, __shfl_xor_sync(0xffffffffu, o, 2));
-        return __fadd_rn(e, o);
+        float v = st.a;
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+        return __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
     }
 };
 
-template <> struct Quad<GX_T_MXFP4> {
+// MXFP4: lane o -> block b = o>>2, quarter l = o&3 of its 16 quant bytes;
+// t = fma(sc_e, p_e, sc_o*p_o) per pair, sumf = sumf + t.
+template <> struct Oct<GX_T_MXFP4> {
     static constexpr int VDT = GX_T_Q8_0;
     static constexpr int UNIT = 64;
     struct St { float s = 0.0f; };
     __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int u,
-                                                int l, St & st) {
-        const int pe = wo + 34 * u;
-        uint32_t qe[1], qo[1];
-        ld_words<1>(wb, pe + 1 + 4 * l, qe);
-        ld_words<1>(wb, pe + 18 + 4 * l, qo);
-        const uint8_t * aq = ar + 64 * u;
-        int ie = dp4a(mxfp4_lut(qe[0] & 0x0f0f0f0fu), lds32(aq + 4 * l), 0);
-        ie = dp4a(mxfp4_lut((qe[0] >> 4) & 0x0f0f0f0fu), lds32(aq + 16 + 4 * l), ie);
-        int io = dp4a(mxfp4_lut(qo[0] & 0x0f0f0f0fu), lds32(aq + 32 + 4 * l), 0);
-        io = dp4a(mxfp4_lut((qo[0] >> 4) & 0x0f0f0f0fu), lds32(aq + 48 + 4 * l), io);
-        ie = quad_sum(ie);
-        io = quad_sum(io);
+                                                int o, St & st) {
+        const int b = o >> 2, l = o & 3;
+        const int pp = wo + 34 * u;
+        uint32_t q[1];
+        ld_words<1>(wb, pp + 17 * b + 1 + 4 * l, q);
+        const uint8_t * aq = ar + 64 * u + 32 * b;
+        int ip = dp4a(mxfp4_lut(q[0] & 0x0f0f0f0fu), lds32(aq + 4 * l), 0);
+        ip = dp4a(mxfp4_lut((q[0] >> 4) & 0x0f0f0f0fu), lds32(aq + 16 + 4 * l), ip);
+        ip = quad_sum(ip);
+        const int other = __shfl_xor_sync(0xffffffffu, ip, 4);
+        const int pe = b ? other : ip, po = b ? ip : other;
         const uint32_t dd = lds32(ar + L.d_off + 4 * u);
-        const float sce = __fmul_rn(h2f((uint16_t)(dd & 0xffffu)), e8m0_half(wb[pe]));
-        const float sco = __fmul_rn(h2f((uint16_t)(dd >> 16)), e8m0_half(wb[pe + 17]));
-        st.s = __fadd_rn(st.s, __fmaf_rn(sce, (float)ie, __fmul_rn(sco, (float)io)));
+        const float sce = __fmul_rn(h2f((uint16_t)(dd & 0xffffu)), e8m0_half(wb[pp]));
+        const float sco = __fmul_rn(h2f((uint16_t)(dd >> 16)), e8m0_half(wb[pp + 17]));
+        st.s = __fadd_rn(st.s, __fmaf_rn(sce, (float)pe, __fmul_rn(sco, (float)po)));
     }
     __device__ __forceinline__ static float finish(St & st) { return st.s; }
 };
 
-template <> struct Quad<GX_T_Q4_K> {
+// Q4_K: lane o -> sub-block o (32 elements: nibble o&1 of quant bytes 32(o>>1)..)
+template <> struct Oct<GX_T_Q4_K> {
     static constexpr int VDT = GX_T_Q8_K;
     static constexpr int UNIT = 256;
     struct St { float s = 0.0f; };
     __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int i,
-                                                int l, St & st) {
+                                                int o, St & st) {
         const int xo = wo + 144 * i;
-        uint32_t q[8];
-        ld_words<8>(wb, xo + 16 + 32 * l, q);
-        uint32_t sw[3];
+        const int m = o >> 1, hn = o & 1;
+        uint32_t q[8], sw[3], dw[1];
+        ld_words<8>(wb, xo + 16 + 32 * m, q);
         ld_words<3>(wb, xo + 4, sw);
-        uint32_t dw[1];
         ld_words<1>(wb, xo, dw);
-        const uint8_t * aq = ar + 256 * i + 64 * l;
-        int p1 = 0, p2 = 0;
+        const uint8_t * aq = ar + 256 * i + 32 * o;
+        int p = 0;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            p1 = dp4a(q[w] & 0x0f0f0f0fu, lds32(aq + 4 * w), p1);
-            p2 = dp4a((q[w] >> 4) & 0x0f0f0f0fu, lds32(aq + 32 + 4 * w), p2);
+        for (int w = 0; w < 8; ++w) p = dp4a((hn ? (q[w] >> 4) : q[w]) & 0x0f0f0f0fu, lds32(aq + 4 * w), p);
+        int sc, mn;
+        if (o < 4) {
+            sc = (sw[0] >> (8 * o)) & 63;
+            mn = (sw[1] >> (8 * o)) & 63;
+        } else {
+            const int b = o - 4;
+            sc = ((sw[2] >> (8 * b)) & 0x0f) | (((sw[0] >> (8 * b + 6)) & 3) << 4);
+            mn = ((sw[2] >> (8 * b + 4)) & 0x0f) | (((sw[1] >> (8 * b + 6)) & 3) << 4);
         }
-        // 6-bit scale and min of sub-blocks a = 2l and 2l+1 (12-byte packing)
-        int sc[2], mn[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int a = 2 * l + h;
-            if (a < 4) {
-                sc[h] = (sw[0] >> (8 * a)) & 63;
-                mn[h] = (sw[1] >> (8 * a)) & 63;
-            } else {
-                const int b = a - 4;
-                sc[h] = ((sw[2] >> (8 * b)) & 0x0f) | (((sw[0] >> (8 * b + 6)) & 3) << 4);
-                mn[h] = ((sw[2] >> (8 * b + 4)) & 0x0f) | (((sw[1] >> (8 * b + 6)) & 3) << 4);
-            }
-        }
-        const uint2 bsw = *reinterpret_cast<const uint2 *>(ar + L.bs_off + 32 * i + 8 * l);
-        const int q8s0 = (int16_t)((int16_t)(bsw.x & 0xffff) + (int16_t)(bsw.x >> 16));
-        const int q8s1 = (int16_t)((int16_t)(bsw.y & 0xffff) + (int16_t)(bsw.y >> 16));
-        const int sumi = quad_sum(p1 * sc[0] + p2 * sc[1]);
-        const int prod = quad_sum(q8s0 * mn[0] + q8s1 * mn[1]);
-        const float yd = *reinterpret_cast<const float *>(ar + L.d_off + 4 * i);
+        const uint32_t bw = lds32(ar + L.bs_off + 32 * i + 4 * o);
+        const int q8s = (int16_t)((int16_t)(bw & 0xffff) + (int16_t)(bw >> 16));
+        const int sumi = oct_sum(p * sc);
+        const int prod = oct_sum(q8s * mn);
+        const float yd = __uint_as_float(lds32(ar + L.d_off + 4 * i));
         st.s = __fmaf_rn(-__fmul_rn(yd, h2f((uint16_t)(dw[0] >> 16))), (float)prod, st.s);
         st.s = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dw[0] & 0xffffu))), (float)sumi, st.s);
     }
     __device__ __forceinline__ static float finish(St & st) { return st.s; }
 };
 
-template <> struct Quad<GX_T_Q6_K> {
+// Q6_K: lane o -> 16-element groups 2o and 2o+1 (elements 32o..32o+31)
+template <> struct Oct<GX_T_Q6_K> {
     static constexpr int VDT = GX_T_Q8_K;
     static constexpr int UNIT = 256;
     struct St { float s = 0.0f; };
     __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int i,
-                                                int l, St & st) {
+                                                int o, St & st) {
         const int xo = wo + 210 * i;
-        const int h = l >> 1, odd = l & 1;
-        uint32_t ql[16], qh[8], scw[1];
-        ld_words<16>(wb, xo + 64 * h, ql);
+        const int j = o >> 1, ho = o & 1, h = j >> 1, odd = j & 1;
+        uint32_t ql[8], qh[8], scw[1];
+        ld_words<8>(wb, xo + 64 * h + 32 * ho, ql);
         ld_words<8>(wb, xo + 128 + 32 * h, qh);
-        ld_words<1>(wb, xo + 192 + 4 * l, scw);
-        const uint8_t * aq = ar + 256 * i + 64 * l;
-        const uint2 bsw = *reinterpret_cast<const uint2 *>(ar + L.bs_off + 32 * i + 8 * l);
-        const int bs4[4] = {(int16_t)(bsw.x & 0xffff), (int16_t)(bsw.x >> 16), (int16_t)(bsw.y & 0xffff),
-                            (int16_t)(bsw.y >> 16)};
-        int isum = 0, mins = 0;
+        ld_words<1>(wb, xo + 192 + 2 * o, scw);
+        const uint8_t * aq = ar + 256 * i + 32 * o;
+        const uint32_t sh = 4u * (uint32_t)odd + 2u * (uint32_t)ho;
+        int pg[2] = {0, 0};
 #pragma unroll
-        for (int gg = 0; gg < 4; ++gg) {
-            int pg = 0;
-#pragma unroll
-            for (int ww = 0; ww < 4; ++ww) {
-                const int w = 4 * gg + ww;
-                const uint32_t nib = (odd ? (ql[w] >> 4) : ql[w]) & 0x0f0f0f0fu;
-                const uint32_t sh = 4u * (uint32_t)odd + (w >= 8 ? 2u : 0u);
-                const uint32_t hb = (qh[w & 7] >> sh) & 0x03030303u;
-                pg = dp4a(nib | (hb << 4), lds32(aq + 4 * w), pg);
-            }
-            const int scg = (int)(int8_t)(scw[0] >> (8 * gg));
-            isum += pg * scg;
-            mins += bs4[gg] * scg;
+        for (int ww = 0; ww < 8; ++ww) {
+            const uint32_t nib = (odd ? (ql[ww] >> 4) : ql[ww]) & 0x0f0f0f0fu;
+            const uint32_t hb = (qh[ww] >> sh) & 0x03030303u;
+            pg[ww >> 2] = dp4a(nib | (hb << 4), lds32(aq + 4 * ww), pg[ww >> 2]);
         }
-        isum = quad_sum(isum);
-        mins = quad_sum(mins);
-        const float yd = *reinterpret_cast<const float *>(ar + L.d_off + 4 * i);
+        const int sc0 = (int)(int8_t)(scw[0] & 0xff), sc1 = (int)(int8_t)((scw[0] >> 8) & 0xff);
+        const uint32_t bw = lds32(ar + L.bs_off + 32 * i + 4 * o);
+        const int isum = oct_sum(pg[0] * sc0 + pg[1] * sc1);
+        const int mins = oct_sum((int)(int16_t)(bw & 0xffff) * sc0 + (int)(int16_t)(bw >> 16) * sc1);
+        const float yd = __uint_as_float(lds32(ar + L.d_off + 4 * i));
         st.s = __fmaf_rn(__fmul_rn(yd, h2f(ld_u16(wb, xo + 208))), (float)(isum - 32 * mins), st.s);
     }
     __device__ __forceinline__ static float finish(St & st) { return st.s; }
 };
 
-template <> struct Quad<GX_T_IQ1_S> {
+// IQ1_S: lane o -> sub-block o; sumi1 + sumi2 is the integer sum over all eight
+template <> struct Oct<GX_T_IQ1_S> {
     static constexpr int VDT = GX_T_Q8_K;
     static constexpr int UNIT = 256;
     struct St { float s = 0.0f; };
     __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int i,
-                                                int l, St & st) {
+                                                int o, St & st) {
         const int xo = wo + 50 * i;
-        uint32_t qsw[2], qhw[1];
-        ld_words<2>(wb, xo + 2 + 8 * l, qsw);
-        ld_words<1>(wb, xo + 34 + 4 * l, qhw);
-        const uint8_t * aq = ar + 256 * i + 64 * l;
-        int p[2] = {0, 0}, ls[2], sg[2];
+        uint32_t qsw[1], qhw[1];
+        ld_words<1>(wb, xo + 2 + 4 * o, qsw);
+        ld_words<1>(wb, xo + 34 + 2 * o, qhw);
+        const uint32_t qh = qhw[0] & 0xffffu;
+        const uint8_t * aq = ar + 256 * i + 32 * o;
+        int p = 0;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            const uint32_t qh = (qhw[0] >> (16 * hh)) & 0xffffu;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t gi = ((qsw[hh] >> (8 * j)) & 0xffu) | (((qh >> (3 * j)) & 7u) << 8);
-                const uint2 g = g_iq1s_grid[gi];
-                p[hh] = dp4a(g.x, lds32(aq + 32 * hh + 8 * j), p[hh]);
-                p[hh] = dp4a(g.y, lds32(aq + 32 * hh + 8 * j + 4), p[hh]);
-            }
-            ls[hh] = 2 * (int)((qh >> 12) & 7u) + 1;
-            sg[hh] = (qh & 0x8000u) ? -1 : 1;
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t gi = ((qsw[0] >> (8 * j)) & 0xffu) | (((qh >> (3 * j)) & 7u) << 8);
+            const uint2 g = g_iq1s_grid[gi];
+            p = dp4a(g.x, lds32(aq + 8 * j), p);
+            p = dp4a(g.y, lds32(aq + 8 * j + 4), p);
         }
-        const uint2 bsw = *reinterpret_cast<const uint2 *>(ar + L.bs_off + 32 * i + 8 * l);
-        const int b0 = (int16_t)(bsw.x & 0xffff), b1 = (int16_t)(bsw.x >> 16);
-        const int b2 = (int16_t)(bsw.y & 0xffff), b3 = (int16_t)(bsw.y >> 16);
-        const int s1 = quad_sum(p[0] * ls[0]);
-        const int s2 = quad_sum(p[1] * ls[1]);
-        const int s3 = quad_sum((b0 + b1) * ls[0] * sg[0] + (b2 + b3) * ls[1] * sg[1]);
-        const float yd = *reinterpret_cast<const float *>(ar + L.d_off + 4 * i);
-        const float expr = __fmaf_rn((float)s3, 0.125f, (float)(s1 + s2));
+        const int ls = 2 * (int)((qh >> 12) & 7u) + 1;
+        const int sg = (qh & 0x8000u) ? -1 : 1;
+        const uint32_t bw = lds32(ar + L.bs_off + 32 * i + 4 * o);
+        const int s12 = oct_sum(p * ls);
+        const int s3 = oct_sum(((int)(int16_t)(bw & 0xffff) + (int)(int16_t)(bw >> 16)) * ls * sg);
+        const float yd = __uint_as_float(lds32(ar + L.d_off + 4 * i));
+        const float expr = __fmaf_rn((float)s3, 0.125f, (float)s12);
         st.s = __fmaf_rn(__fmul_rn(yd, h2f(ld_u16(wb, xo))), expr, st.s);
     }
     __device__ __forceinline__ static float finish(St & st) { return st.s; }
@@ -338,8 +329,8 @@ __device__ __forceinline__ void issue_unit(const DecodeParams & p, int u, uint8_
 //         last CTA that contributed to it (no CTA ever waits for another).
 // MODE 2: down + weighted combine, one token per unit (all k slots).
 template <int TYPE, int MODE>
-__global__ void __launch_bounds__(128) k_decode(const DecodeParams p) {
-    using Q = Quad<TYPE>;
+__global__ void __launch_bounds__(kDecodeMaxThreads, 1) k_decode(const DecodeParams p) {
+    using Q = Oct<TYPE>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t * full = reinterpret_cast<uint64_t *>(smem);   // S stage barriers, then the activation barrier
     uint64_t * abar = full + p.S;
@@ -347,7 +338,7 @@ __global__ void __launch_bounds__(128) k_decode(const DecodeParams p) {
     uint8_t * stages = smem + p.stage_off;
     float * dots = reinterpret_cast<float *>(smem + p.dots_off);
     int * flag = reinterpret_cast<int *>(smem + p.flag_off);
-    const int tid = threadIdx.x, lane = tid & 31, l = tid & 3, row = tid >> 2;
+    const int tid = threadIdx.x, lane = tid & 31, l = tid & 7, row = tid >> 3;
     const int G = gridDim.x;
     const int tiles = p.ne01 / p.R;
     const int U = p.ne00 / Q::UNIT;
@@ -410,7 +401,7 @@ __global__ void __launch_bounds__(128) k_decode(const DecodeParams p) {
         const uint8_t * st_base = stages + s * p.stage_bytes;
         const uint8_t * arow = MODE == 1 ? act : act + (row / p.R) * p.al.pitch;
         typename Q::St acc;
-#pragma unroll 2
+#pragma unroll 4
         for (int v = 0; v < U; ++v) Q::unit(st_base, row * p.pitch_w, arow, p.al, v, l, acc);
         const float dot = Q::finish(acc);
         if (l == 0) dots[row] = dot;

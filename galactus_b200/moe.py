@@ -267,6 +267,45 @@ class StackCall:
         return self.st
 
 
+class StackPlan:
+    """gx_stack_plan_*: a decode stack captured once in a CUDA graph."""
+
+    def __init__(self, arena: "Arena", first_layer: int, n_layers: int, x_ptrs, w_ptrs, out_ptrs, k: int, T: int,
+                 timing: bool = False):
+        self.arena, self.n, self.k, self.T = arena, n_layers, k, T
+        xs = (C.c_void_p * n_layers)(*x_ptrs)
+        ws = (C.c_void_p * n_layers)(*w_ptrs)
+        os_ = (C.c_void_p * n_layers)(*out_ptrs)
+        h = C.c_void_p()
+        L.check(arena._lib.gx_stack_plan_create(arena.h, first_layer, n_layers, C.byref(arena.desc), xs, ws, os_, k, T,
+                                                1 if timing else 0, C.byref(h)), "gx_stack_plan_create")
+        self.h = h
+        self.st = L.gx_serve_stats()
+        self.fn = arena._lib.gx_stack_plan_run
+
+    def __call__(self, ids: np.ndarray, stream=None) -> L.gx_serve_stats:
+        rc = self.fn(self.h, ids.ctypes.data, _stream(stream), C.byref(self.st))
+        if rc != L.GX_OK:
+            raise L.GxError(rc, "gx_stack_plan_run")
+        return self.st
+
+    def timing(self) -> tuple[float, float]:
+        a, b = C.c_double(), C.c_double()
+        L.check(self.arena._lib.gx_stack_plan_timing(self.h, C.byref(a), C.byref(b)), "gx_stack_plan_timing")
+        return a.value, b.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.arena._lib.gx_stack_plan_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def mul_mat_id(type_: int, as_, ne00: int, ne01: int, nb01: int, nb02: int, n_as: int,
                b, ne11: int, ne12: int, nb11: int, nb12: int,
                ids, ne20: int, ne21: int, nbi1: int, dst, stream=None) -> None:

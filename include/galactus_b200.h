@@ -257,6 +257,23 @@ int gx_moe_stack_forward(gx_arena * arena, uint32_t first_layer, uint32_t n_laye
                          const float * const * x, const int32_t * ids, const float * const * w, int64_t k, int64_t T,
                          float * const * out, void * stream, gx_serve_stats * stats);
 
+/* A captured decode plan for a stack of layers: the three kernels of every
+ * layer recorded once in a CUDA graph with fixed input, weight and output
+ * pointers, slot ids read from a device array. Each run serves every layer
+ * through the policy on the host (misses copied as in gx_moe_layer_forward),
+ * copies the slot ids to the device and launches the graph. Same results as
+ * gx_moe_stack_forward. With timing = 1 the graph records CUDA events around
+ * each kernel (no programmatic overlap) and gx_stack_plan_timing returns the
+ * summed gate/up and down kernel milliseconds of the last run.
+ * No reference counterpart: the reference has no device graph. */
+typedef struct gx_stack_plan gx_stack_plan;
+int gx_stack_plan_create(gx_arena * arena, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * desc,
+                         const float * const * x, const float * const * w, float * const * out, int64_t k, int64_t T,
+                         int timing, gx_stack_plan ** plan);
+int gx_stack_plan_run(gx_stack_plan * plan, const int32_t * ids, void * stream, gx_serve_stats * stats);
+int gx_stack_plan_timing(gx_stack_plan * plan, double * gate_up_ms, double * down_ms);
+int gx_stack_plan_destroy(gx_stack_plan * plan);
+
 /* ------------------------------------------------------------- synthetic
  * Seeded synthetic data written straight into device memory (test and bench
  * inputs; the same generator is restated in the oracle):

@@ -276,3 +276,42 @@ def test_remap_serve_strided_and_slot_bytes(gxlib, orc, dev):
             seen += 1
     assert seen > 0
     arena.close()
+
+
+@pytest.mark.parametrize("name", ["qwen3-30b", "olmoe", "gpt-oss-120b"])
+def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name):
+    """The captured decode plan (CUDA graph, slot ids from a device array,
+    programmatic overlap) gives the oracle's bits, with misses and evictions
+    between runs, and the per-layer C-ABI path gives the same bits."""
+    from galactus_b200.moe import StackCall, StackPlan
+    m = _small_model(gxlib, name, experts=12, layers=3)
+    k = m.used
+    arena = gxlib.Arena(m, capacity_bytes=(k + 2) * m.record * m.layers, policy=gxlib.POLICY_AUTO, max_tokens=1)
+    recs = [np.stack([orc.synth_record(m, m.seed, L, e) for e in range(m.experts)]) for L in range(m.layers)]
+    for L in range(m.layers):
+        for e in range(m.experts):
+            arena.load_record(L, e, recs[L][e])
+    x = torch.zeros((m.layers, m.hidden), dtype=torch.float32, device=dev)
+    w = torch.zeros((m.layers, k), dtype=torch.float32, device=dev)
+    out = torch.zeros((m.layers, m.hidden), dtype=torch.float32, device=dev)
+    ptr = lambda t: [t[L].data_ptr() for L in range(m.layers)]
+    plan = StackPlan(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, 1)
+    call = StackCall(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, 1)
+    rng = np.random.default_rng(5)
+    stream = torch.cuda.current_stream()
+    for step in range(6):
+        xs = rng.standard_normal((m.layers, m.hidden)).astype(np.float32)
+        ids = np.stack([_zipf_routes(rng, 1, m.experts, k)[0] for _ in range(m.layers)]).astype(np.int32)  # [L,1,k]
+        ws = rng.random((m.layers, k)).astype(np.float32)
+        x.copy_(torch.from_numpy(xs))
+        w.copy_(torch.from_numpy(ws))
+        runner = plan if step % 2 == 0 else call
+        runner(np.ascontiguousarray(ids), stream)
+        got = H(out)
+        for L in range(m.layers):
+            want = orc.moe_layer(m, recs[L], xs[L][None], ids[L], ws[L][None])
+            np.testing.assert_array_equal(bits(got[L][None]), bits(want), err_msg=f"{name} step {step} layer {L}")
+    assert arena.stats()["misses"] > 0
+    no_device_error(gxlib)
+    plan.close()
+    arena.close()
