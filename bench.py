@@ -52,6 +52,7 @@ def parse():
     ap.add_argument("--sweep-steps", type=int, default=24)
     ap.add_argument("--prefill", type=int, default=512, help="prefill tokens at full residency (0 to skip)")
     ap.add_argument("--cpu-sample-layers", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=0, help="fewer layers (small profiling cases only)")
     return ap.parse_args()
 
 
@@ -188,6 +189,8 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     gx.check(gx.lib().gx_device_init(local))
     model = gx.MODELS[args.model]
+    if args.layers:
+        model = model.with_layers(args.layers)
     E, k, H, I, NL = model.experts, model.used, model.hidden, model.intermediate, model.layers
     stream = torch.cuda.Stream(device=dev)
 
@@ -221,8 +224,8 @@ def run_ours(args):
     setup_s = time.time() - t0
 
     # routes and inputs
-    P = 64                                   # distinct input slots, cycled
     n_tok = args.warmup + args.steps + args.sweep_steps + 8
+    P = min(64, n_tok)                       # distinct input slots, cycled
     ids_all, w_all = routes(model, n_tok, NL, seed=model.seed * 1000 + 17 + rank, rho=0.7)
     rng = np.random.default_rng(rank)
     xs = rng.standard_normal((P, NL, H)).astype(np.float32)
