@@ -111,6 +111,8 @@ _SIGS = {
     "gx_stack_plan_run": (C.c_int, [_P, _P, _P, C.POINTER(gx_serve_stats)]),
     "gx_stack_plan_timing": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "gx_stack_plan_destroy": (C.c_int, [_P]),
+    "gx_moe_ffn_noalloc": (C.c_int, [C.POINTER(gx_layer_desc), _P, C.c_uint64, C.c_uint32, _P, _P, _P, _I64, _I64,
+                                     _P, _P]),
     "gx_synth_normal": (C.c_int, [_P, _I64, C.c_uint64, C.c_uint64, C.c_float, _P]),
     "gx_synth_weights": (C.c_int, [C.c_int, _P, _I64, _I64, C.c_uint64, C.c_uint64, C.c_float, _P]),
 }

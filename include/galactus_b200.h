@@ -274,6 +274,31 @@ int gx_stack_plan_run(gx_stack_plan * plan, const int32_t * ids, void * stream, 
 int gx_stack_plan_timing(gx_stack_plan * plan, double * gate_up_ms, double * down_ms);
 int gx_stack_plan_destroy(gx_stack_plan * plan);
 
+/* ---------------------------------------------------------- no allocation
+ * One routed-expert FFN layer (gate/up + activation, down + weighted combine)
+ * that allocates nothing, for callers that may not call cudaMalloc: a host
+ * framework that owns every device allocation through its own pool, a plugin
+ * loaded into such a process, or a path that cannot absorb an allocation's
+ * latency and synchronization. The caller passes the expert records (slot 0's
+ * record at slot0_record, record_bytes apart, n_slots of them, roles at the
+ * offsets of desc), the layer input x [T, H] (device), HOST slot ids [T, k],
+ * router weights w [T, k] (device) and out [T, H] (device); results equal
+ * gx_moe_layer_forward's for the same slots.
+ * Scratch is one fixed __device__ array of GX_NOALLOC_SCRATCH_BYTES inside
+ * the library, held by every GPU that loads it until exit; k*T, H and I above
+ * the GX_NOALLOC_MAX_* limits are rejected with GX_ERR_INVALID. Every call on
+ * a device shares the array: calls that overlap on the GPU race and must be
+ * serialized by the caller. The first call on a device looks up the array's
+ * address (make it before any stream capture).
+ * No counterpart in the reference. */
+#define GX_NOALLOC_MAX_PAIRS 64
+#define GX_NOALLOC_MAX_HIDDEN 8192
+#define GX_NOALLOC_MAX_INTERMEDIATE 4096
+#define GX_NOALLOC_SCRATCH_BYTES (2u * 1024u * 1024u)
+int gx_moe_ffn_noalloc(const gx_layer_desc * desc, const void * slot0_record, uint64_t record_bytes, uint32_t n_slots,
+                       const float * x, const int32_t * slots, const float * w, int64_t k, int64_t T, float * out,
+                       void * stream);
+
 /* ------------------------------------------------------------- synthetic
  * Seeded synthetic data written straight into device memory (test and bench
  * inputs; the same generator is restated in the oracle):
