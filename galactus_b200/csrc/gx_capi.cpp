@@ -695,10 +695,10 @@ int plan_layer(gx_arena * a, uint32_t layer, const gx_layer_desc * d, int64_t k,
     dn.al = gx::act_layout(lp.vdt_d, (int)I);
     dn.a_rows = (int32_t)k;
     {
-        // 16 rows per stage (128 threads) when the tile keeps 16-byte alignment,
-        // else larger or smaller tiles
-        const int base_r = (int)(16 / k) > 0 ? (int)(16 / k) : 1;
-        const int cands[] = {base_r, 2 * base_r, base_r / 2, base_r / 4, 1};
+        // 32 rows per stage (128 threads, two rows each) when the tile keeps
+        // 16-byte alignment, else larger or smaller tiles; R stays even
+        const int base_r = (int)(32 / k) > 1 ? (int)(32 / k) : 2;
+        const int cands[] = {base_r, 2 * base_r, base_r / 2, base_r / 4, 2};
         int threads = 0;
         dn.R = 0;
         for (int R : cands) {

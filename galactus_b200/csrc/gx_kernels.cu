@@ -532,7 +532,8 @@ static cudaError_t launch_decode_t(DecodeParams & p, int threads, uint32_t smem,
     cudaError_t e = resident_per_sm(k_decode<TYPE, MODE>, threads, smem, per_sm);
     if (e != cudaSuccess) return e;
     const int cap = per_sm * device_sm_count();
-    const int grid = p.n_units < cap ? p.n_units : cap;
+    // one unit per CTA (S = 1) launches every unit; persistent grids are capped
+    const int grid = (p.S == 1 || p.n_units < cap) ? p.n_units : cap;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3((unsigned)threads);
@@ -549,7 +550,8 @@ static cudaError_t launch_decode_t(DecodeParams & p, int threads, uint32_t smem,
 // Shared-memory layout and tiling of a decode launch; 0 when it cannot fit.
 uint32_t decode_layout(int mode, DecodeParams & p, int & threads) {
     const int nexp = mode == 1 ? 2 : p.k;
-    threads = 8 * nexp * p.R;
+    if (mode == 2 && (p.R & 1)) return 0;   // row pairs stay inside one expert tile
+    threads = 4 * nexp * p.R;               // eight lanes per pair of rows
     if (threads > kDecodeMaxThreads || threads < 32 || threads % 32 != 0) return 0;
     if (p.nb01 % 16 == 0) {
         p.row_copy = 1;
@@ -562,10 +564,13 @@ uint32_t decode_layout(int mode, DecodeParams & p, int & threads) {
     p.stage_bytes = (int32_t)align_up((uint64_t)nexp * p.R * p.pitch_w + 16, 128);
     const uint32_t act_bytes = align_up((uint64_t)p.a_rows * p.al.pitch + 16, 128);
     const uint32_t fixed = 128 + act_bytes + 128 + 128;
-    const uint32_t budget = 72 * 1024;   // three CTAs per SM
-    int S = (int)((budget > fixed ? budget - fixed : 0) / (uint32_t)p.stage_bytes);
-    if (S > 4) S = 4;
-    if (S < 2) S = 2;
+    int S = p.S;
+    if (S <= 0) {
+        const uint32_t budget = 72 * 1024;   // three CTAs per SM
+        S = (int)((budget > fixed ? budget - fixed : 0) / (uint32_t)p.stage_bytes);
+        if (S > 4) S = 4;
+        if (S < 2) S = 2;
+    }
     p.S = S;
     p.act_off = 128;
     p.stage_off = p.act_off + act_bytes;
@@ -588,6 +593,8 @@ static cudaError_t launch_decode_mode(int type, DecodeParams & p, int threads, u
     }
 }
 
+static void choose_stages(int mode, DecodeParams & p);
+
 template <int MODE>
 static cudaError_t prepare_decode_mode(int type, int threads, uint32_t smem) {
     int per_sm = 0;
@@ -603,13 +610,30 @@ static cudaError_t prepare_decode_mode(int type, int threads, uint32_t smem) {
 
 cudaError_t prepare_decode(int type, int mode, DecodeParams p) {
     int threads = 0;
+    if (p.S == 0) choose_stages(mode, p);
     const uint32_t smem = decode_layout(mode, p, threads);
     if (smem == 0) return cudaErrorInvalidConfiguration;
     return mode == 1 ? prepare_decode_mode<1>(type, threads, smem) : prepare_decode_mode<2>(type, threads, smem);
 }
 
+// Decode-sized launches (a few units per SM) run one unit per CTA with one
+// stage: half the shared memory per CTA, twice the resident warps, every
+// weight byte requested at once. Larger launches use persistent CTAs with a
+// multi-stage pipeline.
+static void choose_stages(int mode, DecodeParams & p) {
+    DecodeParams one = p;
+    one.S = 1;
+    int threads = 0;
+    const uint32_t smem1 = decode_layout(mode, one, threads);
+    if (smem1 == 0) { p.S = 0; return; }
+    const uint32_t per_sm_smem = 227u * 1024u;
+    const int per_sm = (int)(per_sm_smem / (smem1 + 1024u)) > 0 ? (int)(per_sm_smem / (smem1 + 1024u)) : 1;
+    p.S = p.n_units <= 2 * per_sm * device_sm_count() ? 1 : 0;
+}
+
 cudaError_t launch_decode(int type, int mode, DecodeParams & p, cudaStream_t stream, bool pdl) {
     int threads = 0;
+    if (p.S == 0) choose_stages(mode, p);
     const uint32_t smem = decode_layout(mode, p, threads);
     if (smem == 0) return cudaErrorInvalidConfiguration;
     return mode == 1 ? launch_decode_mode<1>(type, p, threads, smem, stream, pdl)

@@ -101,26 +101,58 @@ __device__ __forceinline__ uint32_t lds_u16_even(const uint8_t * base, int off) 
     return (lds32(base + (off & ~3)) >> ((off & 2) * 8)) & 0xffffu;
 }
 
+// Each lane prepares its lane-constant shared-memory offsets once per row
+// (Lane), then walks the units with immediate offsets. Block sizes of 17, 50
+// and 210 bytes make the byte alignment alternate between even and odd units,
+// so units are processed in (even, odd) pairs, each with its own precomputed
+// shift, in row order.
+
 template <int TYPE> struct Oct;
 
-// Q8_0: lane o -> block b = o>>2 of the pair, NEON lane l = o&3; one
-// accumulator chain per lane, reduced by the faddp trees at the end.
+__device__ __forceinline__ uint32_t bfe16(uint32_t w, uint32_t sh) { return (w >> sh) & 0xffffu; }
+
+// A thread computes two weight rows against one activation row: the
+// activation words and scales are loaded once for both. W is the per-row
+// lane context, A the shared activation context.
+
 template <> struct Oct<GX_T_Q8_0> {
     static constexpr int VDT = GX_T_Q8_0;
     static constexpr int UNIT = 64;
     struct St { float a = 0.0f; };
-    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int u,
-                                                int o, St & st) {
+    struct W { const uint8_t * wq; const uint8_t * wd; uint32_t sh, dsh; };
+    struct A { const uint8_t * aq; const uint8_t * ad; uint32_t ash; };
+    __device__ __forceinline__ static W initw(const uint8_t * wb, int wo, int o) {
         const int b = o >> 2, l = o & 3;
-        const int pb = wo + 68 * u + 34 * b;
-        uint32_t x0[1], x1[1];
-        ld_words<1>(wb, pb + 2 + 4 * l, x0);
-        ld_words<1>(wb, pb + 18 + 4 * l, x1);
-        const float dx = h2f((uint16_t)lds_u16_even(wb, pb));
-        const uint8_t * aq = ar + 64 * u + 32 * b;
-        const float dy = h2f((uint16_t)lds_u16_even(ar, L.d_off + 4 * u + 2 * b));
-        const int ip = dp4a(x1[0], lds32(aq + 16 + 4 * l), dp4a(x0[0], lds32(aq + 4 * l), 0));
-        st.a = __fmaf_rn((float)ip, __fmul_rn(dx, dy), st.a);
+        const int q = wo + 34 * b + 2 + 4 * l, d = wo + 34 * b;
+        W w;
+        w.wq = wb + (q & ~3);
+        w.sh = (uint32_t)(q & 3) * 8u;
+        w.wd = wb + (d & ~3);
+        w.dsh = (uint32_t)(d & 2) * 8u;
+        return w;
+    }
+    __device__ __forceinline__ static A inita(const uint8_t * ar, const ActLayout & L, int o) {
+        const int b = o >> 2, l = o & 3;
+        A a;
+        a.aq = ar + 32 * b + 4 * l;
+        a.ad = ar + L.d_off;
+        a.ash = 16u * (uint32_t)b;
+        return a;
+    }
+    template <int PAR>
+    __device__ __forceinline__ static void unit(const W (&w)[2], const A & a, int u, St (&st)[2]) {
+        const uint8_t * ap = a.aq + 64 * u;
+        const uint32_t y0 = lds32(ap), y1 = lds32(ap + 16);
+        const float dy = h2f((uint16_t)bfe16(lds32(a.ad + 4 * u), a.ash));
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint8_t * q = w[r].wq + 68 * u;
+            const uint32_t x0 = __funnelshift_r(lds32(q), lds32(q + 4), w[r].sh);
+            const uint32_t x1 = __funnelshift_r(lds32(q + 16), lds32(q + 20), w[r].sh);
+            const float dx = h2f((uint16_t)bfe16(lds32(w[r].wd + 68 * u), w[r].dsh));
+            const int ip = dp4a(x1, y1, dp4a(x0, y0, 0));
+            st[r].a = __fmaf_rn((float)ip, __fmul_rn(dx, dy), st[r].a);
+        }
     }
     // ((e0+e1)+(e2+e3)) + ((o0+o1)+(o2+o3)), the NEON faddp trees
     __device__ __forceinline__ static float finish(St & st) {
@@ -131,65 +163,107 @@ template <> struct Oct<GX_T_Q8_0> {
     }
 };
 
-// MXFP4: lane o -> block b = o>>2, quarter l = o&3 of its 16 quant bytes;
+// MXFP4: lane o -> block b = o>>2, quant word l = o&3 of its 16 bytes;
 // t = fma(sc_e, p_e, sc_o*p_o) per pair, sumf = sumf + t.
 template <> struct Oct<GX_T_MXFP4> {
     static constexpr int VDT = GX_T_Q8_0;
     static constexpr int UNIT = 64;
     struct St { float s = 0.0f; };
-    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int u,
-                                                int o, St & st) {
+    struct W { const uint8_t * wq[2]; uint32_t sh[2]; const uint8_t * we; };
+    struct A { const uint8_t * aq; const uint8_t * ad; int b; };
+    __device__ __forceinline__ static W initw(const uint8_t * wb, int wo, int o) {
         const int b = o >> 2, l = o & 3;
-        const int pp = wo + 34 * u;
-        uint32_t q[1];
-        ld_words<1>(wb, pp + 17 * b + 1 + 4 * l, q);
-        const uint8_t * aq = ar + 64 * u + 32 * b;
-        int ip = dp4a(mxfp4_lut(q[0] & 0x0f0f0f0fu), lds32(aq + 4 * l), 0);
-        ip = dp4a(mxfp4_lut((q[0] >> 4) & 0x0f0f0f0fu), lds32(aq + 16 + 4 * l), ip);
-        ip = quad_sum(ip);
-        const int other = __shfl_xor_sync(0xffffffffu, ip, 4);
-        const int pe = b ? other : ip, po = b ? ip : other;
-        const uint32_t dd = lds32(ar + L.d_off + 4 * u);
-        const float sce = __fmul_rn(h2f((uint16_t)(dd & 0xffffu)), e8m0_half(wb[pp]));
-        const float sco = __fmul_rn(h2f((uint16_t)(dd >> 16)), e8m0_half(wb[pp + 17]));
-        st.s = __fadd_rn(st.s, __fmaf_rn(sce, (float)pe, __fmul_rn(sco, (float)po)));
+        W w;
+        for (int par = 0; par < 2; ++par) {
+            const int q = wo + 34 * par + 17 * b + 1 + 4 * l;
+            w.wq[par] = wb + (q & ~3) - 34 * par;   // unit u of parity par reads wq[par] + 34*u
+            w.sh[par] = (uint32_t)(q & 3) * 8u;
+        }
+        w.we = wb + wo;
+        return w;
+    }
+    __device__ __forceinline__ static A inita(const uint8_t * ar, const ActLayout & L, int o) {
+        A a;
+        a.b = o >> 2;
+        a.aq = ar + 32 * a.b + 4 * (o & 3);
+        a.ad = ar + L.d_off;
+        return a;
+    }
+    template <int PAR>
+    __device__ __forceinline__ static void unit(const W (&w)[2], const A & a, int u, St (&st)[2]) {
+        const uint8_t * ap = a.aq + 64 * u;
+        const uint32_t ylo = lds32(ap), yhi = lds32(ap + 16);
+        const uint32_t dd = lds32(a.ad + 4 * u);
+        const float dye = h2f((uint16_t)(dd & 0xffffu)), dyo = h2f((uint16_t)(dd >> 16));
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint8_t * q = w[r].wq[PAR] + 34 * u;
+            const uint32_t qq = __funnelshift_r(lds32(q), lds32(q + 4), w[r].sh[PAR]);
+            int ip = dp4a(mxfp4_lut(qq & 0x0f0f0f0fu), ylo, 0);
+            ip = dp4a(mxfp4_lut((qq >> 4) & 0x0f0f0f0fu), yhi, ip);
+            ip = quad_sum(ip);
+            const int other = __shfl_xor_sync(0xffffffffu, ip, 4);
+            const int pe = a.b ? other : ip, po = a.b ? ip : other;
+            const float sce = __fmul_rn(dye, e8m0_half(w[r].we[34 * u]));
+            const float sco = __fmul_rn(dyo, e8m0_half(w[r].we[34 * u + 17]));
+            st[r].s = __fadd_rn(st[r].s, __fmaf_rn(sce, (float)pe, __fmul_rn(sco, (float)po)));
+        }
     }
     __device__ __forceinline__ static float finish(St & st) { return st.s; }
 };
 
-// Q4_K: lane o -> sub-block o (32 elements: nibble o&1 of quant bytes 32(o>>1)..)
+// Q4_K: lane o -> sub-block o (32 elements: nibble o&1 of quant bytes 32(o>>1)..);
+// rows and superblocks are 16-byte aligned, so quants load 16 bytes at a time.
 template <> struct Oct<GX_T_Q4_K> {
     static constexpr int VDT = GX_T_Q8_K;
     static constexpr int UNIT = 256;
     struct St { float s = 0.0f; };
-    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int i,
-                                                int o, St & st) {
-        const int xo = wo + 144 * i;
-        const int m = o >> 1, hn = o & 1;
-        uint32_t q[8], sw[3], dw[1];
-        ld_words<8>(wb, xo + 16 + 32 * m, q);
-        ld_words<3>(wb, xo + 4, sw);
-        ld_words<1>(wb, xo, dw);
-        const uint8_t * aq = ar + 256 * i + 32 * o;
-        int p = 0;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) p = dp4a((hn ? (q[w] >> 4) : q[w]) & 0x0f0f0f0fu, lds32(aq + 4 * w), p);
-        int sc, mn;
-        if (o < 4) {
-            sc = (sw[0] >> (8 * o)) & 63;
-            mn = (sw[1] >> (8 * o)) & 63;
-        } else {
-            const int b = o - 4;
-            sc = ((sw[2] >> (8 * b)) & 0x0f) | (((sw[0] >> (8 * b + 6)) & 3) << 4);
-            mn = ((sw[2] >> (8 * b + 4)) & 0x0f) | (((sw[1] >> (8 * b + 6)) & 3) << 4);
-        }
-        const uint32_t bw = lds32(ar + L.bs_off + 32 * i + 4 * o);
+    struct W { const uint8_t * wb; };
+    struct A { const uint8_t * aq; const uint8_t * ar; ActLayout L; int o; };
+    __device__ __forceinline__ static W initw(const uint8_t * wb, int wo, int) { return W{wb + wo}; }
+    __device__ __forceinline__ static A inita(const uint8_t * ar, const ActLayout & L, int o) {
+        A a;
+        a.aq = ar + 32 * o;
+        a.ar = ar;
+        a.L = L;
+        a.o = o;
+        return a;
+    }
+    template <int PAR>
+    __device__ __forceinline__ static void unit(const W (&w)[2], const A & a, int i, St (&st)[2]) {
+        const int o = a.o, m = o >> 1;
+        const uint32_t shn = 4u * (uint32_t)(o & 1);
+        const uint8_t * ap = a.aq + 256 * i;
+        const uint4 a0 = *reinterpret_cast<const uint4 *>(ap);
+        const uint4 a1 = *reinterpret_cast<const uint4 *>(ap + 16);
+        const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const uint32_t bw = lds32(a.ar + a.L.bs_off + 32 * i + 4 * o);
         const int q8s = (int16_t)((int16_t)(bw & 0xffff) + (int16_t)(bw >> 16));
-        const int sumi = oct_sum(p * sc);
-        const int prod = oct_sum(q8s * mn);
-        const float yd = __uint_as_float(lds32(ar + L.d_off + 4 * i));
-        st.s = __fmaf_rn(-__fmul_rn(yd, h2f((uint16_t)(dw[0] >> 16))), (float)prod, st.s);
-        st.s = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dw[0] & 0xffffu))), (float)sumi, st.s);
+        const float yd = __uint_as_float(lds32(a.ar + a.L.d_off + 4 * i));
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint8_t * xb = w[r].wb + 144 * i;
+            const uint4 q0 = *reinterpret_cast<const uint4 *>(xb + 16 + 32 * m);
+            const uint4 q1 = *reinterpret_cast<const uint4 *>(xb + 32 + 32 * m);
+            const uint4 hdr = *reinterpret_cast<const uint4 *>(xb);
+            const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            int p = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) p = dp4a((qw[k] >> shn) & 0x0f0f0f0fu, aw[k], p);
+            int sc, mn;
+            if (o < 4) {
+                sc = (hdr.y >> (8 * o)) & 63;
+                mn = (hdr.z >> (8 * o)) & 63;
+            } else {
+                const int b = o - 4;
+                sc = ((hdr.w >> (8 * b)) & 0x0f) | (((hdr.y >> (8 * b + 6)) & 3) << 4);
+                mn = ((hdr.w >> (8 * b + 4)) & 0x0f) | (((hdr.z >> (8 * b + 6)) & 3) << 4);
+            }
+            const int sumi = oct_sum(p * sc);
+            const int prod = oct_sum(q8s * mn);
+            st[r].s = __fmaf_rn(-__fmul_rn(yd, h2f((uint16_t)(hdr.x >> 16))), (float)prod, st[r].s);
+            st[r].s = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(hdr.x & 0xffffu))), (float)sumi, st[r].s);
+        }
     }
     __device__ __forceinline__ static float finish(St & st) { return st.s; }
 };
@@ -199,29 +273,49 @@ template <> struct Oct<GX_T_Q6_K> {
     static constexpr int VDT = GX_T_Q8_K;
     static constexpr int UNIT = 256;
     struct St { float s = 0.0f; };
-    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int i,
-                                                int o, St & st) {
-        const int xo = wo + 210 * i;
+    struct W { const uint8_t * wb; int wo; };
+    struct A { const uint8_t * aq; const uint8_t * ar; ActLayout L; int o; };
+    __device__ __forceinline__ static W initw(const uint8_t * wb, int wo, int) { return W{wb, wo}; }
+    __device__ __forceinline__ static A inita(const uint8_t * ar, const ActLayout & L, int o) {
+        A a;
+        a.aq = ar + 32 * o;
+        a.ar = ar;
+        a.L = L;
+        a.o = o;
+        return a;
+    }
+    template <int PAR>
+    __device__ __forceinline__ static void unit(const W (&w)[2], const A & a, int i, St (&st)[2]) {
+        const int o = a.o;
         const int j = o >> 1, ho = o & 1, h = j >> 1, odd = j & 1;
-        uint32_t ql[8], qh[8], scw[1];
-        ld_words<8>(wb, xo + 64 * h + 32 * ho, ql);
-        ld_words<8>(wb, xo + 128 + 32 * h, qh);
-        ld_words<1>(wb, xo + 192 + 2 * o, scw);
-        const uint8_t * aq = ar + 256 * i + 32 * o;
+        const uint8_t * ap = a.aq + 256 * i;
+        const uint4 a0 = *reinterpret_cast<const uint4 *>(ap);
+        const uint4 a1 = *reinterpret_cast<const uint4 *>(ap + 16);
+        const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
         const uint32_t sh = 4u * (uint32_t)odd + 2u * (uint32_t)ho;
-        int pg[2] = {0, 0};
+        const uint32_t nsh = 4u * (uint32_t)odd;
+        const uint32_t bw = lds32(a.ar + a.L.bs_off + 32 * i + 4 * o);
+        const int bs0 = (int)(int16_t)(bw & 0xffff), bs1 = (int)(int16_t)(bw >> 16);
+        const float yd = __uint_as_float(lds32(a.ar + a.L.d_off + 4 * i));
 #pragma unroll
-        for (int ww = 0; ww < 8; ++ww) {
-            const uint32_t nib = (odd ? (ql[ww] >> 4) : ql[ww]) & 0x0f0f0f0fu;
-            const uint32_t hb = (qh[ww] >> sh) & 0x03030303u;
-            pg[ww >> 2] = dp4a(nib | (hb << 4), lds32(aq + 4 * ww), pg[ww >> 2]);
+        for (int r = 0; r < 2; ++r) {
+            const int xo = w[r].wo + 210 * i;
+            uint32_t ql[8], qh[8], scw[1];
+            ld_words<8>(w[r].wb, xo + 64 * h + 32 * ho, ql);
+            ld_words<8>(w[r].wb, xo + 128 + 32 * h, qh);
+            ld_words<1>(w[r].wb, xo + 192 + 2 * o, scw);
+            int pg[2] = {0, 0};
+#pragma unroll
+            for (int ww = 0; ww < 8; ++ww) {
+                const uint32_t nib = (ql[ww] >> nsh) & 0x0f0f0f0fu;
+                const uint32_t hb = (qh[ww] >> sh) & 0x03030303u;
+                pg[ww >> 2] = dp4a(nib | (hb << 4), aw[ww], pg[ww >> 2]);
+            }
+            const int sc0 = (int)(int8_t)(scw[0] & 0xff), sc1 = (int)(int8_t)((scw[0] >> 8) & 0xff);
+            const int isum = oct_sum(pg[0] * sc0 + pg[1] * sc1);
+            const int mins = oct_sum(bs0 * sc0 + bs1 * sc1);
+            st[r].s = __fmaf_rn(__fmul_rn(yd, h2f(ld_u16(w[r].wb, xo + 208))), (float)(isum - 32 * mins), st[r].s);
         }
-        const int sc0 = (int)(int8_t)(scw[0] & 0xff), sc1 = (int)(int8_t)((scw[0] >> 8) & 0xff);
-        const uint32_t bw = lds32(ar + L.bs_off + 32 * i + 4 * o);
-        const int isum = oct_sum(pg[0] * sc0 + pg[1] * sc1);
-        const int mins = oct_sum((int)(int16_t)(bw & 0xffff) * sc0 + (int)(int16_t)(bw >> 16) * sc1);
-        const float yd = __uint_as_float(lds32(ar + L.d_off + 4 * i));
-        st.s = __fmaf_rn(__fmul_rn(yd, h2f(ld_u16(wb, xo + 208))), (float)(isum - 32 * mins), st.s);
     }
     __device__ __forceinline__ static float finish(St & st) { return st.s; }
 };
@@ -231,30 +325,49 @@ template <> struct Oct<GX_T_IQ1_S> {
     static constexpr int VDT = GX_T_Q8_K;
     static constexpr int UNIT = 256;
     struct St { float s = 0.0f; };
-    __device__ __forceinline__ static void unit(const uint8_t * wb, int wo, const uint8_t * ar, const ActLayout & L, int i,
-                                                int o, St & st) {
-        const int xo = wo + 50 * i;
-        uint32_t qsw[1], qhw[1];
-        ld_words<1>(wb, xo + 2 + 4 * o, qsw);
-        ld_words<1>(wb, xo + 34 + 2 * o, qhw);
-        const uint32_t qh = qhw[0] & 0xffffu;
-        const uint8_t * aq = ar + 256 * i + 32 * o;
-        int p = 0;
+    struct W { const uint8_t * wb; int wo; };
+    struct A { const uint8_t * aq; const uint8_t * ar; ActLayout L; int o; };
+    __device__ __forceinline__ static W initw(const uint8_t * wb, int wo, int) { return W{wb, wo}; }
+    __device__ __forceinline__ static A inita(const uint8_t * ar, const ActLayout & L, int o) {
+        A a;
+        a.aq = ar + 32 * o;
+        a.ar = ar;
+        a.L = L;
+        a.o = o;
+        return a;
+    }
+    template <int PAR>
+    __device__ __forceinline__ static void unit(const W (&w)[2], const A & a, int i, St (&st)[2]) {
+        const int o = a.o;
+        const uint8_t * ap = a.aq + 256 * i;
+        const uint4 a0 = *reinterpret_cast<const uint4 *>(ap);
+        const uint4 a1 = *reinterpret_cast<const uint4 *>(ap + 16);
+        const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const uint32_t bw = lds32(a.ar + a.L.bs_off + 32 * i + 4 * o);
+        const int bsum = (int)(int16_t)(bw & 0xffff) + (int)(int16_t)(bw >> 16);
+        const float yd = __uint_as_float(lds32(a.ar + a.L.d_off + 4 * i));
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t gi = ((qsw[0] >> (8 * j)) & 0xffu) | (((qh >> (3 * j)) & 7u) << 8);
-            const uint2 g = g_iq1s_grid[gi];
-            p = dp4a(g.x, lds32(aq + 8 * j), p);
-            p = dp4a(g.y, lds32(aq + 8 * j + 4), p);
+        for (int r = 0; r < 2; ++r) {
+            const int xo = w[r].wo + 50 * i;
+            uint32_t qsw[1], qhw[1];
+            ld_words<1>(w[r].wb, xo + 2 + 4 * o, qsw);
+            ld_words<1>(w[r].wb, xo + 34 + 2 * o, qhw);
+            const uint32_t qh = qhw[0] & 0xffffu;
+            int p = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t gi = ((qsw[0] >> (8 * j)) & 0xffu) | (((qh >> (3 * j)) & 7u) << 8);
+                const uint2 g = g_iq1s_grid[gi];
+                p = dp4a(g.x, aw[2 * j], p);
+                p = dp4a(g.y, aw[2 * j + 1], p);
+            }
+            const int ls = 2 * (int)((qh >> 12) & 7u) + 1;
+            const int sg = (qh & 0x8000u) ? -1 : 1;
+            const int s12 = oct_sum(p * ls);
+            const int s3 = oct_sum(bsum * ls * sg);
+            const float expr = __fmaf_rn((float)s3, 0.125f, (float)s12);
+            st[r].s = __fmaf_rn(__fmul_rn(yd, h2f(ld_u16(w[r].wb, xo))), expr, st[r].s);
         }
-        const int ls = 2 * (int)((qh >> 12) & 7u) + 1;
-        const int sg = (qh & 0x8000u) ? -1 : 1;
-        const uint32_t bw = lds32(ar + L.bs_off + 32 * i + 4 * o);
-        const int s12 = oct_sum(p * ls);
-        const int s3 = oct_sum(((int)(int16_t)(bw & 0xffff) + (int)(int16_t)(bw >> 16)) * ls * sg);
-        const float yd = __uint_as_float(lds32(ar + L.d_off + 4 * i));
-        const float expr = __fmaf_rn((float)s3, 0.125f, (float)s12);
-        st.s = __fmaf_rn(__fmul_rn(yd, h2f(ld_u16(wb, xo))), expr, st.s);
     }
     __device__ __forceinline__ static float finish(St & st) { return st.s; }
 };
@@ -338,7 +451,11 @@ __global__ void __launch_bounds__(kDecodeMaxThreads, 1) k_decode(const DecodePar
     uint8_t * stages = smem + p.stage_off;
     float * dots = reinterpret_cast<float *>(smem + p.dots_off);
     int * flag = reinterpret_cast<int *>(smem + p.flag_off);
-    const int tid = threadIdx.x, lane = tid & 31, l = tid & 7, row = tid >> 3;
+    const int tid = threadIdx.x, lane = tid & 31, l = tid & 7, grp = tid >> 3;
+    // the two rows of this thread: gate row and up row (MODE 1), or two
+    // adjacent rows of one expert tile (MODE 2); both use the same activation
+    const int row0 = MODE == 1 ? grp : 2 * grp;
+    const int row1 = MODE == 1 ? grp + p.R : 2 * grp + 1;
     const int G = gridDim.x;
     const int tiles = p.ne01 / p.R;
     const int U = p.ne00 / Q::UNIT;
@@ -399,12 +516,23 @@ __global__ void __launch_bounds__(kDecodeMaxThreads, 1) k_decode(const DecodePar
             return;
         }
         const uint8_t * st_base = stages + s * p.stage_bytes;
-        const uint8_t * arow = MODE == 1 ? act : act + (row / p.R) * p.al.pitch;
-        typename Q::St acc;
-#pragma unroll 4
-        for (int v = 0; v < U; ++v) Q::unit(st_base, row * p.pitch_w, arow, p.al, v, l, acc);
-        const float dot = Q::finish(acc);
-        if (l == 0) dots[row] = dot;
+        const uint8_t * arow = MODE == 1 ? act : act + (row0 / p.R) * p.al.pitch;
+        typename Q::St acc[2];
+        const typename Q::W wl[2] = {Q::initw(st_base, row0 * p.pitch_w, l), Q::initw(st_base, row1 * p.pitch_w, l)};
+        const typename Q::A al = Q::inita(arow, p.al, l);
+        int v = 0;
+#pragma unroll 2
+        for (; v + 1 < U; v += 2) {
+            Q::template unit<0>(wl, al, v, acc);
+            Q::template unit<1>(wl, al, v + 1, acc);
+        }
+        if (v < U) Q::template unit<0>(wl, al, v, acc);
+        const float dot0 = Q::finish(acc[0]);
+        const float dot1 = Q::finish(acc[1]);
+        if (l == 0) {
+            dots[row0] = dot0;
+            dots[row1] = dot1;
+        }
         __syncthreads();
         // the stage is free: stream the unit S steps ahead into it
         if (tid == 0) {
