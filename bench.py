@@ -53,7 +53,11 @@ def parse():
     ap.add_argument("--prefill", type=int, default=512, help="prefill tokens at full residency (0 to skip)")
     ap.add_argument("--cpu-sample-layers", type=int, default=3)
     ap.add_argument("--layers", type=int, default=0, help="fewer layers (small profiling cases only)")
-    return ap.parse_args()
+    ap.add_argument("--stack-tiles", default="", help="stack kernel tiling 'Rg,Rd,S,ctas_per_sm' (default: library's)")
+    a = ap.parse_args()
+    if a.stack_tiles:
+        os.environ["GX_STACK_TILES"] = a.stack_tiles
+    return a
 
 
 def measured_peaks():
@@ -294,9 +298,9 @@ def run_ours(args):
     x_fix = torch.empty((NL, H), dtype=torch.float32, device=dev)
     w_fix = torch.empty((NL, k), dtype=torch.float32, device=dev)
 
-    def plan_for(a, timing=False):
+    def plan_for(a, timing=False, layerwise=False):
         return StackPlan(a, 0, NL, [x_fix[L].data_ptr() for L in range(NL)], [w_fix[L].data_ptr() for L in range(NL)],
-                         [out_dev[L].data_ptr() for L in range(NL)], k, 1, timing=timing)
+                         [out_dev[L].data_ptr() for L in range(NL)], k, 1, timing=timing, layerwise=layerwise)
 
     def run_plan(plan, t_first, n, e2e=None):
         st_h = st_m = 0
@@ -356,6 +360,19 @@ def run_ours(args):
         results["e2e"] = {"value": world * args.steps / (ms_e2e / 1e3), "unit": "tok/s",
                           "h2d_bytes_per_step": NL * H * 4 + NL * k * 4, "d2h_bytes_per_step": NL * H * 4}
 
+        plan_info = plan.info()
+
+        # ---------------- the same step as a graph of three kernels per layer
+        lplan = plan_for(arena, layerwise=True)
+        run_plan(lplan, 0, args.warmup)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        run_plan(lplan, args.warmup, args.steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        results["layerwise_graph_tok_s"] = world * args.steps / (max_over_ranks(ev0.elapsed_time(ev1)) / 1e3)
+        lplan.close()
+
         # ---------------- the same step through the per-layer C-ABI calls (no graph)
         call = stack_for(arena)
         tabs = ptr_tables(call)
@@ -367,8 +384,15 @@ def run_ours(args):
         torch.cuda.synchronize()
         results["layer_path_tok_s"] = world * args.steps / (max_over_ranks(ev0.elapsed_time(ev1)) / 1e3)
 
-        # ---------------- per-kernel timing: a graph with events around each kernel
-        tplan = plan_for(arena, timing=True)
+        # ---------------- kernel timing: CUDA events recorded inside the graphs
+        # around the stack kernel, and around each kernel of the layerwise graph
+        kplan = plan_for(arena, timing=True)
+        stack_ms = 0.0
+        for i in range(args.steps):
+            run_plan(kplan, args.warmup + i, 1)
+            stack_ms += kplan.timing()[0]
+        kplan.close()
+        tplan = plan_for(arena, timing=True, layerwise=True)
         gu_ms = dn_ms = 0.0
         calls = 0
         for i in range(args.steps):
@@ -435,7 +459,11 @@ def run_ours(args):
     gu_bytes = k * 2 * I * rb_h + H * 4 + k * I * 4
     dn_bytes = k * H * rb_i + k * I * 4 + k * 4 + H * 4
     gu_avg, dn_avg = gu_ms / max(1, calls), dn_ms / max(1, calls)
-    if gu_ms >= dn_ms:
+    stack_avg = stack_ms / max(1, args.steps)
+    if plan_info["stack_kernel"]:
+        # one launch streams every layer: NL x (gate/up + down) algorithmic bytes
+        dom, dbytes, dms = "k_stack (persistent: all layers, gate/up+act, down+combine)", NL * (gu_bytes + dn_bytes), stack_avg
+    elif gu_ms >= dn_ms:
         dom, dbytes, dms = "k_decode<GATE_UP> (fused gate/up/activation)", gu_bytes, gu_avg
     else:
         dom, dbytes, dms = "k_decode<DOWN> (fused down/combine)", dn_bytes, dn_avg
@@ -457,19 +485,23 @@ def run_ours(args):
                    "l2": f"inputs larger than L2: ~{NL * k * model.record_raw / 1e9:.2f} GB of expert weights read "
                          f"per step vs 126 MB L2, no flush"},
         "e2e": results["e2e"],
-        "gpu_launches": 3 * NL * args.steps,
+        "gpu_launches": (1 if plan_info["stack_kernel"] else 3 * NL) * args.steps,
+        "plan": plan_info,
+        "layerwise_graph_tok_s": results["layerwise_graph_tok_s"],
         "layer_path_tok_s": results["layer_path_tok_s"],
         "hit_rate": results["hit_rate"],
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
                      "algorithmic_bytes_per_launch": dbytes, "avg_launch_ms": dms,
-                     "gate_up_avg_ms": gu_avg, "down_avg_ms": dn_avg, "timed_calls": calls},
+                     "layerwise": {"gate_up_avg_ms": gu_avg, "down_avg_ms": dn_avg, "timed_calls": calls,
+                                   "gate_up_gb_s": gu_bytes / (gu_avg / 1e3) / 1e9 if gu_avg else None,
+                                   "down_gb_s": dn_bytes / (dn_avg / 1e3) / 1e9 if dn_avg else None}},
         "prefill": results.get("prefill"),
         "sweep": sweep,
         "clocks": clocks,
         "setup_s": setup_s,
     }
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.cpu_sample_layers > 0:
         line["cpu_baseline"] = cpu_baseline(model, tier_np, (ids_all, w_all), xs, args.cpu_sample_layers)
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -48,6 +48,16 @@ class gx_serve_stats(C.Structure):
                 ("distinct", C.c_uint32), ("bytes_copied", C.c_uint64)]
 
 
+GX_PLAN_TIMING = 1
+GX_PLAN_LAYERWISE = 2
+
+
+class gx_stack_plan_info(C.Structure):
+    _fields_ = [("stack_kernel", C.c_int32), ("grid", C.c_int32), ("threads", C.c_int32),
+                ("ctas_per_sm", C.c_int32), ("stages", C.c_int32), ("rows_gate_up", C.c_int32),
+                ("rows_down", C.c_int32), ("smem_bytes", C.c_uint32)]
+
+
 class gx_arena_config(C.Structure):
     _fields_ = [("profile", gx_profile), ("capacity_bytes", C.c_uint64), ("protected_fraction", C.c_double),
                 ("policy", C.c_int), ("plan_quotas", C.POINTER(C.c_uint32)), ("device", C.c_int),
@@ -110,6 +120,7 @@ _SIGS = {
                                        C.POINTER(_P), C.POINTER(_P), _I64, _I64, C.c_int, C.POINTER(_P)]),
     "gx_stack_plan_run": (C.c_int, [_P, _P, _P, C.POINTER(gx_serve_stats)]),
     "gx_stack_plan_timing": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+    "gx_stack_plan_info_get": (C.c_int, [_P, C.POINTER(gx_stack_plan_info)]),
     "gx_stack_plan_destroy": (C.c_int, [_P]),
     "gx_moe_ffn_noalloc": (C.c_int, [C.POINTER(gx_layer_desc), _P, C.c_uint64, C.c_uint32, _P, _P, _P, _I64, _I64,
                                      _P, _P]),

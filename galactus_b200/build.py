@@ -20,7 +20,7 @@ GEN = CSRC / "_gen"
 LIB = PKG / "libgalactus_b200.so"
 
 SOURCES = ["gx_kernels.cu", "gx_capi.cpp", "gx_policy.cpp", "gx_noalloc.cu"]
-HEADERS = ["gx_device.cuh", "gx_moe.cuh", "gx_formats.h", "gx_kernels.h", "gx_policy.hpp"]
+HEADERS = ["gx_device.cuh", "gx_moe.cuh", "gx_stack.cuh", "gx_formats.h", "gx_kernels.h", "gx_policy.hpp"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

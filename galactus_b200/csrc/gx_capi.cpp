@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -804,7 +805,111 @@ struct gx_stack_plan {
     cudaEvent_t ev_graph = nullptr;
     int timing = 0;
     std::vector<cudaEvent_t> tev;
+    // persistent stack kernel
+    bool stack = false;
+    gx::StackParams sp{};
+    int grid = 0, threads = 0, per_sm = 0;
+    uint32_t smem = 0;
+    gx::StackLayer * d_layers = nullptr;
+    int32_t * d_cnt = nullptr;          // q_done [n] | gu_done [n*T] | per-block counters [n*T*k*I/qblk]
+    size_t cnt_bytes = 0;
+    uint8_t * d_xq = nullptr;
+    float * d_act = nullptr;
+    uint8_t * d_actq = nullptr;
 };
+
+namespace {
+
+// Tiling of the stack kernel: 8 gate/up rows per gate/up job, 32/k output
+// rows per down job, and as many consumer warps (= ring stages) as the
+// shared memory holds, at most kStackMaxConsumers; GX_STACK_CONSUMERS caps it.
+bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
+    if (sp.k <= 0 || 32 % sp.k != 0) return false;
+    sp.Rg = 8;
+    sp.Rd = 32 / sp.k;
+    int cap = gx::kStackMaxConsumers;
+    if (const char * env = std::getenv("GX_STACK_CONSUMERS")) {
+        const int v = std::atoi(env);
+        if (v >= 1 && v <= gx::kStackMaxConsumers) cap = v;
+    }
+    for (int C = cap; C >= 2; --C) {
+        sp.C = C;
+        smem = gx::stack_layout(sp, threads);
+        if (smem != 0) return true;
+    }
+    return false;
+}
+
+// Device buffers and the layer table of the stack kernel.
+int setup_stack(gx_stack_plan * p, const float * const * x, const float * const * w, float * const * out) {
+    gx_arena * a = p->a;
+    const LayerPlan & l0 = p->lps[0];
+    if (!gx::stack_types_supported(l0.type_gate, l0.type_down)) return GX_ERR_TYPE;
+    gx::StackParams sp{};
+    sp.NL = (int32_t)p->n;
+    sp.k = (int32_t)p->k;
+    sp.T = (int32_t)p->T;
+    sp.H = (int32_t)l0.H;
+    sp.I = (int32_t)l0.I;
+    sp.nb01_g = l0.g.nb01;
+    sp.nb01_d = l0.dn.nb01;
+    sp.alx = l0.g.al;
+    sp.ald = l0.g.al2;
+    sp.qblk = l0.g.qblk;
+    sp.act = l0.g.act;
+    sp.alpha = l0.g.alpha;
+    sp.limit = l0.g.limit;
+    int threads = 0;
+    uint32_t smem = 0;
+    if (!choose_stack_tiles(sp, threads, smem)) return GX_ERR_ALIGN;
+    sp.n_gu = (int32_t)(p->T * p->k * (l0.I / sp.Rg));
+    sp.n_d = (int32_t)(p->T * (l0.H / sp.Rd));
+    int per_sm = 0;
+    ck(gx::prepare_stack(l0.type_gate, l0.type_down, sp, threads, smem, per_sm));
+    if (per_sm > 1) per_sm = 1;   // one CTA per SM: the ring holds the SM's shared memory
+    const int64_t n = p->n, T = p->T, k = p->k;
+    const int64_t nblk = l0.I / sp.qblk;
+    p->cnt_bytes = (size_t)(n + n * T + n * T * k * nblk) * sizeof(int32_t);
+    ck(cudaMalloc(&p->d_cnt, p->cnt_bytes));
+    ck(cudaMemset(p->d_cnt, 0, p->cnt_bytes));
+    ck(cudaMalloc(&p->d_xq, (size_t)(n * T) * sp.alx.pitch));
+    ck(cudaMalloc(&p->d_act, (size_t)(n * T * k * l0.I) * sizeof(float)));
+    ck(cudaMalloc(&p->d_actq, (size_t)(n * T * k) * sp.ald.pitch));
+    std::vector<gx::StackLayer> table((size_t)n);
+    for (int64_t i = 0; i < n; ++i) {
+        const LayerPlan & lp = p->lps[(size_t)i];
+        gx::StackLayer & L = table[(size_t)i];
+        L.wg = lp.g.w0;
+        L.wu = lp.g.w1;
+        L.wd = lp.dn.w0;
+        L.x = x[i];
+        L.rw = w[i];
+        L.out = out[i];
+        L.slots = p->d_slots + i * k * T;
+        L.xq = p->d_xq + (size_t)(i * T) * sp.alx.pitch;
+        L.act = p->d_act + (size_t)(i * T * k) * l0.I;
+        L.actq = p->d_actq + (size_t)(i * T * k) * sp.ald.pitch;
+        L.cnt = p->d_cnt + n + n * T + i * T * k * nblk;
+        L.nb02 = lp.g.nb02;
+        L.n_as = lp.g.n_as;
+        L.pad = 0;
+    }
+    ck(cudaMalloc(&p->d_layers, table.size() * sizeof(gx::StackLayer)));
+    ck(cudaMemcpy(p->d_layers, table.data(), table.size() * sizeof(gx::StackLayer), cudaMemcpyHostToDevice));
+    sp.layers = p->d_layers;
+    sp.q_done = p->d_cnt;
+    sp.gu_done = p->d_cnt + n;
+    p->sp = sp;
+    p->threads = threads;
+    p->smem = smem;
+    p->per_sm = per_sm;
+    p->grid = per_sm * gx::device_sms();
+    p->stack = true;
+    (void)a;
+    return GX_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -853,15 +958,20 @@ int gx_stack_plan_destroy(gx_stack_plan * p) {
     if (p->ev_graph) cudaEventDestroy(p->ev_graph);
     if (p->d_slots) cudaFree(p->d_slots);
     for (auto h : p->h_slots) if (h) cudaFreeHost(h);
+    if (p->d_layers) cudaFree(p->d_layers);
+    if (p->d_cnt) cudaFree(p->d_cnt);
+    if (p->d_xq) cudaFree(p->d_xq);
+    if (p->d_act) cudaFree(p->d_act);
+    if (p->d_actq) cudaFree(p->d_actq);
     delete p;
     return GX_OK;
 }
 
 int gx_stack_plan_create(gx_arena * a, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * d,
                          const float * const * x, const float * const * w, float * const * out, int64_t k, int64_t T,
-                         int timing, gx_stack_plan ** out_plan) {
+                         int flags, gx_stack_plan ** out_plan) {
     if (a == nullptr || d == nullptr || x == nullptr || w == nullptr || out == nullptr || out_plan == nullptr ||
-        n_layers == 0)
+        n_layers == 0 || (flags & ~(GX_PLAN_TIMING | GX_PLAN_LAYERWISE)) != 0)
         return GX_ERR_INVALID;
     *out_plan = nullptr;
     gx_stack_plan * p = new (std::nothrow) gx_stack_plan();
@@ -869,13 +979,14 @@ int gx_stack_plan_create(gx_arena * a, uint32_t first_layer, uint32_t n_layers, 
     const int rc = guarded([&] {
         std::lock_guard<std::mutex> lock(a->mu);
         ck(cudaSetDevice(a->device));
+        const bool timing = (flags & GX_PLAN_TIMING) != 0;
         p->a = a;
         p->first = first_layer;
         p->n = n_layers;
         p->k = k;
         p->T = T;
         p->desc = *d;
-        p->timing = timing;
+        p->timing = timing ? 1 : 0;
         p->lps.resize(n_layers);
         for (uint32_t i = 0; i < n_layers; ++i) {
             const int r = plan_layer(a, first_layer + i, d, k, T, p->lps[i]);
@@ -889,21 +1000,37 @@ int gx_stack_plan_create(gx_arena * a, uint32_t first_layer, uint32_t n_layers, 
             ck(cudaEventCreateWithFlags(&p->ev_h[j], cudaEventDisableTiming));
         }
         ck(cudaEventCreateWithFlags(&p->ev_graph, cudaEventDisableTiming));
+        const bool want_stack = (flags & GX_PLAN_LAYERWISE) == 0 && k * T <= gx::kInlineIds &&
+                                gx::stack_types_supported(p->lps[0].type_gate, p->lps[0].type_down);
+        if (want_stack) {
+            const int r = setup_stack(p, x, w, out);
+            if (r != GX_OK) return r;
+        }
         if (timing) {
-            p->tev.resize((size_t)3 * n_layers);
+            p->tev.resize(p->stack ? 2 : (size_t)3 * n_layers);
             for (auto & e : p->tev) ck(cudaEventCreate(&e));
         }
         // warm every kernel configuration (attributes, occupancy) outside the capture
+        if (!p->stack) {
+            for (uint32_t i = 0; i < n_layers; ++i) {
+                ck(gx::prepare_decode(p->lps[i].type_gate, 1, p->lps[i].g));
+                ck(gx::prepare_decode(p->lps[i].type_down, 2, p->lps[i].dn));
+            }
+        }
         cudaStream_t cap;
         ck(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
-        for (uint32_t i = 0; i < n_layers; ++i) {
-            ck(gx::prepare_decode(p->lps[i].type_gate, 1, p->lps[i].g));
-            ck(gx::prepare_decode(p->lps[i].type_down, 2, p->lps[i].dn));
-        }
         ck(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));
-        for (uint32_t i = 0; i < n_layers; ++i) {
-            cudaEvent_t * tv = timing ? &p->tev[(size_t)3 * i] : nullptr;
-            enqueue_layer(p->lps[i], x[i], w[i], out[i], p->d_slots + (size_t)i * k * T, nullptr, cap, !timing, !timing, tv);
+        if (p->stack) {
+            ck(cudaMemsetAsync(p->d_cnt, 0, p->cnt_bytes, cap));
+            if (timing) ck(cudaEventRecordWithFlags(p->tev[0], cap, cudaEventRecordExternal));
+            ck(gx::launch_stack(p->lps[0].type_gate, p->lps[0].type_down, p->sp, p->grid, p->threads, p->smem, cap));
+            if (timing) ck(cudaEventRecordWithFlags(p->tev[1], cap, cudaEventRecordExternal));
+        } else {
+            for (uint32_t i = 0; i < n_layers; ++i) {
+                cudaEvent_t * tv = timing ? &p->tev[(size_t)3 * i] : nullptr;
+                enqueue_layer(p->lps[i], x[i], w[i], out[i], p->d_slots + (size_t)i * k * T, nullptr, cap, !timing,
+                              !timing, tv);
+            }
         }
         cudaGraph_t graph = nullptr;
         const cudaError_t ce = cudaStreamEndCapture(cap, &graph);
@@ -960,17 +1087,39 @@ int gx_stack_plan_timing(gx_stack_plan * p, double * gate_up_ms, double * down_m
     return guarded([&] {
         ck(cudaEventSynchronize(p->ev_graph));
         double gu = 0.0, dn = 0.0;
-        for (uint32_t i = 0; i < p->n; ++i) {
-            float m1 = 0.f, m2 = 0.f;
-            ck(cudaEventElapsedTime(&m1, p->tev[3 * i], p->tev[3 * i + 1]));
-            ck(cudaEventElapsedTime(&m2, p->tev[3 * i + 1], p->tev[3 * i + 2]));
-            gu += m1;
-            dn += m2;
+        if (p->stack) {
+            float m = 0.f;
+            ck(cudaEventElapsedTime(&m, p->tev[0], p->tev[1]));
+            gu = m;
+        } else {
+            for (uint32_t i = 0; i < p->n; ++i) {
+                float m1 = 0.f, m2 = 0.f;
+                ck(cudaEventElapsedTime(&m1, p->tev[3 * i], p->tev[3 * i + 1]));
+                ck(cudaEventElapsedTime(&m2, p->tev[3 * i + 1], p->tev[3 * i + 2]));
+                gu += m1;
+                dn += m2;
+            }
         }
         if (gate_up_ms) *gate_up_ms = gu;
         if (down_ms) *down_ms = dn;
         return GX_OK;
     });
+}
+
+int gx_stack_plan_info_get(const gx_stack_plan * p, gx_stack_plan_info * info) {
+    if (p == nullptr || info == nullptr) return GX_ERR_INVALID;
+    *info = gx_stack_plan_info{};
+    info->stack_kernel = p->stack ? 1 : 0;
+    if (p->stack) {
+        info->grid = p->grid;
+        info->threads = p->threads;
+        info->ctas_per_sm = p->per_sm;
+        info->stages = p->sp.C;
+        info->rows_gate_up = p->sp.Rg;
+        info->rows_down = p->sp.Rd;
+        info->smem_bytes = p->smem;
+    }
+    return GX_OK;
 }
 
 // --------------------------------------------------------------- synthetic

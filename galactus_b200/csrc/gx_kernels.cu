@@ -21,6 +21,7 @@
 #include "gx_device.cuh"
 #include "gx_kernels.h"
 #include "gx_moe.cuh"
+#include "gx_stack.cuh"
 
 namespace gx {
 
@@ -575,7 +576,7 @@ uint32_t decode_layout(int mode, DecodeParams & p, int & threads) {
     p.act_off = 128;
     p.stage_off = p.act_off + act_bytes;
     p.dots_off = p.stage_off + (uint32_t)S * p.stage_bytes;
-    p.flag_off = p.dots_off + (uint32_t)kDecodeMaxThreads / 8 * 4;
+    p.flag_off = p.dots_off + (uint32_t)kDecodeMaxThreads / 8 * 2 * 4;
     const uint32_t total = p.flag_off + 128;
     if (total > kMaxSmem) return 0;
     return total;
@@ -656,6 +657,79 @@ cudaError_t launch_quant_split(int vdt, const float * src, int ne0, int64_t nrow
     cfg.numAttrs = pdl ? 1 : 0;
     if (vdt == GX_T_Q8_0) return cudaLaunchKernelEx(&cfg, k_quant_split<GX_T_Q8_0>, src, ne0, nrows, nb1, dst, L);
     return cudaLaunchKernelEx(&cfg, k_quant_split<GX_T_Q8_K>, src, ne0, nrows, nb1, dst, L);
+}
+
+// ------------------------------------------------------- stack launcher
+
+int device_sms() { return device_sm_count(); }
+
+bool stack_types_supported(int type_gate, int type_down) { return type_gate == GX_T_Q8_0 && type_down == GX_T_Q8_0; }
+
+// Bulk-copy mode of one role: rows of a multiple of 128 bytes get 16 bytes of
+// padding against bank conflicts and one copy per row; other 16-byte rows
+// are copied as one tile per expert.
+static bool stack_copy_mode(int64_t nb01, int R, int32_t & row_copy, int32_t & pitch) {
+    if (nb01 % 16 != 0 || (R * nb01) % 16 != 0) return false;
+    row_copy = nb01 % 128 == 0 ? 1 : 0;
+    pitch = (int32_t)(row_copy ? nb01 + 16 : nb01);
+    return true;
+}
+
+// Shared-memory layout of the stack kernel; 0 when the shape is not covered.
+// Q8_0 jobs: 8 gate + 8 up rows (two lanes per row) or k*Rd = 32 down rows
+// (two rows per lane pair); rows of K % 256 == 0 elements, 16-byte aligned.
+uint32_t stack_layout(StackParams & p, int & threads) {
+    if (p.Rg != 8 || p.Rd < 1 || p.k * p.Rd != 32) return 0;
+    if (p.H % 256 || p.I % 256 || p.I % p.Rg || p.qblk % p.Rg || p.H % p.Rd) return 0;
+    if (p.C < 1 || p.C > kStackMaxConsumers) return 0;
+    threads = 64 + 32 * p.C;
+    if (!stack_copy_mode(p.nb01_g, p.Rg, p.row_copy_g, p.pitch_g)) return 0;
+    if (!stack_copy_mode(p.nb01_d, p.Rd, p.row_copy_d, p.pitch_d)) return 0;
+    const uint64_t gw = 2ull * p.Rg * (uint64_t)p.pitch_g, dw = (uint64_t)p.k * p.Rd * (uint64_t)p.pitch_d;
+    p.act_off_g = (int32_t)gw;
+    p.act_off_d = (int32_t)dw;
+    const uint64_t ga = gw + (uint64_t)p.alx.pitch, da = dw + (uint64_t)p.k * p.ald.pitch;
+    p.stage_bytes = (int32_t)align_up(ga > da ? ga : da, 128);
+    p.bar_off = 0;
+    p.stage_off = 256;   // 3*C mbarriers
+    p.scratch_off = p.stage_off + (uint32_t)p.C * (uint32_t)p.stage_bytes;
+    p.slots_off = p.scratch_off + (uint32_t)p.C * 64u * 4u;
+    const uint32_t total = p.slots_off + align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
+    return total <= kMaxSmem ? total : 0;
+}
+
+template <int TG, int TD>
+static cudaError_t stack_dispatch(const StackParams * p, int grid, int threads, uint32_t smem, cudaStream_t stream,
+                                  int * per_sm) {
+    if (per_sm) return resident_per_sm(k_stack<TG, TD>, threads, smem, *per_sm);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    // all CTAs must be resident at once: units wait on units of other CTAs
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_stack<TG, TD>, *p);
+}
+
+static cudaError_t stack_switch(int tg, int td, const StackParams * p, int grid, int threads, uint32_t smem,
+                                cudaStream_t stream, int * per_sm) {
+    if (tg == GX_T_Q8_0 && td == GX_T_Q8_0) return stack_dispatch<GX_T_Q8_0, GX_T_Q8_0>(p, grid, threads, smem, stream, per_sm);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t prepare_stack(int type_gate, int type_down, const StackParams & p, int threads, uint32_t smem, int & per_sm) {
+    per_sm = 0;
+    return stack_switch(type_gate, type_down, &p, 0, threads, smem, nullptr, &per_sm);
+}
+
+cudaError_t launch_stack(int type_gate, int type_down, const StackParams & p, int grid, int threads, uint32_t smem,
+                         cudaStream_t stream) {
+    return stack_switch(type_gate, type_down, &p, grid, threads, smem, stream, nullptr);
 }
 
 ActLayout act_layout_host(int vdt, int n) { return act_layout(vdt, n); }

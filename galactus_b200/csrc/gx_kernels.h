@@ -95,7 +95,55 @@ struct DecodeParams {
     uint32_t act_off, stage_off, dots_off, flag_off;
 };
 
+// ------------------------------------------------------------ stack kernel
 
+// One layer of a persistent stack launch (device-resident table).
+struct StackLayer {
+    const uint8_t * wg;        // gate role base of slot 0
+    const uint8_t * wu;        // up role base of slot 0
+    const uint8_t * wd;        // down role base of slot 0
+    const float * x;           // [T, H] input rows
+    const float * rw;          // [T, k] router weights
+    float * out;               // [T, H]
+    const int32_t * slots;     // [T, k] slot ids
+    uint8_t * xq;              // T split-layout rows of x (alx.pitch)
+    float * act;               // [T*k, I] activation (f32)
+    uint8_t * actq;            // T*k split-layout rows of act (ald.pitch)
+    int32_t * cnt;             // [T*k, I/qblk] gate/up units finished per Q8 block
+    int64_t nb02;              // record stride (bytes between slots)
+    int32_t n_as;              // slots of the layer
+    int32_t pad;
+};
+
+constexpr int kStackMaxConsumers = 8;
+
+struct StackParams {
+    const StackLayer * layers;
+    int32_t * q_done;          // [NL]   1 once x_L is quantized
+    int32_t * gu_done;         // [NL*T] gate/up jobs finished per token
+    int32_t NL, k, T, H, I;
+    int64_t nb01_g, nb01_d;    // gate/up and down row bytes
+    int32_t Rg;                // gate (and up) rows per gate/up job
+    int32_t Rd;                // output rows per down job (k*Rd weight rows)
+    int32_t C;                 // consumer warps per CTA = ring stages
+    int32_t row_copy_g, row_copy_d, pitch_g, pitch_d;
+    int32_t stage_bytes;       // weights then activation rows
+    int32_t act_off_g, act_off_d;   // activation offset inside a gate/up or down stage
+    ActLayout alx, ald;        // layouts of xq rows and actq rows
+    int32_t qblk;              // elements per Q8 block of the down input
+    int32_t n_gu, n_d;         // gate/up and down jobs per layer
+    int32_t act;
+    float alpha, limit;
+    uint32_t bar_off, stage_off, scratch_off, slots_off;
+};
+
+uint32_t stack_layout(StackParams & p, int & threads);
+bool stack_types_supported(int type_gate, int type_down);
+// Resident CTAs per SM of the stack kernel for this layout (0 on error).
+cudaError_t prepare_stack(int type_gate, int type_down, const StackParams & p, int threads, uint32_t smem, int & per_sm);
+cudaError_t launch_stack(int type_gate, int type_down, const StackParams & p, int grid, int threads, uint32_t smem,
+                         cudaStream_t stream);
+int device_sms();
 
 uint32_t decode_layout(int mode, DecodeParams & p, int & threads);
 cudaError_t launch_decode(int type, int mode, DecodeParams & p, cudaStream_t stream, bool pdl);

@@ -271,14 +271,16 @@ class StackPlan:
     """gx_stack_plan_*: a decode stack captured once in a CUDA graph."""
 
     def __init__(self, arena: "Arena", first_layer: int, n_layers: int, x_ptrs, w_ptrs, out_ptrs, k: int, T: int,
-                 timing: bool = False):
+                 timing: bool = False, layerwise: bool = False):
         self.arena, self.n, self.k, self.T = arena, n_layers, k, T
         xs = (C.c_void_p * n_layers)(*x_ptrs)
         ws = (C.c_void_p * n_layers)(*w_ptrs)
         os_ = (C.c_void_p * n_layers)(*out_ptrs)
         h = C.c_void_p()
         L.check(arena._lib.gx_stack_plan_create(arena.h, first_layer, n_layers, C.byref(arena.desc), xs, ws, os_, k, T,
-                                                1 if timing else 0, C.byref(h)), "gx_stack_plan_create")
+                                                (L.GX_PLAN_TIMING if timing else 0)
+                                                | (L.GX_PLAN_LAYERWISE if layerwise else 0),
+                                                C.byref(h)), "gx_stack_plan_create")
         self.h = h
         self.st = L.gx_serve_stats()
         self.fn = arena._lib.gx_stack_plan_run
@@ -289,7 +291,15 @@ class StackPlan:
             raise L.GxError(rc, "gx_stack_plan_run")
         return self.st
 
+    def info(self) -> dict:
+        """Launch shape: stack_kernel (one persistent kernel) or per-layer kernels."""
+        i = L.gx_stack_plan_info()
+        L.check(self.arena._lib.gx_stack_plan_info_get(self.h, C.byref(i)), "gx_stack_plan_info_get")
+        return {name: getattr(i, name) for name, _ in i._fields_}
+
     def timing(self) -> tuple[float, float]:
+        """(gate/up ms, down ms) summed over layers; the stack kernel reports
+        its whole duration as the first value and 0.0 as the second."""
         a, b = C.c_double(), C.c_double()
         L.check(self.arena._lib.gx_stack_plan_timing(self.h, C.byref(a), C.byref(b)), "gx_stack_plan_timing")
         return a.value, b.value

@@ -257,21 +257,44 @@ int gx_moe_stack_forward(gx_arena * arena, uint32_t first_layer, uint32_t n_laye
                          const float * const * x, const int32_t * ids, const float * const * w, int64_t k, int64_t T,
                          float * const * out, void * stream, gx_serve_stats * stats);
 
-/* A captured decode plan for a stack of layers: the three kernels of every
- * layer recorded once in a CUDA graph with fixed input, weight and output
- * pointers, slot ids read from a device array. Each run serves every layer
- * through the policy on the host (misses copied as in gx_moe_layer_forward),
- * copies the slot ids to the device and launches the graph. Same results as
- * gx_moe_stack_forward. With timing = 1 the graph records CUDA events around
- * each kernel (no programmatic overlap) and gx_stack_plan_timing returns the
- * summed gate/up and down kernel milliseconds of the last run.
+/* A captured decode plan for a stack of layers, recorded once in a CUDA graph
+ * with fixed input, weight and output pointers and slot ids read from a
+ * device array. Each run serves every layer through the policy on the host
+ * (misses copied as in gx_moe_layer_forward), copies the slot ids to the
+ * device and launches the graph. Same results as gx_moe_stack_forward.
+ *
+ * For decode sizes (k*T <= 64) and the weight-type pairs Q8_0/Q8_0,
+ * Q4_K/Q6_K, MXFP4/MXFP4 and IQ1_S/IQ1_S the graph holds ONE persistent
+ * cooperative kernel for all layers, which streams the expert rows of the
+ * whole stack through a bulk-copy ring with no drain between layers (it needs
+ * every layer's slot ids when it starts, which the plan's run provides).
+ * Otherwise, or with GX_PLAN_LAYERWISE, the graph holds the three kernels of
+ * every layer.
+ *
+ * flags: GX_PLAN_TIMING records CUDA events around the kernels (layerwise
+ * plans then run without programmatic overlap); gx_stack_plan_timing returns
+ * the summed gate/up and down kernel milliseconds of the last run, or, for
+ * the stack kernel, its whole duration in gate_up_ms and 0 in down_ms.
  * No reference counterpart: the reference has no device graph. */
+#define GX_PLAN_TIMING 1
+#define GX_PLAN_LAYERWISE 2
 typedef struct gx_stack_plan gx_stack_plan;
+typedef struct gx_stack_plan_info {
+    int32_t stack_kernel;     /* 1: one persistent kernel for the stack, 0: three kernels per layer */
+    int32_t grid;             /* CTAs of the stack kernel */
+    int32_t threads;          /* threads per CTA */
+    int32_t ctas_per_sm;
+    int32_t stages;           /* bulk-copy ring stages per CTA */
+    int32_t rows_gate_up;     /* gate (and up) rows per gate/up unit */
+    int32_t rows_down;        /* down rows per expert per down unit */
+    uint32_t smem_bytes;      /* dynamic shared memory per CTA */
+} gx_stack_plan_info;
 int gx_stack_plan_create(gx_arena * arena, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * desc,
                          const float * const * x, const float * const * w, float * const * out, int64_t k, int64_t T,
-                         int timing, gx_stack_plan ** plan);
+                         int flags, gx_stack_plan ** plan);
 int gx_stack_plan_run(gx_stack_plan * plan, const int32_t * ids, void * stream, gx_serve_stats * stats);
 int gx_stack_plan_timing(gx_stack_plan * plan, double * gate_up_ms, double * down_ms);
+int gx_stack_plan_info_get(const gx_stack_plan * plan, gx_stack_plan_info * info);
 int gx_stack_plan_destroy(gx_stack_plan * plan);
 
 /* ---------------------------------------------------------- no allocation

@@ -278,40 +278,89 @@ def test_remap_serve_strided_and_slot_bytes(gxlib, orc, dev):
     arena.close()
 
 
-@pytest.mark.parametrize("name", ["qwen3-30b", "olmoe", "gpt-oss-120b"])
-def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name):
-    """The captured decode plan (CUDA graph, slot ids from a device array,
-    programmatic overlap) gives the oracle's bits, with misses and evictions
-    between runs, and the per-layer C-ABI path gives the same bits."""
+@pytest.mark.parametrize("name,T,layers,layerwise", [
+    ("qwen3-30b", 1, 3, False), ("olmoe", 1, 3, False), ("gpt-oss-120b", 1, 3, False),
+    ("qwen3-235b", 1, 3, False), ("deepseek-v3", 1, 2, False), ("qwen3-30b", 1, 10, False),
+    ("qwen3-30b", 3, 3, False), ("gpt-oss-120b", 5, 3, False),
+    ("qwen3-30b", 1, 3, True), ("olmoe", 2, 3, True),
+])
+def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name, T, layers, layerwise):
+    """The captured decode plan (CUDA graph, slot ids from a device array) gives
+    the oracle's bits, with misses and evictions between runs (T = 1), and the
+    per-layer C-ABI path gives the same bits. Without GX_PLAN_LAYERWISE the
+    graph is the single persistent stack kernel, which streams every layer's
+    expert rows through one bulk-copy ring."""
     from galactus_b200.moe import StackCall, StackPlan
-    m = _small_model(gxlib, name, experts=12, layers=3)
+    m = _small_model(gxlib, name, experts=12, layers=layers)
     k = m.used
-    arena = gxlib.Arena(m, capacity_bytes=(k + 2) * m.record * m.layers, policy=gxlib.POLICY_AUTO, max_tokens=1)
+    slots = k + 2 if T == 1 else m.experts
+    arena = gxlib.Arena(m, capacity_bytes=slots * m.record * m.layers, policy=gxlib.POLICY_AUTO, max_tokens=T)
     recs = [np.stack([orc.synth_record(m, m.seed, L, e) for e in range(m.experts)]) for L in range(m.layers)]
     for L in range(m.layers):
         for e in range(m.experts):
             arena.load_record(L, e, recs[L][e])
-    x = torch.zeros((m.layers, m.hidden), dtype=torch.float32, device=dev)
-    w = torch.zeros((m.layers, k), dtype=torch.float32, device=dev)
-    out = torch.zeros((m.layers, m.hidden), dtype=torch.float32, device=dev)
+    x = torch.zeros((m.layers, T, m.hidden), dtype=torch.float32, device=dev)
+    w = torch.zeros((m.layers, T, k), dtype=torch.float32, device=dev)
+    out = torch.zeros((m.layers, T, m.hidden), dtype=torch.float32, device=dev)
     ptr = lambda t: [t[L].data_ptr() for L in range(m.layers)]
-    plan = StackPlan(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, 1)
-    call = StackCall(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, 1)
-    rng = np.random.default_rng(5)
+    plan = StackPlan(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, T, layerwise=layerwise)
+    info = plan.info()
+    stack_types = {(gxlib.TYPE_Q8_0, gxlib.TYPE_Q8_0)}
+    expect = not layerwise and (m.type_gate, m.type_down) in stack_types
+    assert info["stack_kernel"] == (1 if expect else 0), info
+    call = StackCall(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, T)
+    rng = np.random.default_rng(5 + T)
     stream = torch.cuda.current_stream()
     for step in range(6):
-        xs = rng.standard_normal((m.layers, m.hidden)).astype(np.float32)
-        ids = np.stack([_zipf_routes(rng, 1, m.experts, k)[0] for _ in range(m.layers)]).astype(np.int32)  # [L,1,k]
-        ws = rng.random((m.layers, k)).astype(np.float32)
+        xs = rng.standard_normal((m.layers, T, m.hidden)).astype(np.float32)
+        ids = np.stack([_zipf_routes(rng, T, m.experts, k)[0] for _ in range(m.layers)]).astype(np.int32)  # [L,T,k]
+        ws = rng.random((m.layers, T, k)).astype(np.float32)
         x.copy_(torch.from_numpy(xs))
         w.copy_(torch.from_numpy(ws))
+        out.fill_(float("nan"))
         runner = plan if step % 2 == 0 else call
         runner(np.ascontiguousarray(ids), stream)
         got = H(out)
+        no_device_error(gxlib)
         for L in range(m.layers):
-            want = orc.moe_layer(m, recs[L], xs[L][None], ids[L], ws[L][None])
-            np.testing.assert_array_equal(bits(got[L][None]), bits(want), err_msg=f"{name} step {step} layer {L}")
-    assert arena.stats()["misses"] > 0
+            want = orc.moe_layer(m, recs[L], xs[L], ids[L], ws[L])
+            np.testing.assert_array_equal(bits(got[L]), bits(want), err_msg=f"{name} T={T} step {step} layer {L}")
+    if T == 1:
+        assert arena.stats()["misses"] > 0
     no_device_error(gxlib)
     plan.close()
     arena.close()
+
+
+def test_stack_kernel_timing(gxlib, orc, dev):
+    """A timing plan of the stack kernel reports one positive duration (events
+    recorded inside the graph around the kernel) and the oracle's bits."""
+    from galactus_b200.moe import StackPlan
+    m = _small_model(gxlib, "qwen3-30b", experts=12, layers=2)
+    k = m.used
+    arena = gxlib.Arena(m, capacity_bytes=m.experts * m.record * m.layers, policy=gxlib.POLICY_AUTO, max_tokens=1)
+    recs = [np.stack([orc.synth_record(m, m.seed, L, e) for e in range(m.experts)]) for L in range(m.layers)]
+    for L in range(m.layers):
+        for e in range(m.experts):
+            arena.load_record(L, e, recs[L][e])
+    rng = np.random.default_rng(17)
+    xs = rng.standard_normal((m.layers, 1, m.hidden)).astype(np.float32)
+    ws = rng.random((m.layers, 1, k)).astype(np.float32)
+    x = torch.from_numpy(xs).to(dev)
+    w = torch.from_numpy(ws).to(dev)
+    out = torch.zeros((m.layers, 1, m.hidden), dtype=torch.float32, device=dev)
+    ptr = lambda t: [t[L].data_ptr() for L in range(m.layers)]
+    plan = StackPlan(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, 1, timing=True)
+    assert plan.info()["stack_kernel"] == 1
+    ids = np.stack([_zipf_routes(rng, 1, m.experts, k)[0] for _ in range(m.layers)]).astype(np.int32)
+    stream = torch.cuda.current_stream()
+    plan(np.ascontiguousarray(ids), stream)
+    torch.cuda.synchronize()
+    ms, zero = plan.timing()
+    assert ms > 0.0 and zero == 0.0
+    for L in range(m.layers):
+        want = orc.moe_layer(m, recs[L], xs[L], ids[L], ws[L])
+        np.testing.assert_array_equal(bits(H(out)[L]), bits(want))
+    plan.close()
+    arena.close()
+    no_device_error(gxlib)
