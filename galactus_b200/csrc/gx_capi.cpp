@@ -810,7 +810,6 @@ struct gx_stack_plan {
     gx::StackParams sp{};
     int grid = 0, threads = 0, per_sm = 0;
     uint32_t smem = 0;
-    gx::StackLayer * d_layers = nullptr;
     int32_t * d_cnt = nullptr;          // q_done [n] | gu_done [n*T] | per-block counters [n*T*k*I/qblk]
     size_t cnt_bytes = 0;
     uint8_t * d_xq = nullptr;
@@ -845,8 +844,11 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     gx_arena * a = p->a;
     const LayerPlan & l0 = p->lps[0];
     if (!gx::stack_types_supported(l0.type_gate, l0.type_down)) return GX_ERR_TYPE;
-    gx::StackParams sp{};
+    if (p->n > (uint32_t)gx::kStackMaxLayers) return GX_ERR_INVALID;
+    gx::StackParams & sp = p->sp;
+    sp = gx::StackParams{};
     sp.NL = (int32_t)p->n;
+    sp.skew = p->n >= 2 ? 2 : 1;
     sp.k = (int32_t)p->k;
     sp.T = (int32_t)p->T;
     sp.H = (int32_t)l0.H;
@@ -875,10 +877,9 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     ck(cudaMalloc(&p->d_xq, (size_t)(n * T) * sp.alx.pitch));
     ck(cudaMalloc(&p->d_act, (size_t)(n * T * k * l0.I) * sizeof(float)));
     ck(cudaMalloc(&p->d_actq, (size_t)(n * T * k) * sp.ald.pitch));
-    std::vector<gx::StackLayer> table((size_t)n);
     for (int64_t i = 0; i < n; ++i) {
         const LayerPlan & lp = p->lps[(size_t)i];
-        gx::StackLayer & L = table[(size_t)i];
+        gx::StackLayer & L = sp.layers[i];
         L.wg = lp.g.w0;
         L.wu = lp.g.w1;
         L.wd = lp.dn.w0;
@@ -894,12 +895,8 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
         L.n_as = lp.g.n_as;
         L.pad = 0;
     }
-    ck(cudaMalloc(&p->d_layers, table.size() * sizeof(gx::StackLayer)));
-    ck(cudaMemcpy(p->d_layers, table.data(), table.size() * sizeof(gx::StackLayer), cudaMemcpyHostToDevice));
-    sp.layers = p->d_layers;
     sp.q_done = p->d_cnt;
     sp.gu_done = p->d_cnt + n;
-    p->sp = sp;
     p->threads = threads;
     p->smem = smem;
     p->per_sm = per_sm;
@@ -958,7 +955,6 @@ int gx_stack_plan_destroy(gx_stack_plan * p) {
     if (p->ev_graph) cudaEventDestroy(p->ev_graph);
     if (p->d_slots) cudaFree(p->d_slots);
     for (auto h : p->h_slots) if (h) cudaFreeHost(h);
-    if (p->d_layers) cudaFree(p->d_layers);
     if (p->d_cnt) cudaFree(p->d_cnt);
     if (p->d_xq) cudaFree(p->d_xq);
     if (p->d_act) cudaFree(p->d_act);
@@ -1001,6 +997,7 @@ int gx_stack_plan_create(gx_arena * a, uint32_t first_layer, uint32_t n_layers, 
         }
         ck(cudaEventCreateWithFlags(&p->ev_graph, cudaEventDisableTiming));
         const bool want_stack = (flags & GX_PLAN_LAYERWISE) == 0 && k * T <= gx::kInlineIds &&
+                                n_layers <= (uint32_t)gx::kStackMaxLayers &&
                                 gx::stack_types_supported(p->lps[0].type_gate, p->lps[0].type_down);
         if (want_stack) {
             const int r = setup_stack(p, x, w, out);

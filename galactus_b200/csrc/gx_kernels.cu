@@ -681,18 +681,18 @@ static bool stack_copy_mode(int64_t nb01, int R, int32_t & row_copy, int32_t & p
 uint32_t stack_layout(StackParams & p, int & threads) {
     if (p.Rg != 8 || p.Rd < 1 || p.k * p.Rd != 32) return 0;
     if (p.H % 256 || p.I % 256 || p.I % p.Rg || p.qblk % p.Rg || p.H % p.Rd) return 0;
-    if (p.C < 1 || p.C > kStackMaxConsumers) return 0;
-    threads = 64 + 32 * p.C;
+    if (p.C < 1 || p.C > kStackMaxConsumers || p.NL < 1 || p.NL > kStackMaxLayers) return 0;
+    threads = 96 + 32 * p.C;
     if (!stack_copy_mode(p.nb01_g, p.Rg, p.row_copy_g, p.pitch_g)) return 0;
     if (!stack_copy_mode(p.nb01_d, p.Rd, p.row_copy_d, p.pitch_d)) return 0;
     const uint64_t gw = 2ull * p.Rg * (uint64_t)p.pitch_g, dw = (uint64_t)p.k * p.Rd * (uint64_t)p.pitch_d;
-    p.act_off_g = (int32_t)gw;
-    p.act_off_d = (int32_t)dw;
-    const uint64_t ga = gw + (uint64_t)p.alx.pitch, da = dw + (uint64_t)p.k * p.ald.pitch;
-    p.stage_bytes = (int32_t)align_up(ga > da ? ga : da, 128);
-    p.bar_off = 0;
-    p.stage_off = 256;   // 3*C mbarriers
-    p.scratch_off = p.stage_off + (uint32_t)p.C * (uint32_t)p.stage_bytes;
+    p.stage_bytes = (int32_t)align_up(gw > dw ? gw : dw, 128);
+    p.bar_off = 0;      // 3*C + 2*kStackBufs mbarriers
+    p.meta_off = 256;   // metadata word and release counter per stage, buffer counters
+    p.stage_off = 384;
+    p.xbuf_off = p.stage_off + (uint32_t)p.C * (uint32_t)p.stage_bytes;
+    p.dbuf_off = p.xbuf_off + align_up((uint64_t)kStackBufs * p.alx.pitch, 128);
+    p.scratch_off = p.dbuf_off + align_up((uint64_t)kStackBufs * p.k * p.ald.pitch, 128);
     p.slots_off = p.scratch_off + (uint32_t)p.C * 64u * 4u;
     const uint32_t total = p.slots_off + align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
     return total <= kMaxSmem ? total : 0;

@@ -116,9 +116,10 @@ struct StackLayer {
 };
 
 constexpr int kStackMaxConsumers = 8;
+constexpr int kStackMaxLayers = 128;   // the layer table travels in the kernel parameters
+constexpr int kStackBufs = 2;          // activation buffers per kind (gate/up inputs, down inputs)
 
 struct StackParams {
-    const StackLayer * layers;
     int32_t * q_done;          // [NL]   1 once x_L is quantized
     int32_t * gu_done;         // [NL*T] gate/up jobs finished per token
     int32_t NL, k, T, H, I;
@@ -126,15 +127,16 @@ struct StackParams {
     int32_t Rg;                // gate (and up) rows per gate/up job
     int32_t Rd;                // output rows per down job (k*Rd weight rows)
     int32_t C;                 // consumer warps per CTA = ring stages
+    int32_t skew;              // down jobs of layer L follow the gate/up jobs of layer L+skew
     int32_t row_copy_g, row_copy_d, pitch_g, pitch_d;
-    int32_t stage_bytes;       // weights then activation rows
-    int32_t act_off_g, act_off_d;   // activation offset inside a gate/up or down stage
+    int32_t stage_bytes;       // weight rows of one job
     ActLayout alx, ald;        // layouts of xq rows and actq rows
     int32_t qblk;              // elements per Q8 block of the down input
     int32_t n_gu, n_d;         // gate/up and down jobs per layer
     int32_t act;
     float alpha, limit;
-    uint32_t bar_off, stage_off, scratch_off, slots_off;
+    uint32_t bar_off, meta_off, stage_off, xbuf_off, dbuf_off, scratch_off, slots_off;
+    StackLayer layers[kStackMaxLayers];
 };
 
 uint32_t stack_layout(StackParams & p, int & threads);

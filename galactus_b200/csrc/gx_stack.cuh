@@ -3,24 +3,27 @@
 //
 // One cooperative launch (one CTA per SM) runs every layer of a micro-batch
 // whose slot ids are all known when it starts. The jobs of the stack form one
-// global list,
-//   [gate/up jobs of layer 0][gate/up jobs of layer 1][down jobs of layer 0]
-//   [gate/up jobs of layer 2][down jobs of layer 1] ... [down jobs of layer NL-1]
+// global list in which the down jobs of layer L follow the gate/up jobs of
+// layer L+skew:
+//   [GU(0)] .. [GU(skew-1)] [GU(skew)] [D(0)] [GU(skew+1)] [D(1)] ... [D(NL-1)]
 // and CTA b takes jobs b, b+G, b+2G, ... ; its j-th job uses ring stage j % C.
 // Inside a CTA:
 //   warp 0        weight producer: as soon as a stage is released, bulk-TMA
 //                 copies the expert rows of the CTA's next job into it. Weights
 //                 never depend on earlier jobs, so the HBM stream runs ahead
 //                 across job, half-layer and layer boundaries;
-//   warp 1        activation producer: waits until the job's input exists
-//                 (x_L quantized; every gate/up job of token t finished) and
-//                 copies the input rows into the same stage;
-//   warps 2..C+1  consumers: warp c computes the jobs of stage c, releases the
-//                 stage, then runs the job's epilogue (activation and its Q8
-//                 quantization, or the weighted combine).
-// The x_L quantization runs first, in the consumer warps of CTA L mod G.
-// There is no CTA-wide barrier after set-up: roles synchronize only through
-// mbarriers (full/empty per stage) and the global counters.
+//   warp 1        gate/up input producer: once per (layer, token) that the
+//                 CTA's jobs need, waits until x_L is quantized and copies the
+//                 row into one of two buffers; tells each job which buffer;
+//   warp 2        down input producer: the same for the k activation rows of
+//                 a token, after every gate/up job of that token finished;
+//   warps 3..C+2  consumers: warp c computes the jobs of stage c, releases the
+//                 stage and the input buffer, then runs the job's epilogue
+//                 (activation and its Q8 quantization, or the combine).
+// The x_L quantization runs first, in the consumer warps of CTA L mod G. The
+// layer table travels in the kernel parameters (constant bank), the slot ids
+// are copied to shared memory at the start. After set-up there is no
+// CTA-wide barrier: roles synchronize through mbarriers and counters.
 //
 // Deadlock freedom: a job waits only on jobs of an earlier half-layer; every
 // CTA issues and computes its jobs in increasing order and all CTAs are
@@ -57,6 +60,11 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 
 __device__ __forceinline__ uint4 lds128(const uint8_t * p) { return *reinterpret_cast<const uint4 *>(p); }
 
+// Release/acquire at GPU scope: orders this thread's (and, after a warp or
+// CTA barrier, its peers') earlier accesses before its later ones. The
+// publish/consume protocol of the kernel needs nothing stronger.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 // Bounded wait until *p reaches target (the counters only grow).
 __device__ __forceinline__ bool stack_wait(const int32_t * p, int32_t target) {
     for (uint32_t i = 0; i < (1u << 23); ++i) {
@@ -81,28 +89,30 @@ struct StackJob {
     int L, gu, t, r0, pair;
 };
 
-// Job order: [GU(0)] then, for B = 0..NL-1, [GU(B+1)] [D(B)]. The down jobs
-// of a layer come after the gate/up jobs of the next one, so a CTA reaches
-// them a whole gate/up phase after the jobs they wait on were issued.
 __device__ __forceinline__ StackJob stack_job(const StackParams & p, int j) {
     StackJob J;
     int w;
-    if (j < p.n_gu) {
-        J.L = 0;
+    const int d = p.skew;
+    const int seg = p.n_gu + p.n_d;
+    if (j < d * p.n_gu) {
+        J.L = j / p.n_gu;
         J.gu = 1;
-        w = j;
+        w = j - J.L * p.n_gu;
     } else {
-        const int seg = p.n_gu + p.n_d;
-        const int jj = j - p.n_gu;
-        const int B = jj / seg;
-        w = jj - B * seg;
-        if (B + 1 < p.NL && w < p.n_gu) {
-            J.L = B + 1;
-            J.gu = 1;
+        const int jj = j - d * p.n_gu;
+        const int full = p.NL - d;   // blocks [GU(B+d)][D(B)]
+        if (jj < full * seg) {
+            const int B = jj / seg;
+            w = jj - B * seg;
+            J.gu = w < p.n_gu;
+            J.L = J.gu ? B + d : B;
+            if (!J.gu) w -= p.n_gu;
         } else {
-            J.L = B;
+            const int jr = jj - full * seg;
+            const int B = jr / p.n_d;
+            J.L = full + B;
             J.gu = 0;
-            if (B + 1 < p.NL) w -= p.n_gu;
+            w = jr - B * p.n_d;
         }
     }
     if (J.gu) {
@@ -201,23 +211,109 @@ __device__ __forceinline__ void stack_issue_weights(const StackParams & p, const
     }
 }
 
+// Input producer of one kind (0: gate/up inputs x_L, 1: down inputs).
+// Walks the CTA's jobs in order; for each job of its kind it makes sure the
+// job's input rows are in one of kStackBufs buffers (one bulk copy per new
+// (layer, token)), writes the buffer index and fill parity into the stage's
+// metadata word and arrives on the stage's input barrier.
+//
+// A producer skips the jobs of the other kind, so it can be two or more
+// phases ahead of a stage's "empty" mbarrier, where a parity wait would be
+// ambiguous; it waits instead on the stage's release counter rel[s] (jobs of
+// stage s whose consumer released it), which only grows.
+__device__ __forceinline__ void stack_input_producer(const StackParams & p, int kind, int mine, int b, int G,
+                                                     volatile int * rel, uint64_t * afull, uint64_t * bbar,
+                                                     int * meta, volatile int * bufdone, uint8_t * buf, int buf_bytes) {
+    const int C = p.C;
+    const int gu_per_token = p.k * (p.I / p.Rg);
+    int key[kStackBufs], iss[kStackBufs], fills[kStackBufs];
+#pragma unroll
+    for (int i = 0; i < kStackBufs; ++i) {
+        key[i] = -1;
+        iss[i] = 0;
+        fills[i] = 0;
+    }
+    int cur = -1, next = 0;
+    for (int jl = 0; jl < mine; ++jl) {
+        const StackJob J = stack_job(p, b + jl * G);
+        if (J.gu != (kind == 0 ? 1 : 0)) continue;
+        const int s = jl % C, n = jl / C;
+        // job jl - C (the previous job of stage s) has been released
+        bool freed = n == 0;
+        for (uint32_t i = 0; i < (1u << 23) && !freed; ++i) {
+            freed = rel[s] >= n;
+            if (!freed && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+        }
+        if (!freed) {
+            record_error(GX_DEVERR_TIMEOUT);
+            break;
+        }
+        __threadfence_block();
+        const int k2 = J.L * p.T + J.t;
+        if (cur < 0 || key[cur] != k2) {
+            const int bi = next;
+            next = (next + 1) % kStackBufs;
+            // every job that used the buffer before is done with it
+            bool ok = false;
+            for (uint32_t i = 0; i < (1u << 23) && !ok; ++i) {
+                ok = bufdone[bi] >= iss[bi];
+                if (!ok && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+            }
+            if (ok) ok = kind == 0 ? stack_wait(p.q_done + J.L, 1) : stack_wait(p.gu_done + k2, gu_per_token);
+            if (!ok) {
+                record_error(GX_DEVERR_TIMEOUT);
+                break;
+            }
+            fence_acq_rel_gpu();
+            fence_proxy_async_global();
+            const StackLayer & ly = p.layers[J.L];
+            uint8_t * dst = buf + bi * buf_bytes;
+            if (kind == 0) {
+                tma_expect(bbar + bi, (uint32_t)p.alx.pitch);
+                tma_load(dst, ly.xq + (int64_t)J.t * p.alx.pitch, (uint32_t)p.alx.pitch, bbar + bi);
+            } else {
+                const uint32_t bytes = (uint32_t)(p.k * p.ald.pitch);
+                tma_expect(bbar + bi, bytes);
+                tma_load(dst, ly.actq + (int64_t)J.t * p.k * p.ald.pitch, bytes, bbar + bi);
+            }
+            key[bi] = k2;
+            ++fills[bi];
+            cur = bi;
+        }
+        ++iss[cur];
+        meta[s] = cur | (((fills[cur] - 1) & 1) << 8);
+        mbar_arrive(afull + s);
+    }
+    // copies in flight land before the CTA can exit
+#pragma unroll
+    for (int i = 0; i < kStackBufs; ++i)
+        if (fills[i] > 0) stack_mbar_wait(bbar + i, (uint32_t)((fills[i] - 1) & 1));
+}
+
 template <int TG, int TD>
-__global__ void __launch_bounds__(64 + 32 * kStackMaxConsumers, 1) k_stack(const StackParams p) {
+__global__ void __launch_bounds__(96 + 32 * kStackMaxConsumers, 1) k_stack(const __grid_constant__ StackParams p) {
     static_assert(TG == GX_T_Q8_0 && TD == GX_T_Q8_0, "stack kernel rows: Q8_0");
     extern __shared__ __align__(128) uint8_t smem[];
     const int C = p.C;
     uint64_t * wfull = reinterpret_cast<uint64_t *>(smem + p.bar_off);
     uint64_t * afull = wfull + C;
     uint64_t * empty = afull + C;
+    uint64_t * xbar = empty + C;            // kStackBufs input-buffer barriers per kind
+    uint64_t * dbar = xbar + kStackBufs;
+    int * meta = reinterpret_cast<int *>(smem + p.meta_off);
+    int * bufdone = meta + kStackMaxConsumers;       // [2][kStackBufs]
+    int * rel = bufdone + 2 * kStackBufs;             // [C] releases per stage
     uint8_t * stages = smem + p.stage_off;
+    uint8_t * xbuf = smem + p.xbuf_off;
+    uint8_t * dbuf = smem + p.dbuf_off;
+    const int xbytes = p.alx.pitch, dbytes = p.k * p.ald.pitch;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, b = blockIdx.x;
     const int NJ = p.NL * (p.n_gu + p.n_d);
     const int mine = b < NJ ? (NJ - b + G - 1) / G : 0;   // jobs of this CTA
-    const int gu_per_token = p.k * (p.I / p.Rg);
 
     // every slot id of the launch is checked before any load and kept in
-    // shared memory for the producer
+    // shared memory for the weight producer
     int32_t * slots = reinterpret_cast<int32_t *>(smem + p.slots_off);
     {
         int bad = 0;
@@ -228,13 +324,14 @@ __global__ void __launch_bounds__(64 + 32 * kStackMaxConsumers, 1) k_stack(const
             if (e < 0 || e >= p.layers[L].n_as) bad = 1;
             slots[j] = e;
         }
+        if (tid < 2 * kStackBufs + kStackMaxConsumers) bufdone[tid] = 0;   // bufdone and rel
         if (__syncthreads_or(bad)) {
             if (tid == 0) record_error(GX_DEVERR_DOMAIN);
             return;
         }
     }
     if (tid == 0) {
-        for (int s = 0; s < 3 * C; ++s) mbar_init(wfull + s, 1);
+        for (int s = 0; s < 3 * C + 2 * kStackBufs; ++s) mbar_init(wfull + s, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -259,43 +356,17 @@ __global__ void __launch_bounds__(64 + 32 * kStackMaxConsumers, 1) k_stack(const
                 stack_mbar_wait(wfull + jl % C, (uint32_t)((jl / C) & 1));
         return;
     }
-    if (warp == 1) {
-        // -------------------------------------------- activation producer
+    if (warp == 1 || warp == 2) {
+        // -------------------------------------------------- input producers
         if (lane != 0) return;
-        int issued = 0;
-        for (int jl = 0; jl < mine; ++jl) {
-            const int s = jl % C, n = jl / C;
-            if (n > 0 && !stack_mbar_wait(empty + s, (uint32_t)((n - 1) & 1))) {
-                record_error(GX_DEVERR_TIMEOUT);
-                break;
-            }
-            const StackJob J = stack_job(p, b + jl * G);
-            const StackLayer & ly = p.layers[J.L];
-            const bool ok = J.gu ? stack_wait(p.q_done + J.L, 1) : stack_wait(p.gu_done + J.L * p.T + J.t, gu_per_token);
-            if (!ok) {
-                record_error(GX_DEVERR_TIMEOUT);
-                break;
-            }
-            __threadfence();
-            fence_proxy_async_global();
-            uint8_t * st = stages + s * p.stage_bytes;
-            if (J.gu) {
-                tma_expect(afull + s, (uint32_t)p.alx.pitch);
-                tma_load(st + p.act_off_g, ly.xq + (int64_t)J.t * p.alx.pitch, (uint32_t)p.alx.pitch, afull + s);
-            } else {
-                const uint32_t bytes = (uint32_t)(p.k * p.ald.pitch);
-                tma_expect(afull + s, bytes);
-                tma_load(st + p.act_off_d, ly.actq + (int64_t)J.t * p.k * p.ald.pitch, bytes, afull + s);
-            }
-            ++issued;
-        }
-        for (int jl = issued - C > 0 ? issued - C : 0; jl < issued; ++jl)
-            stack_mbar_wait(afull + jl % C, (uint32_t)((jl / C) & 1));
+        const int kind = warp - 1;
+        stack_input_producer(p, kind, mine, b, G, rel, afull, kind == 0 ? xbar : dbar, meta,
+                             bufdone + kind * kStackBufs, kind == 0 ? xbuf : dbuf, kind == 0 ? xbytes : dbytes);
         return;
     }
 
     // ------------------------------------------------------------ consumers
-    const int c = warp - 2;
+    const int c = warp - 3;
     if (c >= C) return;
     // quantize the inputs of layers L = b, b+G, ... (one warp per Q8 block)
     {
@@ -314,7 +385,7 @@ __global__ void __launch_bounds__(64 + 32 * kStackMaxConsumers, 1) k_stack(const
             fence_proxy_async_global();
             named_barrier(1, 32 * C);
             if (c == 0 && lane == 0) {
-                __threadfence();
+                fence_acq_rel_gpu();
                 for (int L = b; L < p.NL; L += G) atomicExch(p.q_done + L, 1);
             }
         }
@@ -324,24 +395,35 @@ __global__ void __launch_bounds__(64 + 32 * kStackMaxConsumers, 1) k_stack(const
     for (int jl = c; jl < mine; jl += C) {
         const int n = jl / C;
         const uint32_t ph = (uint32_t)(n & 1);
-        const bool ok = stack_mbar_wait(wfull + c, ph) && stack_mbar_wait(afull + c, ph);
+        bool ok = stack_mbar_wait(wfull + c, ph) && stack_mbar_wait(afull + c, ph);
+        const StackJob J = stack_job(p, b + jl * G);
+        const int mt = ok ? *reinterpret_cast<volatile int *>(meta + c) : 0;
+        const int bi = mt & 0xff;
+        uint64_t * ibar = (J.gu ? xbar : dbar) + bi;
+        ok = ok && stack_mbar_wait(ibar, (uint32_t)(mt >> 8));
         if (__any_sync(0xffffffffu, !ok)) {
             if (lane == 0) record_error(GX_DEVERR_TIMEOUT);
             break;
         }
-        const StackJob J = stack_job(p, b + jl * G);
         const StackLayer & ly = p.layers[J.L];
         const uint8_t * st = stages + c * p.stage_bytes;
+        int * done = bufdone + (J.gu ? 0 : kStackBufs) + bi;
         if (J.gu) {
             // lane = par*16 + role*8 + i: gate (role 0) or up (role 1) row i
             const int row = lane & 15;
+            const uint8_t * xa = xbuf + bi * xbytes;
             const uint8_t * rb[1] = {st + row * p.pitch_g + 32 * par};
-            const uint8_t * ab[1] = {st + p.act_off_g + 32 * par};
-            const uint8_t * ad[1] = {st + p.act_off_g + p.alx.d_off};
+            const uint8_t * ab[1] = {xa + 32 * par};
+            const uint8_t * ad[1] = {xa + p.alx.d_off};
             float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
             q8_0_rows<1>(rb, ab, ad, par, p.H / 64, acc);
             __syncwarp();
-            if (lane == 0) mbar_arrive(empty + c);   // the stage is free
+            if (lane == 0) {
+                __threadfence_block();
+                atomicAdd(done, 1);
+                atomicAdd(rel + c, 1);
+                mbar_arrive(empty + c);   // stage and input buffer are free
+            }
             const float dot = q8_0_finish(acc[0]);
             const float up = __shfl_down_sync(0xffffffffu, dot, 8);
             const int nblk = p.I / p.qblk, blk = J.r0 / p.qblk;
@@ -352,19 +434,19 @@ __global__ void __launch_bounds__(64 + 32 * kStackMaxConsumers, 1) k_stack(const
             __syncwarp();
             int last = 0;
             if (lane == 0) {
-                __threadfence();
+                fence_acq_rel_gpu();
                 last = atomicAdd(ly.cnt + J.pair * nblk + blk, 1) == p.qblk / p.Rg - 1;
             }
             if (__shfl_sync(0xffffffffu, last, 0)) {
                 // this job finished the Q8 block last: quantize it
-                __threadfence();
+                fence_acq_rel_gpu();
                 quant_block_split<GX_T_Q8_0, true>(ly.act + (int64_t)J.pair * p.I, ly.actq + (int64_t)J.pair * p.ald.pitch,
                                                    p.ald, blk, lane);
                 fence_proxy_async_global();
                 __syncwarp();
             }
             if (lane == 0) {
-                __threadfence();
+                fence_acq_rel_gpu();
                 atomicAdd(p.gu_done + J.L * p.T + J.t, 1);
             }
         } else {
@@ -374,15 +456,21 @@ __global__ void __launch_bounds__(64 + 32 * kStackMaxConsumers, 1) k_stack(const
             // warp fall in distinct bank groups
             const int q = lane & 15;
             const int m0 = q / p.Rd, m1 = (q + 16) / p.Rd;
+            const uint8_t * da = dbuf + bi * dbytes;
             const uint8_t * rb[2] = {st + q * p.pitch_d + 32 * par, st + (q + 16) * p.pitch_d + 32 * par};
-            const uint8_t * a0 = st + p.act_off_d + m0 * p.ald.pitch;
-            const uint8_t * a1 = st + p.act_off_d + m1 * p.ald.pitch;
+            const uint8_t * a0 = da + m0 * p.ald.pitch;
+            const uint8_t * a1 = da + m1 * p.ald.pitch;
             const uint8_t * ab[2] = {a0 + 32 * par, a1 + 32 * par};
             const uint8_t * ad[2] = {a0 + p.ald.d_off, a1 + p.ald.d_off};
             float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
             q8_0_rows<2>(rb, ab, ad, par, p.I / 64, acc);
             __syncwarp();
-            if (lane == 0) mbar_arrive(empty + c);
+            if (lane == 0) {
+                __threadfence_block();
+                atomicAdd(done, 1);
+                atomicAdd(rel + c, 1);
+                mbar_arrive(empty + c);
+            }
             const float d0 = q8_0_finish(acc[0]);
             const float d1 = q8_0_finish(acc[1]);
             if (lane < 16) {
