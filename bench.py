@@ -53,11 +53,10 @@ def parse():
     ap.add_argument("--prefill", type=int, default=512, help="prefill tokens at full residency (0 to skip)")
     ap.add_argument("--cpu-sample-layers", type=int, default=3)
     ap.add_argument("--layers", type=int, default=0, help="fewer layers (small profiling cases only)")
-    ap.add_argument("--stack-tiles", default="", help="stack kernel tiling 'Rg,Rd,S,ctas_per_sm' (default: library's)")
-    a = ap.parse_args()
-    if a.stack_tiles:
-        os.environ["GX_STACK_TILES"] = a.stack_tiles
-    return a
+    ap.add_argument("--headline-only", action="store_true",
+                    help="time the headline and e2e lines only (profiling runs): skips the layerwise, per-layer-call "
+                         "and prefill comparison sections, which lie outside the timed region")
+    return ap.parse_args()
 
 
 def measured_peaks():
@@ -361,72 +360,79 @@ def run_ours(args):
                           "h2d_bytes_per_step": NL * H * 4 + NL * k * 4, "d2h_bytes_per_step": NL * H * 4}
 
         plan_info = plan.info()
+        results["layerwise_graph_tok_s"] = results["layer_path_tok_s"] = None
 
-        # ---------------- the same step as a graph of three kernels per layer
-        lplan = plan_for(arena, layerwise=True)
-        run_plan(lplan, 0, args.warmup)
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        run_plan(lplan, args.warmup, args.steps)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        results["layerwise_graph_tok_s"] = world * args.steps / (max_over_ranks(ev0.elapsed_time(ev1)) / 1e3)
-        lplan.close()
-
-        # ---------------- the same step through the per-layer C-ABI calls (no graph)
-        call = stack_for(arena)
-        tabs = ptr_tables(call)
-        run_steps(call, tabs, 0, args.warmup)
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        run_steps(call, tabs, args.warmup, args.steps)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        results["layer_path_tok_s"] = world * args.steps / (max_over_ranks(ev0.elapsed_time(ev1)) / 1e3)
-
-        # ---------------- kernel timing: CUDA events recorded inside the graphs
-        # around the stack kernel, and around each kernel of the layerwise graph
+        # ---------------- kernel timing: CUDA events recorded inside the graph
+        # around the stack kernel (the roofline's dominant kernel)
         kplan = plan_for(arena, timing=True)
         stack_ms = 0.0
         for i in range(args.steps):
             run_plan(kplan, args.warmup + i, 1)
             stack_ms += kplan.timing()[0]
         kplan.close()
-        tplan = plan_for(arena, timing=True, layerwise=True)
         gu_ms = dn_ms = 0.0
         calls = 0
-        for i in range(args.steps):
-            run_plan(tplan, args.warmup + i, 1)
-            a_, b_ = tplan.timing()
-            gu_ms += a_
-            dn_ms += b_
-            calls += NL
-        tplan.close()
-        err = device_error()
-        if err:
-            raise RuntimeError(f"device error {err}")
 
-        # ---------------- prefill at full residency
-        if args.prefill:
-            Tp = args.prefill
-            pid, pw = routes(model, Tp, NL, seed=4242 + rank, rho=0.7)
-            px = torch.from_numpy(rng.standard_normal((NL, Tp, H)).astype(np.float32)).to(dev)
-            pwd = torch.from_numpy(np.ascontiguousarray(pw.transpose(1, 0, 2))).to(dev)
-            pout = torch.empty((NL, Tp, H), dtype=torch.float32, device=dev)
-            pcall = StackCall(arena, 0, NL, [px[L].data_ptr() for L in range(NL)],
-                              [pwd[L].data_ptr() for L in range(NL)], [pout[L].data_ptr() for L in range(NL)], k, Tp)
-            pids = np.ascontiguousarray(pid.transpose(1, 0, 2))                      # [NL, Tp, k]
-            pcall(pids, stream)
+    with torch.cuda.stream(stream):
+        if not args.headline_only:
+            # ---------------- the same step as a graph of three kernels per layer
+            lplan = plan_for(arena, layerwise=True)
+            run_plan(lplan, 0, args.warmup)
             torch.cuda.synchronize()
-            reps = 2
             ev0.record(stream)
-            for _ in range(reps):
-                pcall(pids, stream)
+            run_plan(lplan, args.warmup, args.steps)
             ev1.record(stream)
             torch.cuda.synchronize()
-            pms = max_over_ranks(ev0.elapsed_time(ev1)) / reps
-            results["prefill"] = {"tokens": Tp, "tok_s": world * Tp / (pms / 1e3), "ms": pms}
-            del px, pwd, pout
+            results["layerwise_graph_tok_s"] = world * args.steps / (max_over_ranks(ev0.elapsed_time(ev1)) / 1e3)
+            lplan.close()
+
+            # ---------------- the same step through the per-layer C-ABI calls (no graph)
+            call = stack_for(arena)
+            tabs = ptr_tables(call)
+            run_steps(call, tabs, 0, args.warmup)
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            run_steps(call, tabs, args.warmup, args.steps)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            results["layer_path_tok_s"] = world * args.steps / (max_over_ranks(ev0.elapsed_time(ev1)) / 1e3)
+
+            # ---------------- per-kernel timing of the layerwise graph
+            tplan = plan_for(arena, timing=True, layerwise=True)
+            gu_ms = dn_ms = 0.0
+            calls = 0
+            for i in range(args.steps):
+                run_plan(tplan, args.warmup + i, 1)
+                a_, b_ = tplan.timing()
+                gu_ms += a_
+                dn_ms += b_
+                calls += NL
+            tplan.close()
+            err = device_error()
+            if err:
+                raise RuntimeError(f"device error {err}")
+
+            # ---------------- prefill at full residency
+            if args.prefill:
+                Tp = args.prefill
+                pid, pw = routes(model, Tp, NL, seed=4242 + rank, rho=0.7)
+                px = torch.from_numpy(rng.standard_normal((NL, Tp, H)).astype(np.float32)).to(dev)
+                pwd = torch.from_numpy(np.ascontiguousarray(pw.transpose(1, 0, 2))).to(dev)
+                pout = torch.empty((NL, Tp, H), dtype=torch.float32, device=dev)
+                pcall = StackCall(arena, 0, NL, [px[L].data_ptr() for L in range(NL)],
+                                  [pwd[L].data_ptr() for L in range(NL)], [pout[L].data_ptr() for L in range(NL)], k, Tp)
+                pids = np.ascontiguousarray(pid.transpose(1, 0, 2))                      # [NL, Tp, k]
+                pcall(pids, stream)
+                torch.cuda.synchronize()
+                reps = 2
+                ev0.record(stream)
+                for _ in range(reps):
+                    pcall(pids, stream)
+                ev1.record(stream)
+                torch.cuda.synchronize()
+                pms = max_over_ranks(ev0.elapsed_time(ev1)) / reps
+                results["prefill"] = {"tokens": Tp, "tok_s": world * Tp / (pms / 1e3), "ms": pms}
+                del px, pwd, pout
     plan.close()
     arena.close()
 

@@ -820,16 +820,22 @@ struct gx_stack_plan {
 namespace {
 
 // Tiling of the stack kernel: 8 gate/up rows per gate/up job, 32/k output
-// rows per down job, and as many consumer warps (= ring stages) as the
-// shared memory holds, at most kStackMaxConsumers; GX_STACK_CONSUMERS caps it.
+// rows per down job, as many ring stages as the shared memory holds (at most
+// kStackMaxConsumers; GX_STACK_STAGES caps it) and GX_STACK_WARPS consumer
+// warps (default 8).
 bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
     if (sp.k <= 0 || 32 % sp.k != 0) return false;
     sp.Rg = 8;
     sp.Rd = 32 / sp.k;
     int cap = gx::kStackMaxConsumers;
-    if (const char * env = std::getenv("GX_STACK_CONSUMERS")) {
+    if (const char * env = std::getenv("GX_STACK_STAGES")) {
         const int v = std::atoi(env);
         if (v >= 1 && v <= gx::kStackMaxConsumers) cap = v;
+    }
+    sp.W = 8;
+    if (const char * env = std::getenv("GX_STACK_WARPS")) {
+        const int v = std::atoi(env);
+        if (v >= 1 && v <= gx::kStackMaxWarps) sp.W = v;
     }
     for (int C = cap; C >= 2; --C) {
         sp.C = C;

@@ -682,18 +682,33 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     if (p.Rg != 8 || p.Rd < 1 || p.k * p.Rd != 32) return 0;
     if (p.H % 256 || p.I % 256 || p.I % p.Rg || p.qblk % p.Rg || p.H % p.Rd) return 0;
     if (p.C < 1 || p.C > kStackMaxConsumers || p.NL < 1 || p.NL > kStackMaxLayers) return 0;
-    threads = 96 + 32 * p.C;
-    if (!stack_copy_mode(p.nb01_g, p.Rg, p.row_copy_g, p.pitch_g)) return 0;
+    if (p.W < 1 || p.W > kStackMaxWarps) return 0;
+    threads = 96 + 32 * p.W;
+    if (p.nb01_g % 16 != 0) return 0;
     if (!stack_copy_mode(p.nb01_d, p.Rd, p.row_copy_d, p.pitch_d)) return 0;
-    const uint64_t gw = 2ull * p.Rg * (uint64_t)p.pitch_g, dw = (uint64_t)p.k * p.Rd * (uint64_t)p.pitch_d;
+    // gate/up tiles: tile t starts at a 16-byte chunk index = {0, 1, 4, 5}[t]
+    // mod 8; a quarter warp reads one row of each tile at both parities
+    // (+32 bytes), i.e. chunk groups {0,2}, {1,3}, {4,6}, {5,7}
+    {
+        static const int xs[4] = {0, 1, 4, 5};
+        const uint64_t tile = 4ull * (uint64_t)p.nb01_g;
+        p.gu_tile[0] = 0;
+        for (int t = 1; t < 4; ++t) {
+            uint64_t c = (p.gu_tile[t - 1] + tile + 15) / 16;
+            while (c % 8 != (uint64_t)xs[t]) ++c;
+            p.gu_tile[t] = (int32_t)(c * 16);
+        }
+    }
+    const uint64_t gw = (uint64_t)p.gu_tile[3] + 4ull * (uint64_t)p.nb01_g;
+    const uint64_t dw = (uint64_t)p.k * p.Rd * (uint64_t)p.pitch_d;
     p.stage_bytes = (int32_t)align_up(gw > dw ? gw : dw, 128);
     p.bar_off = 0;      // 3*C + 2*kStackBufs mbarriers
     p.meta_off = 256;   // metadata word and release counter per stage, buffer counters
     p.stage_off = 384;
     p.xbuf_off = p.stage_off + (uint32_t)p.C * (uint32_t)p.stage_bytes;
     p.dbuf_off = p.xbuf_off + align_up((uint64_t)kStackBufs * p.alx.pitch, 128);
-    p.scratch_off = p.dbuf_off + align_up((uint64_t)kStackBufs * p.k * p.ald.pitch, 128);
-    p.slots_off = p.scratch_off + (uint32_t)p.C * 64u * 4u;
+    p.wt_off = p.dbuf_off + align_up((uint64_t)kStackBufs * p.k * p.ald.pitch, 128);
+    p.slots_off = p.wt_off + (uint32_t)p.NL * 32u;   // per-layer weight bases
     const uint32_t total = p.slots_off + align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
     return total <= kMaxSmem ? total : 0;
 }

@@ -115,7 +115,8 @@ struct StackLayer {
     int32_t pad;
 };
 
-constexpr int kStackMaxConsumers = 8;
+constexpr int kStackMaxConsumers = 8;   // ring stages
+constexpr int kStackMaxWarps = 10;      // consumer warps
 constexpr int kStackMaxLayers = 128;   // the layer table travels in the kernel parameters
 constexpr int kStackBufs = 2;          // activation buffers per kind (gate/up inputs, down inputs)
 
@@ -126,16 +127,19 @@ struct StackParams {
     int64_t nb01_g, nb01_d;    // gate/up and down row bytes
     int32_t Rg;                // gate (and up) rows per gate/up job
     int32_t Rd;                // output rows per down job (k*Rd weight rows)
-    int32_t C;                 // consumer warps per CTA = ring stages
+    int32_t C;                 // ring stages
+    int32_t W;                 // consumer warps (may exceed C)
     int32_t skew;              // down jobs of layer L follow the gate/up jobs of layer L+skew
-    int32_t row_copy_g, row_copy_d, pitch_g, pitch_d;
+    int32_t row_copy_d, pitch_d;
+    int32_t gu_tile[4];        // gate/up job: 4 tiles of 4 rows (gate 0-3, 4-7, up 0-3, 4-7) at these
+                               // stage offsets, staggered so quarter-warp loads hit distinct bank groups
     int32_t stage_bytes;       // weight rows of one job
     ActLayout alx, ald;        // layouts of xq rows and actq rows
     int32_t qblk;              // elements per Q8 block of the down input
     int32_t n_gu, n_d;         // gate/up and down jobs per layer
     int32_t act;
     float alpha, limit;
-    uint32_t bar_off, meta_off, stage_off, xbuf_off, dbuf_off, scratch_off, slots_off;
+    uint32_t bar_off, meta_off, stage_off, xbuf_off, dbuf_off, wt_off, slots_off;
     StackLayer layers[kStackMaxLayers];
 };
 

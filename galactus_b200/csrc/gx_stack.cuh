@@ -89,7 +89,26 @@ struct StackJob {
     int L, gu, t, r0, pair;
 };
 
-__device__ __forceinline__ StackJob stack_job(const StackParams & p, int j) {
+// Job-list geometry, copied once into registers by every role.
+struct StackGeom {
+    int NL, n_gu, n_d, skew, tiles_g, tiles_d, Rg, Rd, k;
+};
+
+__device__ __forceinline__ StackGeom stack_geom(const StackParams & p) {
+    StackGeom g;
+    g.NL = p.NL;
+    g.n_gu = p.n_gu;
+    g.n_d = p.n_d;
+    g.skew = p.skew;
+    g.tiles_g = p.I / p.Rg;
+    g.tiles_d = p.H / p.Rd;
+    g.Rg = p.Rg;
+    g.Rd = p.Rd;
+    g.k = p.k;
+    return g;
+}
+
+__device__ __forceinline__ StackJob stack_job(const StackGeom & p, int j) {
     StackJob J;
     int w;
     const int d = p.skew;
@@ -116,18 +135,79 @@ __device__ __forceinline__ StackJob stack_job(const StackParams & p, int j) {
         }
     }
     if (J.gu) {
-        const int tiles = p.I / p.Rg;
-        J.pair = w / tiles;
-        J.r0 = (w - J.pair * tiles) * p.Rg;
+        J.pair = w / p.tiles_g;
+        J.r0 = (w - J.pair * p.tiles_g) * p.Rg;
         J.t = J.pair / p.k;
     } else {
-        const int tiles = p.H / p.Rd;
-        J.t = w / tiles;
-        J.r0 = (w - J.t * tiles) * p.Rd;
+        J.t = w / p.tiles_d;
+        J.r0 = (w - J.t * p.tiles_d) * p.Rd;
         J.pair = J.t * p.k;
     }
     return J;
 }
+
+// Weight bases of one layer, kept in shared memory for the weight producer.
+struct StackWeights {
+    const uint8_t * wg;
+    const uint8_t * wu;
+    const uint8_t * wd;
+    int64_t nb02;
+};
+
+// Row-copy geometry of the weight producer (registers).
+struct StackCopy {
+    int64_t nb01_g, nb01_d;
+    int pitch_d, row_copy_d, T, k, Rg, Rd;
+    int tile[4];
+};
+
+// The weight producer's walk over jobs b, b+G, b+2G, ... without divisions
+// by the segment lengths: segments are GU(0) .. GU(skew-1), then
+// [GU(B+skew)][D(B)] for B < NL-skew, then D(NL-skew) .. D(NL-1).
+struct StackWalk {
+    int seg, w;   // current segment and index inside it
+    __device__ __forceinline__ void kind(const StackGeom & g, int & L, int & gu) const {
+        const int d = g.skew, mid = 2 * (g.NL - d);
+        if (seg < d) {
+            L = seg;
+            gu = 1;
+        } else if (seg < d + mid) {
+            const int k = seg - d;
+            gu = (k & 1) == 0;
+            L = gu ? (k >> 1) + d : (k >> 1);
+        } else {
+            L = g.NL - d + (seg - d - mid);
+            gu = 0;
+        }
+    }
+    __device__ __forceinline__ int len(const StackGeom & g) const {
+        int L, gu;
+        kind(g, L, gu);
+        return gu ? g.n_gu : g.n_d;
+    }
+    __device__ __forceinline__ void advance(const StackGeom & g, int step) {
+        w += step;
+        for (int l = len(g); w >= l; l = len(g)) {
+            w -= l;
+            ++seg;
+            if (seg >= g.skew + 2 * (g.NL - g.skew) + g.skew) break;
+        }
+    }
+    __device__ __forceinline__ StackJob job(const StackGeom & g) const {
+        StackJob J;
+        kind(g, J.L, J.gu);
+        if (J.gu) {
+            J.pair = w / g.tiles_g;
+            J.r0 = (w - J.pair * g.tiles_g) * g.Rg;
+            J.t = J.pair / g.k;
+        } else {
+            J.t = w / g.tiles_d;
+            J.r0 = (w - J.t * g.tiles_d) * g.Rd;
+            J.pair = J.t * g.k;
+        }
+        return J;
+    }
+};
 
 // Q8_0 x Q8_0 rows of one parity: NR rows, row r against activation row r,
 // K/64 units (a multiple of four). rb[r] = row base + 32*p, ab[r] =
@@ -171,42 +251,37 @@ __device__ __forceinline__ float q8_0_finish(const float (&a)[4]) {
     return __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 16));
 }
 
-// Weight copies of job J into a stage, issued by the 32 lanes of the producer
-// warp in parallel (one copy per lane); slot ids come from shared memory.
-__device__ __forceinline__ void stack_issue_weights(const StackParams & p, const StackJob & J, const int32_t * slots,
-                                                    uint8_t * stage, uint64_t * bar, int lane) {
-    const StackLayer & ly = p.layers[J.L];
-    const int32_t * sl = slots + J.L * p.T * p.k;
+// the same with the parity lanes adjacent (lane and lane ^ 1)
+__device__ __forceinline__ float q8_0_finish_x1(const float (&a)[4]) {
+    const float s = __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
+    return __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
+}
+
+// Weight copies of job J into a stage, issued by one thread; slot ids and
+// the layer's weight bases come from shared memory.
+__device__ __forceinline__ void stack_issue_weights(const StackCopy & q, const StackJob & J, const int32_t * slots,
+                                                    const StackWeights * wt, uint8_t * stage, uint64_t * bar) {
+    const StackWeights ly = wt[J.L];
+    const int32_t * sl = slots + J.L * q.T * q.k;
     if (J.gu) {
-        const int64_t off = (int64_t)sl[J.pair] * ly.nb02 + (int64_t)J.r0 * p.nb01_g;
-        const uint32_t bytes = (uint32_t)(p.Rg * p.nb01_g);
-        if (lane == 0) tma_expect(bar, 2u * bytes);
-        __syncwarp();
-        if (p.row_copy_g) {
-            // copy i: role i / Rg, row i % Rg
-            for (int i = lane; i < 2 * p.Rg; i += 32) {
-                const int m = i / p.Rg, r = i - m * p.Rg;
-                tma_load(stage + i * p.pitch_g, (m == 0 ? ly.wg : ly.wu) + off + (int64_t)r * p.nb01_g,
-                         (uint32_t)p.nb01_g, bar);
-            }
-        } else if (lane < 2) {
-            tma_load(stage + lane * p.Rg * p.pitch_g, (lane == 0 ? ly.wg : ly.wu) + off, bytes, bar);
-        }
+        // 4 tiles of 4 rows: gate rows r0..r0+3, r0+4..r0+7, then up rows
+        const int64_t off = (int64_t)sl[J.pair] * ly.nb02 + (int64_t)J.r0 * q.nb01_g;
+        const uint32_t tile = (uint32_t)(4 * q.nb01_g);
+        tma_expect(bar, 4u * tile);
+        for (int t = 0; t < 4; ++t)
+            tma_load(stage + q.tile[t], (t < 2 ? ly.wg : ly.wu) + off + (int64_t)(t & 1) * tile, tile, bar);
     } else {
-        const uint32_t bytes = (uint32_t)(p.Rd * p.nb01_d);
-        if (lane == 0) tma_expect(bar, (uint32_t)p.k * bytes);
-        __syncwarp();
-        if (p.row_copy_d) {
-            for (int i = lane; i < p.k * p.Rd; i += 32) {
-                const int m = i / p.Rd, r = i - m * p.Rd;
-                tma_load(stage + i * p.pitch_d,
-                         ly.wd + (int64_t)sl[J.pair + m] * ly.nb02 + (int64_t)(J.r0 + r) * p.nb01_d, (uint32_t)p.nb01_d,
-                         bar);
+        const uint32_t bytes = (uint32_t)(q.Rd * q.nb01_d);
+        tma_expect(bar, (uint32_t)q.k * bytes);
+        for (int m = 0; m < q.k; ++m) {
+            const uint8_t * src = ly.wd + (int64_t)sl[J.pair + m] * ly.nb02 + (int64_t)J.r0 * q.nb01_d;
+            uint8_t * dst = stage + m * q.Rd * q.pitch_d;
+            if (q.row_copy_d) {
+                for (int r = 0; r < q.Rd; ++r)
+                    tma_load(dst + r * q.pitch_d, src + (int64_t)r * q.nb01_d, (uint32_t)q.nb01_d, bar);
+            } else {
+                tma_load(dst, src, bytes, bar);
             }
-        } else {
-            for (int m = lane; m < p.k; m += 32)
-                tma_load(stage + m * p.Rd * p.pitch_d, ly.wd + (int64_t)sl[J.pair + m] * ly.nb02 + (int64_t)J.r0 * p.nb01_d,
-                         bytes, bar);
         }
     }
 }
@@ -225,6 +300,7 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
                                                      volatile int * rel, uint64_t * afull, uint64_t * bbar,
                                                      int * meta, volatile int * bufdone, uint8_t * buf, int buf_bytes) {
     const int C = p.C;
+    const StackGeom g = stack_geom(p);
     const int gu_per_token = p.k * (p.I / p.Rg);
     int key[kStackBufs], iss[kStackBufs], fills[kStackBufs];
 #pragma unroll
@@ -234,9 +310,13 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
         fills[i] = 0;
     }
     int cur = -1, next = 0;
-    for (int jl = 0; jl < mine; ++jl) {
-        const StackJob J = stack_job(p, b + jl * G);
-        if (J.gu != (kind == 0 ? 1 : 0)) continue;
+    StackWalk walk{0, 0};
+    walk.advance(g, b);
+    for (int jl = 0; jl < mine; ++jl, walk.advance(g, G)) {
+        int jL, jgu;
+        walk.kind(g, jL, jgu);
+        if (jgu != (kind == 0 ? 1 : 0)) continue;
+        const StackJob J = walk.job(g);
         const int s = jl % C, n = jl / C;
         // job jl - C (the previous job of stage s) has been released
         bool freed = n == 0;
@@ -291,7 +371,7 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
 }
 
 template <int TG, int TD>
-__global__ void __launch_bounds__(96 + 32 * kStackMaxConsumers, 1) k_stack(const __grid_constant__ StackParams p) {
+__global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __grid_constant__ StackParams p) {
     static_assert(TG == GX_T_Q8_0 && TD == GX_T_Q8_0, "stack kernel rows: Q8_0");
     extern __shared__ __align__(128) uint8_t smem[];
     const int C = p.C;
@@ -315,6 +395,7 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxConsumers, 1) k_stack(const
     // every slot id of the launch is checked before any load and kept in
     // shared memory for the weight producer
     int32_t * slots = reinterpret_cast<int32_t *>(smem + p.slots_off);
+    StackWeights * wt = reinterpret_cast<StackWeights *>(smem + p.wt_off);
     {
         int bad = 0;
         const int per = p.T * p.k;
@@ -324,7 +405,15 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxConsumers, 1) k_stack(const
             if (e < 0 || e >= p.layers[L].n_as) bad = 1;
             slots[j] = e;
         }
-        if (tid < 2 * kStackBufs + kStackMaxConsumers) bufdone[tid] = 0;   // bufdone and rel
+        for (int L = tid; L < p.NL; L += blockDim.x) {
+            StackWeights w;
+            w.wg = p.layers[L].wg;
+            w.wu = p.layers[L].wu;
+            w.wd = p.layers[L].wd;
+            w.nb02 = p.layers[L].nb02;
+            wt[L] = w;
+        }
+        if (tid < 2 * kStackBufs + kStackMaxConsumers + 1) bufdone[tid] = 0;   // bufdone, rel, next job
         if (__syncthreads_or(bad)) {
             if (tid == 0) record_error(GX_DEVERR_DOMAIN);
             return;
@@ -338,22 +427,38 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxConsumers, 1) k_stack(const
 
     if (warp == 0) {
         // ------------------------------------------------ weight producer
-        int issued = 0;
+        if (lane != 0) return;
+        const StackGeom g = stack_geom(p);
+        StackCopy q;
+        q.nb01_g = p.nb01_g;
+        q.nb01_d = p.nb01_d;
+        q.pitch_d = p.pitch_d;
+        q.row_copy_d = p.row_copy_d;
+        q.T = p.T;
+        q.k = p.k;
+        q.Rg = p.Rg;
+        q.Rd = p.Rd;
+        for (int t = 0; t < 4; ++t) q.tile[t] = p.gu_tile[t];
+        const int stage_bytes = p.stage_bytes;
+        StackWalk walk{0, 0};
+        walk.advance(g, b);
+        int issued = 0, s = 0, n = 0;
         for (int jl = 0; jl < mine; ++jl) {
-            const int s = jl % C, n = jl / C;
-            bool ok = true;
-            if (n > 0 && lane == 0) ok = stack_mbar_wait(empty + s, (uint32_t)((n - 1) & 1));
-            if (!__shfl_sync(0xffffffffu, (int)ok, 0)) {
-                if (lane == 0) record_error(GX_DEVERR_TIMEOUT);
+            if (n > 0 && !stack_mbar_wait(empty + s, (uint32_t)((n - 1) & 1))) {
+                record_error(GX_DEVERR_TIMEOUT);
                 break;
             }
-            stack_issue_weights(p, stack_job(p, b + jl * G), slots, stages + s * p.stage_bytes, wfull + s, lane);
+            stack_issue_weights(q, walk.job(g), slots, wt, stages + s * stage_bytes, wfull + s);
             ++issued;
+            walk.advance(g, G);
+            if (++s == C) {
+                s = 0;
+                ++n;
+            }
         }
         // let the last copy of every stage land before the CTA can exit
-        if (lane == 0)
-            for (int jl = issued - C > 0 ? issued - C : 0; jl < issued; ++jl)
-                stack_mbar_wait(wfull + jl % C, (uint32_t)((jl / C) & 1));
+        for (int jl = issued - C > 0 ? issued - C : 0; jl < issued; ++jl)
+            stack_mbar_wait(wfull + jl % C, (uint32_t)((jl / C) & 1));
         return;
     }
     if (warp == 1 || warp == 2) {
@@ -366,15 +471,20 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxConsumers, 1) k_stack(const
     }
 
     // ------------------------------------------------------------ consumers
+    // W consumer warps take the CTA's jobs dynamically (a shared counter), so
+    // a warp busy with an epilogue never leaves a loaded stage idle; job jl
+    // still uses stage jl % C, and each stage is consumed in job order: the
+    // warp that takes job jl first waits until job jl - C was released.
+    const int W = p.W;
     const int c = warp - 3;
-    if (c >= C) return;
+    if (c >= W) return;
     // quantize the inputs of layers L = b, b+G, ... (one warp per Q8 block)
     {
         const int nblk = p.H / 32;
         bool any = false;
         for (int L = b; L < p.NL; L += G) {
             const StackLayer & ly = p.layers[L];
-            for (int wi = c; wi < p.T * nblk; wi += C) {
+            for (int wi = c; wi < p.T * nblk; wi += W) {
                 const int t = wi / nblk, ib = wi - t * nblk;
                 quant_block_split<GX_T_Q8_0, false>(ly.x + (int64_t)t * p.H, ly.xq + (int64_t)t * p.alx.pitch, p.alx, ib,
                                                     lane);
@@ -383,21 +493,36 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxConsumers, 1) k_stack(const
         }
         if (any) {
             fence_proxy_async_global();
-            named_barrier(1, 32 * C);
+            named_barrier(1, 32 * W);
             if (c == 0 && lane == 0) {
                 fence_acq_rel_gpu();
                 for (int L = b; L < p.NL; L += G) atomicExch(p.q_done + L, 1);
             }
         }
     }
-    float * scratch = reinterpret_cast<float *>(smem + p.scratch_off) + c * 64;
+    const StackGeom g = stack_geom(p);
     const int par = lane >> 4;   // block parity of this lane
-    for (int jl = c; jl < mine; jl += C) {
-        const int n = jl / C;
+    int * next_job = rel + kStackMaxConsumers;
+    for (;;) {
+        int jl = 0;
+        if (lane == 0) jl = atomicAdd(next_job, 1);
+        jl = __shfl_sync(0xffffffffu, jl, 0);
+        if (jl >= mine) break;
+        const int cs = jl % C, n = jl / C;
         const uint32_t ph = (uint32_t)(n & 1);
-        bool ok = stack_mbar_wait(wfull + c, ph) && stack_mbar_wait(afull + c, ph);
-        const StackJob J = stack_job(p, b + jl * G);
-        const int mt = ok ? *reinterpret_cast<volatile int *>(meta + c) : 0;
+        // the previous job of this stage was released: its phases completed
+        bool ok = true;
+        if (lane == 0) {
+            ok = n == 0;
+            for (uint32_t i = 0; i < (1u << 23) && !ok; ++i) {
+                ok = *reinterpret_cast<volatile int *>(rel + cs) >= n;
+                if (!ok && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+            }
+        }
+        ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+        ok = ok && stack_mbar_wait(wfull + cs, ph) && stack_mbar_wait(afull + cs, ph);
+        const StackJob J = stack_job(g, b + jl * G);
+        const int mt = ok ? *reinterpret_cast<volatile int *>(meta + cs) : 0;
         const int bi = mt & 0xff;
         uint64_t * ibar = (J.gu ? xbar : dbar) + bi;
         ok = ok && stack_mbar_wait(ibar, (uint32_t)(mt >> 8));
@@ -406,30 +531,32 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxConsumers, 1) k_stack(const
             break;
         }
         const StackLayer & ly = p.layers[J.L];
-        const uint8_t * st = stages + c * p.stage_bytes;
+        const uint8_t * st = stages + cs * p.stage_bytes;
         int * done = bufdone + (J.gu ? 0 : kStackBufs) + bi;
         if (J.gu) {
-            // lane = par*16 + role*8 + i: gate (role 0) or up (role 1) row i
-            const int row = lane & 15;
+            // lane = qr*8 + tile*2 + gp: row qr of tile `tile` (gate rows 4*tile+qr
+            // for tiles 0, 1; up rows 4*(tile-2)+qr for tiles 2, 3), block parity gp
+            const int qr = lane >> 3, tl = (lane >> 1) & 3, gp = lane & 1;
             const uint8_t * xa = xbuf + bi * xbytes;
-            const uint8_t * rb[1] = {st + row * p.pitch_g + 32 * par};
-            const uint8_t * ab[1] = {xa + 32 * par};
+            const uint8_t * rb[1] = {st + p.gu_tile[tl] + qr * (int)p.nb01_g + 32 * gp};
+            const uint8_t * ab[1] = {xa + 32 * gp};
             const uint8_t * ad[1] = {xa + p.alx.d_off};
             float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-            q8_0_rows<1>(rb, ab, ad, par, p.H / 64, acc);
+            q8_0_rows<1>(rb, ab, ad, gp, p.H / 64, acc);
             __syncwarp();
             if (lane == 0) {
                 __threadfence_block();
                 atomicAdd(done, 1);
-                atomicAdd(rel + c, 1);
-                mbar_arrive(empty + c);   // stage and input buffer are free
+                atomicAdd(rel + cs, 1);
+                mbar_arrive(empty + cs);   // stage and input buffer are free
             }
-            const float dot = q8_0_finish(acc[0]);
-            const float up = __shfl_down_sync(0xffffffffu, dot, 8);
+            const float dot = q8_0_finish_x1(acc[0]);
+            // gate row i = 4*tl + qr (tl < 2) pairs with up row i in tile tl + 2 (lane + 4)
+            const float up = __shfl_down_sync(0xffffffffu, dot, 4);
             const int nblk = p.I / p.qblk, blk = J.r0 / p.qblk;
-            if (lane < p.Rg) {
+            if (gp == 0 && tl < 2) {
                 const float a = p.act == 1 ? act_swiglu_oai(dot, up, p.alpha, p.limit) : act_swiglu(dot, up);
-                ly.act[(int64_t)J.pair * p.I + J.r0 + lane] = a;
+                ly.act[(int64_t)J.pair * p.I + J.r0 + 4 * tl + qr] = a;
             }
             __syncwarp();
             int last = 0;
@@ -468,23 +595,23 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxConsumers, 1) k_stack(const
             if (lane == 0) {
                 __threadfence_block();
                 atomicAdd(done, 1);
-                atomicAdd(rel + c, 1);
-                mbar_arrive(empty + c);
+                atomicAdd(rel + cs, 1);
+                mbar_arrive(empty + cs);
             }
             const float d0 = q8_0_finish(acc[0]);
             const float d1 = q8_0_finish(acc[1]);
-            if (lane < 16) {
-                scratch[q] = d0;
-                scratch[q + 16] = d1;
+            // output row rr = lane < Rd: weight row R = m*Rd + rr of expert m
+            // is d0 of lane R (R < 16) or d1 of lane R - 16
+            const float * wr = ly.rw + (int64_t)J.t * p.k;
+            float accf = 0.0f;
+            for (int mm = 0; mm < p.k; ++mm) {
+                const int R = mm * p.Rd + (lane < p.Rd ? lane : 0);
+                const float v0 = __shfl_sync(0xffffffffu, d0, R & 15);
+                const float v1 = __shfl_sync(0xffffffffu, d1, R & 15);
+                const float prod = __fmul_rn(R < 16 ? v0 : v1, lane < p.Rd ? wr[mm] : 0.0f);
+                accf = mm == 0 ? prod : __fadd_rn(accf, prod);
             }
-            __syncwarp();
-            if (lane < p.Rd) {
-                const float * wr = ly.rw + (int64_t)J.t * p.k;
-                float accf = __fmul_rn(scratch[lane], wr[0]);
-                for (int mm = 1; mm < p.k; ++mm) accf = __fadd_rn(accf, __fmul_rn(scratch[mm * p.Rd + lane], wr[mm]));
-                ly.out[(int64_t)J.t * p.H + J.r0 + lane] = accf;
-            }
-            __syncwarp();
+            if (lane < p.Rd) ly.out[(int64_t)J.t * p.H + J.r0 + lane] = accf;
         }
     }
 }
