@@ -44,7 +44,7 @@ L2_BYTES = 126 * 2 ** 20
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="qwen3-30b")
@@ -67,58 +67,83 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def pci_bus_id(torch, dev):
+    """NVML's PCI bus id string of a CUDA device (CUDA and NVML orders can differ)."""
+    try:
+        pr = torch.cuda.get_device_properties(dev)
+        return f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+    except Exception:
+        return None
+
+
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock and clock-event reasons sampled DURING the timed region: NVML
+    read-only queries polled every ~2 ms from a background thread (enough
+    samples even for a 20 ms region). Nothing is set."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+               "hw_power_brake": "nvmlClocksEventReasonHwPowerBrakeSlowdown"}
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, pci_bus_id: str | None = None):
         self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
+        self.pci = pci_bus_id
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.masks: dict[str, int] = {}
+        self._stop = threading.Event()
+        self.t = None
+        self.nv = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml as nv
+            nv.nvmlInit()
+            try:
+                h = nv.nvmlDeviceGetHandleByPciBusId(self.pci) if self.pci else nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            except Exception:
+                h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.nv, self.h = nv, h
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.masks = {k: getattr(nv, v, 0) for k, v in self.REASONS.items()}
+            self.t = threading.Thread(target=self._poll, daemon=True)
             self.t.start()
+            time.sleep(0.01)
         except Exception:
-            self.proc = None
+            self.nv = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _poll(self):
+        nv, h = self.nv, self.h
+        while not self._stop.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                     int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+            except Exception:
+                return
+            time.sleep(0.002)
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
+        self._stop.set()
+        if self.t:
+            self.t.join(timeout=2)
+        if self.nv:
             try:
-                self.proc.wait(timeout=5)
+                self.nv.nvmlShutdown()
             except Exception:
-                self.proc.kill()
+                pass
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = set()
+        for _, mask in self.samples:
+            for name, bit in self.masks.items():
+                if bit and (mask & bit):
+                    reasons.add(name)
+        sm = [c for c, _ in self.samples]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvml"}
 
 
 # ------------------------------------------------------------ CPU baseline
@@ -329,7 +354,7 @@ def run_ours(args):
         torch.cuda.synchronize()
         barrier()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local) as clk:
+        with ClockSampler(local, pci_bus_id(torch, dev)) as clk:
             torch.cuda.synchronize()
             ev0.record(stream)
             h, m = run_plan(plan, args.warmup, args.steps)
