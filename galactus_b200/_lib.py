@@ -14,7 +14,7 @@ GX_OK = 0
 STATUS = {
     0: "GX_OK", -1: "GX_ERR_INVALID", -2: "GX_ERR_TYPE", -3: "GX_ERR_ALIGN", -4: "GX_ERR_DOMAIN",
     -5: "GX_ERR_BATCH", -6: "GX_ERR_SLOTS", -7: "GX_ERR_CUDA", -8: "GX_ERR_TIMEOUT", -9: "GX_ERR_NOMEM",
-    -10: "GX_ERR_COPY", -11: "GX_ERR_STATE", -12: "GX_ERR_DEVICE",
+    -10: "GX_ERR_COPY", -11: "GX_ERR_STATE", -12: "GX_ERR_DEVICE", -13: "GX_ERR_COMM",
 }
 for _code, _name in STATUS.items():
     globals()[_name] = _code
@@ -48,6 +48,7 @@ class gx_serve_stats(C.Structure):
                 ("distinct", C.c_uint32), ("bytes_copied", C.c_uint64)]
 
 
+GX_EP_MODULO, GX_EP_BLOCK = 0, 1
 GX_PLAN_TIMING = 1
 GX_PLAN_LAYERWISE = 2
 
@@ -122,6 +123,15 @@ _SIGS = {
     "gx_stack_plan_timing": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "gx_stack_plan_info_get": (C.c_int, [_P, C.POINTER(gx_stack_plan_info)]),
     "gx_stack_plan_destroy": (C.c_int, [_P]),
+    "gx_ep_owner": (C.c_int, [C.c_int32, C.c_uint32, C.c_int32, C.c_int32, _P, _P]),
+    "gx_ep_plan": (C.c_int, [C.c_int32, C.c_uint32, C.c_int32, _P, _I64, _I64, _P, _P]),
+    "gx_ep_init": (C.c_int, [_P, _P, C.c_int32, C.c_int32, C.c_uint32, C.c_int32, C.POINTER(_P)]),
+    "gx_ep_destroy": (C.c_int, [_P]),
+    "gx_ep_dispatch": (C.c_int, [_P, C.c_uint32, _P, _P, _I64, _I64, _I64, _P]),
+    "gx_ep_compute": (C.c_int, [_P, C.POINTER(gx_layer_desc), _P, C.POINTER(gx_serve_stats)]),
+    "gx_ep_combine": (C.c_int, [_P, _P, _P, _P]),
+    "gx_ep_layer_forward": (C.c_int, [_P, C.c_uint32, C.POINTER(gx_layer_desc), _P, _P, _P, _I64, _I64, _P, _P,
+                                      C.POINTER(gx_serve_stats)]),
     "gx_moe_ffn_noalloc": (C.c_int, [C.POINTER(gx_layer_desc), _P, C.c_uint64, C.c_uint32, _P, _P, _P, _I64, _I64,
                                      _P, _P]),
     "gx_synth_normal": (C.c_int, [_P, _I64, C.c_uint64, C.c_uint64, C.c_float, _P]),

@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 GEN = CSRC / "_gen"
 LIB = PKG / "libgalactus_b200.so"
 
-SOURCES = ["gx_kernels.cu", "gx_capi.cpp", "gx_policy.cpp", "gx_noalloc.cu"]
+SOURCES = ["gx_kernels.cu", "gx_capi.cpp", "gx_policy.cpp", "gx_noalloc.cu", "gx_ep.cpp"]
 HEADERS = ["gx_device.cuh", "gx_moe.cuh", "gx_stack.cuh", "gx_formats.h", "gx_kernels.h", "gx_policy.hpp"]
 
 NVCC_FLAGS = [
@@ -81,7 +81,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         subprocess.run(cmd, check=True)
         objs.append(str(obj))
     cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-cudart", "static",
-           "-o", str(LIB), *objs, "-lpthread"]
+           "-o", str(LIB), *objs, "-lpthread", "-ldl"]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)

@@ -161,6 +161,7 @@ const char * gx_status_string(int status) {
         case GX_ERR_COPY: return "host->HBM copy failed";
         case GX_ERR_STATE: return "call out of order";
         case GX_ERR_DEVICE: return "a kernel reported an error";
+        case GX_ERR_COMM: return "an NCCL call failed or NCCL could not be loaded";
         default: return "unknown status";
     }
 }

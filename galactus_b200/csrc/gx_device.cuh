@@ -490,7 +490,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t b
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
-// bulk copy global -> shared, completion counted on the mbarrier (no multicast)
+// bulk copy global -> shared of this CTA, completion counted on the mbarrier
 __device__ __forceinline__ void bulk_g2s(void * dst_smem, const void * src_gmem, uint32_t bytes, uint64_t * bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst_smem)),

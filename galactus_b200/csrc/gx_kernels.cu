@@ -200,6 +200,28 @@ __global__ void k_combine(const float * y, const float * w, float * out, int64_t
     }
 }
 
+// ------------------------------------------------------- row gather/scatter
+// dst[i] = src[idx[i]] (gather) or dst[idx[i]] = src[i] (scatter), rows of
+// H floats, 16-byte vectors when H % 4 == 0 (expert-parallel dispatch and
+// combine staging).
+__global__ void k_move_rows(const float * src, const int32_t * idx, int64_t n, int64_t H, float * dst, int scatter) {
+    const int64_t per = (H % 4 == 0) ? H / 4 : H;
+    const int64_t total = n * per;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / per, c = i - r * per;
+        const int64_t sr = scatter ? r : idx[r], dr = scatter ? idx[r] : r;
+        if (H % 4 == 0) {
+            reinterpret_cast<float4 *>(dst + dr * H)[c] = reinterpret_cast<const float4 *>(src + sr * H)[c];
+        } else {
+            dst[dr * H + c] = src[sr * H + c];
+        }
+    }
+}
+
+__global__ void k_fill(float * dst, int64_t n, float v) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) dst[i] = v;
+}
+
 // ----------------------------------------------------------- synthetic data
 // Counter-based generator (splitmix64 finaliser of Steele, Lea & Flood 2014),
 // N(0,1) approximated by the standardised sum of four 16-bit uniforms
@@ -464,6 +486,20 @@ cudaError_t launch_expf(const float * x, float * y, int64_t n, cudaStream_t stre
 cudaError_t launch_combine(const float * y, const float * w, float * out, int64_t H, int k, int64_t T, cudaStream_t stream) {
     if (H * T <= 0) return cudaSuccess;
     k_combine<<<grid_1d(H * T, 256), 256, 0, stream>>>(y, w, out, H, k, T);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_move_rows(const float * src, const int32_t * idx, int64_t n, int64_t H, float * dst, bool scatter,
+                             cudaStream_t stream) {
+    if (n <= 0 || H <= 0) return cudaSuccess;
+    const int64_t per = (H % 4 == 0) ? H / 4 : H;
+    k_move_rows<<<grid_1d(n * per, 256), 256, 0, stream>>>(src, idx, n, H, dst, scatter ? 1 : 0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fill(float * dst, int64_t n, float v, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    k_fill<<<grid_1d(n, 256), 256, 0, stream>>>(dst, n, v);
     return cudaGetLastError();
 }
 

@@ -166,6 +166,9 @@ cudaError_t launch_swiglu_oai(const float * g, const float * u, float * out, int
                               cudaStream_t stream);
 cudaError_t launch_expf(const float * x, float * y, int64_t n, cudaStream_t stream);
 cudaError_t launch_combine(const float * y, const float * w, float * out, int64_t H, int k, int64_t T, cudaStream_t stream);
+cudaError_t launch_move_rows(const float * src, const int32_t * idx, int64_t n, int64_t H, float * dst, bool scatter,
+                             cudaStream_t stream);
+cudaError_t launch_fill(float * dst, int64_t n, float v, cudaStream_t stream);
 cudaError_t launch_synth_normal(float * dst, int64_t n, uint64_t seed, uint64_t stream_id, float sigma, cudaStream_t stream);
 cudaError_t launch_synth_weights(int type, void * dst, int64_t ne00, int64_t n_rows, uint64_t seed, uint64_t stream_id,
                                  float sigma, cudaStream_t stream);

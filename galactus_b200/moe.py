@@ -316,6 +316,59 @@ class StackPlan:
             pass
 
 
+def ep_owner(placement: int, n_expert: int, world: int, expert: int) -> tuple[int, int]:
+    """(rank, local id) of a global expert under an expert-parallel placement."""
+    r, l = C.c_int32(), C.c_int32()
+    L.check(L.lib().gx_ep_owner(placement, n_expert, world, expert, C.byref(r), C.byref(l)), "gx_ep_owner")
+    return r.value, l.value
+
+
+def ep_plan(placement: int, n_expert: int, world: int, ids: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Per-destination pair counts and the pair indices t*k+s grouped by destination."""
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    T, k = ids.shape
+    counts = np.zeros(world, np.int32)
+    pairs = np.zeros(T * k, np.int32)
+    L.check(L.lib().gx_ep_plan(placement, n_expert, world, ids.ctypes.data, k, T, counts.ctypes.data,
+                               pairs.ctypes.data), "gx_ep_plan")
+    return counts, pairs
+
+
+class ExpertParallel:
+    """gx_ep_*: expert-parallel layer steps over an NCCL communicator.
+    `arena` holds this rank's experts (local ids); `comm` is an ncclComm_t
+    address, e.g. the NCCL process group's ``_comm_ptr()``."""
+
+    def __init__(self, arena: "Arena", comm: int, rank: int, world: int, n_expert: int,
+                 placement: int = L.GX_EP_MODULO):
+        self.arena = arena
+        h = C.c_void_p()
+        L.check(arena._lib.gx_ep_init(arena.h, C.c_void_p(comm), rank, world, n_expert, placement, C.byref(h)),
+                "gx_ep_init")
+        self.h = h
+        self.st = L.gx_serve_stats()
+
+    def layer_forward(self, layer: int, x, ids: np.ndarray, w, out, stream=None) -> L.gx_serve_stats:
+        """x [T, H] device f32, ids [T, k] HOST global expert ids, w [T, k] device, out [T, H] device."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        T, k = ids.shape
+        L.check(self.arena._lib.gx_ep_layer_forward(self.h, layer, C.byref(self.arena.desc), _ptr(x), ids.ctypes.data,
+                                                    _ptr(w), k, T, _ptr(out), _stream(stream), C.byref(self.st)),
+                "gx_ep_layer_forward")
+        return self.st
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.arena._lib.gx_ep_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def mul_mat_id(type_: int, as_, ne00: int, ne01: int, nb01: int, nb02: int, n_as: int,
                b, ne11: int, ne12: int, nb11: int, nb12: int,
                ids, ne20: int, ne21: int, nbi1: int, dst, stream=None) -> None:

@@ -42,6 +42,7 @@ extern "C" {
 #define GX_ERR_COPY      -10  /* a host->HBM miss copy failed */
 #define GX_ERR_STATE     -11  /* call out of order (e.g. no host tier) */
 #define GX_ERR_DEVICE    -12  /* a kernel reported an error (see gx_device_error) */
+#define GX_ERR_COMM      -13  /* an NCCL call failed or NCCL could not be loaded */
 
 /* ggml type ids (ggml.h numbering) of the formats this library computes on */
 #define GX_TYPE_Q8_0   8
@@ -321,6 +322,53 @@ int gx_stack_plan_destroy(gx_stack_plan * plan);
 int gx_moe_ffn_noalloc(const gx_layer_desc * desc, const void * slot0_record, uint64_t record_bytes, uint32_t n_slots,
                        const float * x, const int32_t * slots, const float * w, int64_t k, int64_t T, float * out,
                        void * stream);
+
+/* ------------------------------------------------------- expert parallel
+ * The experts of a model shard over G ranks, one process per GPU: expert e
+ * lives on rank e % G (GX_EP_MODULO) or e / ceil(E/G) (GX_EP_BLOCK), where
+ * its local id is e / G, respectively e - rank*ceil(E/G). Each rank owns an
+ * arena over its local experts (created as usual, with n_expert = the local
+ * count and max_tokens >= the pairs it may receive per layer). A layer step
+ * for the rank's own T tokens:
+ *   dispatch   every (token, slot) pair sends the token's input row and the
+ *              global expert id to the expert's rank (NCCL send/recv, one
+ *              group per step; pairs of local experts stay local);
+ *   compute    the received pairs run the routed-expert FFN on the local
+ *              arena (remap with local ids, gate/up, activation, down) with
+ *              one slot each and unit router weight, i.e. the bare down
+ *              output of each pair;
+ *   combine    each pair's output row goes back to its home rank, which
+ *              sums w[t,s]*y[t,s] in slot order s = 0..k-1 (the single-GPU
+ *              combine, so results are bit-identical to one GPU holding all
+ *              experts).
+ * nccl_comm is an ncclComm_t of the caller covering exactly the G ranks with
+ * this rank numbering (e.g. the communicator of torch's NCCL process group);
+ * the library calls ncclGroupStart/End, ncclSend and ncclRecv from the NCCL
+ * already loaded in the process (or libnccl.so.2, or GX_NCCL_LIB).
+ * gx_ep_plan is the host-only routing step: the pairs this rank sends to each
+ * peer, in (token, slot) order grouped by destination rank.
+ * No counterpart in the reference (it runs on one machine). */
+#define GX_EP_MODULO 0
+#define GX_EP_BLOCK 1
+typedef struct gx_ep gx_ep;
+int gx_ep_owner(int32_t placement, uint32_t n_expert, int32_t world, int32_t expert, int32_t * rank, int32_t * local_id);
+int gx_ep_plan(int32_t placement, uint32_t n_expert, int32_t world, const int32_t * ids, int64_t k, int64_t T,
+               int32_t * send_counts, int32_t * send_pairs);
+int gx_ep_init(gx_arena * local_arena, void * nccl_comm, int32_t rank, int32_t world, uint32_t n_expert,
+               int32_t placement, gx_ep ** ep);
+int gx_ep_destroy(gx_ep * ep);
+/* dispatch: x device f32 [T, H]; ids HOST i32 [T, k] of global expert ids.
+ * Synchronizes the stream once (the peers' pair counts and expert ids are
+ * needed on the host for the slot policy). */
+int gx_ep_dispatch(gx_ep * ep, uint32_t layer, const float * x, const int32_t * ids, int64_t k, int64_t T, int64_t H,
+                   void * stream);
+/* compute: the pairs received by the last dispatch, on the local arena */
+int gx_ep_compute(gx_ep * ep, const gx_layer_desc * desc, void * stream, gx_serve_stats * stats);
+/* combine: w device f32 [T, k] router weights, out device f32 [T, H] */
+int gx_ep_combine(gx_ep * ep, const float * w, float * out, void * stream);
+/* the three in sequence */
+int gx_ep_layer_forward(gx_ep * ep, uint32_t layer, const gx_layer_desc * desc, const float * x, const int32_t * ids,
+                        const float * w, int64_t k, int64_t T, float * out, void * stream, gx_serve_stats * stats);
 
 /* ------------------------------------------------------------- synthetic
  * Seeded synthetic data written straight into device memory (test and bench
