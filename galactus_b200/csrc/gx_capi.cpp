@@ -129,6 +129,12 @@ struct gx_arena {
     uint8_t * d_xq = nullptr;           // quantized layer inputs, split layout, one row per token
     uint8_t * d_actq = nullptr;         // quantized activations of the down projection, one row per (token, slot)
     int32_t * d_cnt = nullptr;          // per (token, slot, Q8 block) completion counters, zero between calls
+    // expert-grouped (prefill) path: per-pair outputs and the pair grouping
+    float * d_y = nullptr;              // [pairs, H] down output of each (token, slot)
+    int32_t * h_grp = nullptr;          // pinned staging of the grouping arrays
+    int32_t * d_grp = nullptr;
+    size_t grp_cap = 0;                 // ints
+    cudaEvent_t ev_grp = nullptr;
     int32_t * d_ids = nullptr;          // kStageRing x (used * max_tokens) slot ids
     int32_t * h_ids = nullptr;          // pinned staging of the same
     cudaEvent_t ev_stage[kStageRing] = {};
@@ -252,6 +258,10 @@ int gx_arena_destroy(gx_arena * a) {
     if (a->d_xq) cudaFree(a->d_xq);
     if (a->d_actq) cudaFree(a->d_actq);
     if (a->d_cnt) cudaFree(a->d_cnt);
+    if (a->d_y) cudaFree(a->d_y);
+    if (a->d_grp) cudaFree(a->d_grp);
+    if (a->h_grp) cudaFreeHost(a->h_grp);
+    if (a->ev_grp) cudaEventDestroy(a->ev_grp);
     if (a->h_ids) cudaFreeHost(a->h_ids);
     for (auto e : a->tev) if (e) cudaEventDestroy(e);
     if (a->h_tier && a->own_tier) cudaFreeHost(a->h_tier);
@@ -741,6 +751,131 @@ void enqueue_layer(const LayerPlan & lp, const float * x, const float * w, float
     if (tv && tv[2]) ck(cudaEventRecordWithFlags(tv[2], s, cudaEventRecordExternal));
 }
 
+// Micro-batches with many (token, slot) pairs run the expert-grouped kernels:
+// every expert's rows are read once per layer instead of once per pair.
+constexpr int64_t kGroupedPairs = 128;
+
+bool use_grouped(const LayerPlan & lp, int64_t pairs) {
+    if (const char * env = std::getenv("GX_GROUPED")) {
+        if (env[0] == '0') return false;
+    }
+    return pairs >= kGroupedPairs && lp.type_gate == gx::GX_T_Q8_0 && lp.type_down == gx::GX_T_Q8_0 && lp.H % 256 == 0 &&
+           lp.I % 256 == 0;
+}
+
+// quantize x -> gate/up grouped -> quantize act -> down grouped -> combine
+void prefill_layer(gx_arena * a, const LayerPlan & lp, const float * x, const int32_t * slots, const float * w, float * out,
+                   cudaStream_t s) {
+    const int64_t T = lp.T, k = lp.k, P = T * k, H = lp.H, I = lp.I;
+    const int32_t n_as = lp.g.n_as;
+    if (a->d_y == nullptr) ck(cudaMalloc(&a->d_y, (size_t)(a->used * a->max_tokens) * (size_t)a->hidden * sizeof(float)));
+    if (a->ev_grp == nullptr) ck(cudaEventCreateWithFlags(&a->ev_grp, cudaEventDisableTiming));
+    // grouping: counting sort of the pairs by slot
+    const int64_t slots_used = std::min<int64_t>(P, n_as);
+    const int64_t units_max = slots_used * (I / 8 + H / 16);
+    const size_t need = (size_t)(n_as + 1) + 3 * (size_t)P + 4 * (size_t)units_max;
+    if (need > a->grp_cap) {
+        if (a->h_grp) {
+            ck(cudaEventSynchronize(a->ev_grp));
+            cudaFreeHost(a->h_grp);
+            a->h_grp = nullptr;
+        }
+        if (a->d_grp) cudaFree(a->d_grp);
+        a->d_grp = nullptr;
+        a->grp_cap = 0;
+        ck(cudaHostAlloc(&a->h_grp, need * sizeof(int32_t), cudaHostAllocDefault));
+        ck(cudaMalloc(&a->d_grp, need * sizeof(int32_t)));
+        a->grp_cap = need;
+    }
+    ck(cudaEventSynchronize(a->ev_grp));   // the previous upload out of h_grp has run
+    int32_t * seg = a->h_grp;
+    int32_t * src_tok = seg + (n_as + 1);
+    int32_t * src_pair = src_tok + P;
+    int32_t * dst = src_pair + P;
+    int32_t * u_slot_g = dst + P;
+    int32_t * u_row_g = u_slot_g + units_max;
+    int32_t * u_slot_d = u_row_g + units_max;
+    int32_t * u_row_d = u_slot_d + units_max;
+    for (int32_t e = 0; e <= n_as; ++e) seg[e] = 0;
+    for (int64_t i = 0; i < P; ++i) {
+        if (slots[i] < 0 || slots[i] >= n_as) throw PolicyError(GX_ERR_SLOTS, "slot id out of range");
+        ++seg[slots[i] + 1];
+    }
+    for (int32_t e = 0; e < n_as; ++e) seg[e + 1] += seg[e];
+    std::vector<int32_t> fill(seg, seg + n_as);
+    for (int64_t i = 0; i < P; ++i) {
+        const int32_t j = fill[(size_t)slots[i]]++;
+        src_tok[j] = (int32_t)(i / k);
+        src_pair[j] = (int32_t)i;
+        dst[j] = (int32_t)i;
+    }
+    int32_t ng = 0, nd = 0;
+    for (int32_t e = 0; e < n_as; ++e) {
+        if (seg[e + 1] == seg[e]) continue;
+        for (int64_t r = 0; r < I; r += 8) {
+            u_slot_g[ng] = e;
+            u_row_g[ng++] = (int32_t)r;
+        }
+        for (int64_t r = 0; r < H; r += 16) {
+            u_slot_d[nd] = e;
+            u_row_d[nd++] = (int32_t)r;
+        }
+    }
+    ck(cudaMemcpyAsync(a->d_grp, a->h_grp, need * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    ck(cudaEventRecord(a->ev_grp, s));
+    const int32_t * dseg = a->d_grp;
+    const int32_t * dtok = dseg + (n_as + 1);
+    const int32_t * dpair = dtok + P;
+    const int32_t * ddst = dpair + P;
+    const int32_t * dusg = ddst + P;
+    const int32_t * durg = dusg + units_max;
+    const int32_t * dusd = durg + units_max;
+    const int32_t * durd = dusd + units_max;
+
+    ck(gx::launch_quant_split(gx::GX_T_Q8_0, x, (int)H, T, H * 4, a->d_xq, s, false));
+    gx::PrefillParams g{};
+    g.w0 = lp.g.w0;
+    g.w1 = lp.g.w1;
+    g.nb01 = lp.g.nb01;
+    g.nb02 = lp.g.nb02;
+    g.K = (int32_t)H;
+    g.n_as = n_as;
+    g.n_units = ng;
+    g.unit_slot = dusg;
+    g.unit_row0 = durg;
+    g.seg_start = dseg;
+    g.pair_src = dtok;
+    g.pair_dst = ddst;
+    g.aq = a->d_xq;
+    g.al = lp.g.al;
+    g.out = a->d_act;
+    g.out_ld = I;
+    g.act = lp.g.act;
+    g.alpha = lp.g.alpha;
+    g.limit = lp.g.limit;
+    const uint32_t smem_g = gx::prefill_layout(g);
+    if (smem_g == 0) throw PolicyError(GX_ERR_ALIGN, "grouped gate/up layout");
+    ck(gx::launch_prefill(0, g, smem_g, s));
+    ck(gx::launch_quant_split(gx::GX_T_Q8_0, a->d_act, (int)I, P, I * 4, a->d_actq, s, false));
+    gx::PrefillParams dn = g;
+    dn.w0 = lp.dn.w0;
+    dn.w1 = nullptr;
+    dn.nb01 = lp.dn.nb01;
+    dn.K = (int32_t)I;
+    dn.n_units = nd;
+    dn.unit_slot = dusd;
+    dn.unit_row0 = durd;
+    dn.pair_src = dpair;
+    dn.aq = a->d_actq;
+    dn.al = lp.dn.al;
+    dn.out = a->d_y;
+    dn.out_ld = H;
+    const uint32_t smem_d = gx::prefill_layout(dn);
+    if (smem_d == 0) throw PolicyError(GX_ERR_ALIGN, "grouped down layout");
+    ck(gx::launch_prefill(1, dn, smem_d, s));
+    ck(gx::launch_combine(a->d_y, w, out, H, (int)k, T, s));
+}
+
 int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x, const int32_t * ids,
                          const float * w, int64_t k, int64_t T, float * out, cudaStream_t s, gx_serve_stats * stats) {
     if (x == nullptr || ids == nullptr || w == nullptr || out == nullptr) return GX_ERR_INVALID;
@@ -754,6 +889,13 @@ int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, 
     rc = arena_serve(a, layer, ids, (uint32_t)n, slots, a->last_ev[lp.li], s, &sst);
     if (rc != GX_OK) return rc;
     if (stats) *stats = sst;
+
+    if (use_grouped(lp, n)) {
+        prefill_layer(a, lp, x, slots, w, out, s);
+        ck(cudaEventRecord(a->ev_done[lp.li], s));
+        a->last_ev[lp.li] = a->ev_done[lp.li];
+        return GX_OK;
+    }
 
     const int32_t * ids_dev = nullptr;
     if (n > gx::kInlineIds) {

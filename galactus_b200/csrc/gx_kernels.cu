@@ -22,6 +22,7 @@
 #include "gx_kernels.h"
 #include "gx_moe.cuh"
 #include "gx_stack.cuh"
+#include "gx_prefill.cuh"
 
 namespace gx {
 
@@ -781,6 +782,43 @@ cudaError_t prepare_stack(int type_gate, int type_down, const StackParams & p, i
 cudaError_t launch_stack(int type_gate, int type_down, const StackParams & p, int grid, int threads, uint32_t smem,
                          cudaStream_t stream) {
     return stack_switch(type_gate, type_down, &p, grid, threads, smem, stream, nullptr);
+}
+
+// ------------------------------------------------------ prefill launchers
+
+// Shared-memory layout of a prefill CTA: barriers, the four staggered weight
+// tiles (gx_stack's bank-group offsets), two activation chunks.
+uint32_t prefill_layout(PrefillParams & p) {
+    if (p.K % 256 != 0 || p.nb01 % 16 != 0 || p.al.pitch % 16 != 0) return 0;
+    static const int xs[4] = {0, 1, 4, 5};
+    const uint64_t tile = 4ull * (uint64_t)p.nb01;
+    p.tile[0] = 0;
+    for (int t = 1; t < 4; ++t) {
+        uint64_t c = (p.tile[t - 1] + tile + 15) / 16;
+        while (c % 8 != (uint64_t)xs[t]) ++c;
+        p.tile[t] = (int32_t)(c * 16);
+    }
+    const uint64_t wbytes = (uint64_t)p.tile[3] + tile;
+    p.act_off = align_up(128 + wbytes, 128);
+    const uint64_t total = (uint64_t)p.act_off + 2ull * kPrefillChunk * (uint64_t)p.al.pitch;
+    return total <= kMaxSmem ? (uint32_t)total : 0;
+}
+
+template <int MODE>
+static cudaError_t launch_prefill_t(const PrefillParams & p, uint32_t smem, cudaStream_t stream) {
+    static int configured = 0;   // per instantiation
+    if ((int)smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(k_prefill<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = (int)smem;
+    }
+    if (p.n_units <= 0) return cudaSuccess;
+    k_prefill<MODE><<<p.n_units, 32 * kPrefillWarps, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill(int mode, const PrefillParams & p, uint32_t smem, cudaStream_t stream) {
+    return mode == 0 ? launch_prefill_t<0>(p, smem, stream) : launch_prefill_t<1>(p, smem, stream);
 }
 
 ActLayout act_layout_host(int vdt, int n) { return act_layout(vdt, n); }

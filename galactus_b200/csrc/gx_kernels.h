@@ -143,6 +143,32 @@ struct StackParams {
     StackLayer layers[kStackMaxLayers];
 };
 
+// Expert-grouped prefill kernels (gx_prefill.cuh).
+struct PrefillParams {
+    const uint8_t * w0;        // gate (MODE 0) or down (MODE 1) role base of slot 0
+    const uint8_t * w1;        // up role base (MODE 0)
+    int64_t nb01, nb02;        // row bytes, record stride
+    int32_t K;                 // row length in elements (multiple of 256)
+    int32_t n_as;              // slots of the layer
+    int32_t tile[4];           // staggered offsets of the four 4-row weight tiles
+    uint32_t act_off;          // shared-memory offset of the two activation chunks
+    int32_t n_units;
+    const int32_t * unit_slot; // [n_units]
+    const int32_t * unit_row0; // [n_units] first weight row of the unit (MODE 0: of 8 gate/up rows)
+    const int32_t * seg_start; // [n_as+1] the slot's range in the sorted pair arrays
+    const int32_t * pair_src;  // [P] activation row of each sorted pair (MODE 0: token, MODE 1: pair)
+    const int32_t * pair_dst;  // [P] output row (the pair index t*k+s)
+    const uint8_t * aq;        // activation rows, split layout
+    ActLayout al;
+    float * out;               // MODE 0: act [P, I]; MODE 1: y [P, H]
+    int64_t out_ld;
+    int32_t act;
+    float alpha, limit;
+};
+
+uint32_t prefill_layout(PrefillParams & p);
+cudaError_t launch_prefill(int mode, const PrefillParams & p, uint32_t smem, cudaStream_t stream);
+
 uint32_t stack_layout(StackParams & p, int & threads);
 bool stack_types_supported(int type_gate, int type_down);
 // Resident CTAs per SM of the stack kernel for this layout (0 on error).

@@ -244,6 +244,40 @@ def test_layer_forward_bitwise_with_churn(gxlib, orc, dev, name):
     arena.close()
 
 
+@pytest.mark.parametrize("T", [16, 64, 257])
+def test_grouped_prefill_matches_oracle(gxlib, orc, dev, T):
+    """Micro-batches of >= 128 (token, slot) pairs take the expert-grouped
+    kernels (each expert's rows read once, its tokens streamed in chunks of
+    16, four per warp); the bits equal the oracle and the per-pair decode path
+    (GX_GROUPED=0), including experts with one token and with 17 chunks."""
+    import os
+    m = _small_model(gxlib, "qwen3-30b", experts=12, layers=1)
+    k = m.used
+    arena = gxlib.Arena(m, capacity_bytes=m.experts * m.record, policy=gxlib.POLICY_AUTO, max_tokens=T)
+    recs = np.stack([orc.synth_record(m, m.seed, 0, e) for e in range(m.experts)])
+    for e in range(m.experts):
+        arena.load_record(0, e, recs[e])
+    rng = np.random.default_rng(900 + T)
+    ids, w = _zipf_routes(rng, T, m.experts, k)
+    x = rng.standard_normal((T, m.hidden)).astype(np.float32)
+    stream = torch.cuda.current_stream()
+    out = torch.full((T, m.hidden), float("nan"), dtype=torch.float32, device=dev)
+    arena.layer_forward(0, D(x), ids, D(w), out, stream=stream)
+    got = H(out)
+    os.environ["GX_GROUPED"] = "0"
+    try:
+        out2 = torch.full((T, m.hidden), float("nan"), dtype=torch.float32, device=dev)
+        arena.layer_forward(0, D(x), ids, D(w), out2, stream=stream)
+        per_pair = H(out2)
+    finally:
+        del os.environ["GX_GROUPED"]
+    want = orc.moe_layer(m, recs, x, ids, w)
+    np.testing.assert_array_equal(bits(got), bits(want), err_msg=f"grouped T={T}")
+    np.testing.assert_array_equal(bits(per_pair), bits(want), err_msg=f"per-pair T={T}")
+    no_device_error(gxlib)
+    arena.close()
+
+
 def test_remap_serve_strided_and_slot_bytes(gxlib, orc, dev):
     """The remap node reads and writes through strides, and every served slot
     holds exactly its record's bytes after churn (the serve-check pattern)."""
