@@ -123,6 +123,12 @@ _SIGS = {
     "gx_stack_plan_timing": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "gx_stack_plan_info_get": (C.c_int, [_P, C.POINTER(gx_stack_plan_info)]),
     "gx_stack_plan_destroy": (C.c_int, [_P]),
+    "gx_cache_plan_load": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
+    "gx_cache_plan_destroy": (None, [_P]),
+    "gx_cache_plan_info": (C.c_int, [_P, _P, _P, _P, _P, C.c_char_p, C.c_size_t]),
+    "gx_cache_plan_curve": (C.c_int, [_P, C.c_uint32, _P]),
+    "gx_plan_layer_quotas": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P, C.c_uint64, C.c_uint32, C.c_uint32, _P]),
+    "gx_policy_plan_quotas": (C.c_int, [C.POINTER(gx_profile), C.c_uint64, C.c_double, _P, _P]),
     "gx_ep_owner": (C.c_int, [C.c_int32, C.c_uint32, C.c_int32, C.c_int32, _P, _P]),
     "gx_ep_plan": (C.c_int, [C.c_int32, C.c_uint32, C.c_int32, _P, _I64, _I64, _P, _P]),
     "gx_ep_init": (C.c_int, [_P, _P, C.c_int32, C.c_int32, C.c_uint32, C.c_int32, C.POINTER(_P)]),

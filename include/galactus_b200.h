@@ -124,6 +124,31 @@ int32_t gx_policy_slot_of(const gx_policy * policy, uint32_t layer, uint32_t exp
 /* Cumulative counters (ExpertCache::hits/accesses/cold_bytes). */
 int gx_policy_counters(const gx_policy * policy, uint64_t * hits, uint64_t * accesses, uint64_t * cold_bytes);
 
+/* ------------------------------------------------------------- cache plan
+ * Per-layer quotas from measured miss curves (CachePlan and plan_layer_quotas,
+ * src/h4/h4-cache-plan.hpp:55-117, src/h4/h4-cache-plan.cpp:31-223).
+ * gx_cache_plan_load reads the reference's plan file ("galactus-cache-plan 1",
+ * arch/first_layer/last_layer/experts/used/source/tokens, one "curve <layer>
+ * m_0 ... m_experts" line per layer, "end"); malformed files are rejected.
+ * gx_plan_layer_quotas: curves [n_layers][curve_len] (misses at quota
+ * 0..curve_len-1), record_bytes [n_layers] -> quotas [n_layers], never above
+ * budget_bytes, never below floor or above ceiling (the reference allocator).
+ * gx_policy_plan_quotas: the quotas the engine applies for a plan: the budget
+ * the uniform quota buys and floor = uniform probation + 1
+ * (src/h4/h4-expert-cache.cpp:136-200). GX_ERR_STATE when the plan does not
+ * apply (other geometry, full residency, a result below 2 slots): keep the
+ * uniform quota. The result feeds gx_arena_config.plan_quotas. */
+typedef struct gx_cache_plan gx_cache_plan;
+int gx_cache_plan_load(const char * path, gx_cache_plan ** plan);
+void gx_cache_plan_destroy(gx_cache_plan * plan);
+int gx_cache_plan_info(const gx_cache_plan * plan, uint32_t * first_layer, uint32_t * last_layer, uint32_t * experts,
+                       uint32_t * used, char * arch, size_t arch_cap);
+int gx_cache_plan_curve(const gx_cache_plan * plan, uint32_t layer, uint32_t * misses);
+int gx_plan_layer_quotas(const uint32_t * curves, uint32_t n_layers, uint32_t curve_len, const uint64_t * record_bytes,
+                         uint64_t budget_bytes, uint32_t floor, uint32_t ceiling, uint32_t * quotas);
+int gx_policy_plan_quotas(const gx_profile * profile, uint64_t capacity_bytes, double protected_fraction,
+                          const gx_cache_plan * plan, uint32_t * quotas);
+
 /* ------------------------------------------------------------------ arena
  * The slot arena in HBM (one slab per layer, quota x record bytes, 16 KiB
  * aligned) and the pinned host tier that backs it (every record of every

@@ -11,6 +11,9 @@ Fixtures:
   q8_0_quant.npz         f32 blocks and gguf-py's Q8_0 quantization of them
   policy_traces.json     micro-batch traces and the reference policy's answers
                          (hits, evictions, slots, resident set) per batch
+  plan_quotas.json       synthetic miss curves (noisy, with flat steps and
+                         rises), budgets, floors, ceilings and the reference
+                         allocator's quotas (oracle/_ref/h4ref_plan)
 """
 from __future__ import annotations
 
@@ -65,6 +68,48 @@ def blocks_iq1_s(rng):
     return b
 
 
+def synthetic_curve(rng, experts: int) -> list[int]:
+    """Misses at quota 0..experts: a falling curve with noise, flat steps and
+    occasional rises (an SLRU is not a stack algorithm); entries 0 and 1 repeat
+    the value at quota 2, as the reference's plans do."""
+    start = int(rng.integers(500, 3000))
+    vals, v = [], float(start)
+    for q in range(experts + 1):
+        if q >= 3:
+            v = max(0.0, v * float(rng.uniform(0.80, 1.0)) - float(rng.integers(0, 20)))
+            if rng.random() < 0.15:
+                v += float(rng.integers(1, 40))   # a rise
+        vals.append(int(v))
+    vals[0] = vals[1] = vals[2]
+    return vals
+
+
+def make_plan_cases() -> None:
+    import subprocess
+    ref = HERE.parent.parent / "oracle" / "_ref" / "h4ref_plan"
+    if not ref.exists():
+        print("reference plan binary absent: plan_quotas.json not regenerated")
+        return
+    rng = np.random.default_rng(4242)
+    cases = []
+    for i in range(40):
+        n = int(rng.integers(1, 24))
+        experts = int(rng.choice([8, 16, 32, 64, 128]))
+        curves = [synthetic_curve(rng, experts) for _ in range(n)]
+        rec = [int(rng.choice([16384 * int(rng.integers(50, 400)), 4079616, 5013504])) for _ in range(n)]
+        floor = int(rng.integers(2, max(3, experts // 4)))
+        ceiling = int(rng.choice([experts, max(floor, experts // 2)]))
+        base = sum(rec) * floor
+        budget = int(base + rng.uniform(-0.05, 1.5) * sum(rec) * max(1, experts // 3))
+        stdin = f"Q {n} {experts + 1} {floor} {ceiling} {budget}\n" + " ".join(map(str, rec)) + "\n" + \
+            "\n".join(" ".join(map(str, c)) for c in curves) + "\n"
+        out = subprocess.run([str(ref)], input=stdin, capture_output=True, text=True, check=True).stdout.split()
+        cases.append({"curves": curves, "record_bytes": rec, "floor": floor, "ceiling": ceiling, "budget": budget,
+                      "quotas": [int(v) for v in out[1:]] if out[0] == "R" else None})
+    (HERE / "plan_quotas.json").write_text(json.dumps(cases))
+    print("plan_quotas.json:", len(cases), "cases,", sum(c["quotas"] is None for c in cases), "rejected")
+
+
 def main() -> None:
     rng = np.random.default_rng(20261201)
     IQ1_S.init_grid()
@@ -86,6 +131,7 @@ def main() -> None:
     # policy traces, answered by the reference's own ExpertCache/ExpertStore
     from oracle import oracle as orc
     orc.build()
+    make_plan_cases()
     if not orc.ref_replay_available():
         print("reference policy binary absent: policy_traces.json not regenerated")
         return
@@ -135,4 +181,7 @@ def main() -> None:
 
 
 if __name__ == "__main__":
+    if "--plans" in sys.argv:
+        make_plan_cases()
+        sys.exit(0)
     main()
