@@ -123,6 +123,8 @@ _SIGS = {
     "gx_stack_plan_timing": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "gx_stack_plan_info_get": (C.c_int, [_P, C.POINTER(gx_stack_plan_info)]),
     "gx_stack_plan_destroy": (C.c_int, [_P]),
+    "gx_route_observer_open": (C.c_int, [C.c_char_p, C.c_char_p, C.c_uint64]),
+    "gx_route_observer_close": (C.c_int, []),
     "gx_cache_plan_load": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
     "gx_cache_plan_destroy": (None, [_P]),
     "gx_cache_plan_info": (C.c_int, [_P, _P, _P, _P, _P, C.c_char_p, C.c_size_t]),

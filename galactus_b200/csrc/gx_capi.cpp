@@ -15,6 +15,7 @@
 #include "../../include/galactus_b200.h"
 #include "gx_formats.h"
 #include "gx_kernels.h"
+#include "gx_observer.hpp"
 #include "gx_policy.hpp"
 
 using gx::PolicyError;
@@ -22,6 +23,11 @@ using gx::SlotPolicy;
 
 struct gx_policy {
     SlotPolicy impl;
+    // geometry for the route observer's context lines
+    uint64_t capacity = 0;
+    double fraction = 0.0;
+    uint32_t used = 0;
+    std::vector<uint64_t> record;
     explicit gx_policy(SlotPolicy && p) : impl(std::move(p)) {}
 };
 
@@ -103,6 +109,47 @@ int serve_policy(SlotPolicy & P, uint32_t layer, const int32_t * experts, uint32
     }
     if (st) *st = local;
     return GX_OK;
+}
+
+// The serve, with the route observer around it when a trace is open: the
+// residency of every key sampled before the serve, the serve's clock, and the
+// host->HBM bytes it issued (src/h4/h4-route-observer.hpp:84-128).
+template <typename F>
+int observed(const gx_policy * pol, uint32_t layer, const int32_t * experts, uint32_t count, uint32_t tokens,
+             uint32_t k, F && serve) {
+    uint64_t bytes = 0;
+    if (!gx::observer_enabled()) return serve(bytes);
+    const SlotPolicy & P = pol->impl;
+    if ((uint64_t)tokens * k != count) {
+        tokens = 1;
+        k = count;
+    }
+    const uint64_t enter = gx::observer_now_ns();
+    thread_local std::vector<uint8_t> resident;
+    resident.assign(count, 0);
+    const bool in_range = layer >= P.first_layer() && layer <= P.last_layer();
+    for (uint32_t i = 0; i < count && in_range; ++i)
+        resident[i] = experts[i] >= 0 && (uint32_t)experts[i] < P.experts() && P.slot_of(layer, (uint32_t)experts[i]) >= 0;
+    const uint64_t start = gx::observer_now_ns();
+    const int rc = serve(bytes);
+    const uint64_t end = gx::observer_now_ns();
+    if (rc == GX_OK) {
+        gx::ObserverGeometry g{pol->capacity, pol->fraction, P.quota_uniform(), P.probation_of(P.first_layer()),
+                               P.quota_uniform(), P.first_layer(), P.last_layer(), P.experts(), pol->used,
+                               pol->record.data()};
+        gx::observer_record(g, layer, tokens, k, experts, resident.data(), enter, start, end, bytes);
+    }
+    return rc;
+}
+
+gx_policy * make_gx_policy(const gx_profile & prof, uint64_t capacity, double fraction, int policy,
+                           const uint32_t * plan) {
+    gx_policy * p = new gx_policy(make_policy(prof, capacity, fraction, policy, plan));
+    p->capacity = capacity;
+    p->fraction = fraction;
+    p->used = prof.used;
+    p->record.assign(prof.record_bytes, prof.record_bytes + (prof.last_layer - prof.first_layer + 1));
+    return p;
 }
 
 }  // namespace
@@ -200,7 +247,7 @@ int gx_policy_create(const gx_profile * profile, uint64_t capacity_bytes, double
                      const uint32_t * plan_quotas, gx_policy ** out) {
     if (profile == nullptr || out == nullptr) return GX_ERR_INVALID;
     return guarded([&] {
-        *out = new gx_policy(make_policy(*profile, capacity_bytes, protected_fraction, policy, plan_quotas));
+        *out = make_gx_policy(*profile, capacity_bytes, protected_fraction, policy, plan_quotas);
         return GX_OK;
     });
 }
@@ -222,7 +269,14 @@ int gx_policy_serve(gx_policy * policy, uint32_t layer, const int32_t * experts,
                     uint8_t * hit_out, int32_t * evicted_out, gx_serve_stats * stats) {
     if (policy == nullptr || (count > 0 && (experts == nullptr || slots_out == nullptr))) return GX_ERR_INVALID;
     return guarded([&] {
-        return serve_policy(policy->impl, layer, experts, count, slots_out, hit_out, evicted_out, nullptr, stats);
+        return observed(policy, layer, experts, count, 1, count, [&](uint64_t & bytes) {
+            gx_serve_stats st{};
+            const int rc = serve_policy(policy->impl, layer, experts, count, slots_out, hit_out, evicted_out, nullptr, &st);
+            if (stats) *stats = st;
+            // whole records per miss: what a reader of the backing tier would pull
+            if (rc == GX_OK) bytes = (uint64_t)st.misses * policy->record[layer - policy->impl.first_layer()];
+            return rc;
+        });
     });
 }
 
@@ -278,8 +332,7 @@ int gx_arena_create(const gx_arena_config * c, gx_arena ** out) {
     const int rc = guarded([&] {
         a->device = c->device;
         ck(cudaSetDevice(c->device));
-        a->policy = new gx_policy(make_policy(c->profile, c->capacity_bytes, c->protected_fraction, c->policy,
-                                              c->plan_quotas));
+        a->policy = make_gx_policy(c->profile, c->capacity_bytes, c->protected_fraction, c->policy, c->plan_quotas);
         const SlotPolicy & P = a->policy->impl;
         const uint32_t n = P.layer_count();
         a->record.assign(c->profile.record_bytes, c->profile.record_bytes + n);
@@ -417,8 +470,25 @@ namespace {
 // Serve a micro-batch and issue one host->HBM copy per miss on the copy
 // stream. The copies start after `after` (the last consumer of the layer's
 // slots) and `consumer` waits for them.
+int arena_serve_impl(gx_arena * a, uint32_t layer, const int32_t * experts, uint32_t count, int32_t * slots,
+                     cudaEvent_t after, cudaStream_t consumer, gx_serve_stats * st_out);
+
+// One micro-batch of one layer through the policy, miss copies issued on the
+// copy stream; `tokens` x `k` is the micro-batch shape (for the route trace).
 int arena_serve(gx_arena * a, uint32_t layer, const int32_t * experts, uint32_t count, int32_t * slots,
-                cudaEvent_t after, cudaStream_t consumer, gx_serve_stats * st_out) {
+                cudaEvent_t after, cudaStream_t consumer, gx_serve_stats * st_out, uint32_t tokens, uint32_t k) {
+    return observed(a->policy, layer, experts, count, tokens, k, [&](uint64_t & bytes) {
+        gx_serve_stats st{};
+        const int rc = arena_serve_impl(a, layer, experts, count, slots, after, consumer, &st);
+        // the trace counts whole records per miss, the unit of the reference's reader
+        if (rc == GX_OK) bytes = (uint64_t)st.misses * a->record[a->L(layer)];
+        if (st_out) *st_out = st;
+        return rc;
+    });
+}
+
+int arena_serve_impl(gx_arena * a, uint32_t layer, const int32_t * experts, uint32_t count, int32_t * slots,
+                     cudaEvent_t after, cudaStream_t consumer, gx_serve_stats * st_out) {
     thread_local std::vector<std::pair<int32_t, int32_t>> misses;
     misses.clear();
     gx_serve_stats st{};
@@ -488,7 +558,8 @@ int gx_remap_serve(gx_arena * a, uint32_t layer, const int32_t * ids, int64_t ne
         cudaStream_t consumer = reinterpret_cast<cudaStream_t>(stream);
         // everything already queued on the consumer stream may read the slab
         ck(cudaEventRecord(a->ev_snapshot, consumer));
-        const int rc = arena_serve(a, layer, experts.data(), (uint32_t)n, sl.data(), a->ev_snapshot, consumer, stats);
+        const int rc = arena_serve(a, layer, experts.data(), (uint32_t)n, sl.data(), a->ev_snapshot, consumer, stats,
+                                   (uint32_t)ne1, (uint32_t)ne0);
         if (rc != GX_OK) return rc;
         char * dst = reinterpret_cast<char *>(slots);
         for (int64_t i1 = 0, f = 0; i1 < ne1; ++i1)
@@ -527,7 +598,7 @@ int gx_arena_warm_all(gx_arena * a, void * stream) {
                 std::vector<int32_t> ex(cnt), sl(cnt);
                 for (uint32_t j = 0; j < cnt; ++j) ex[j] = (int32_t)(e0 + j);
                 ck(cudaEventRecord(a->ev_snapshot, consumer));
-                const int rc = arena_serve(a, layer, ex.data(), cnt, sl.data(), a->ev_snapshot, consumer, nullptr);
+                const int rc = arena_serve(a, layer, ex.data(), cnt, sl.data(), a->ev_snapshot, consumer, nullptr, 1, cnt);
                 if (rc != GX_OK) return rc;
             }
         }
@@ -886,7 +957,7 @@ int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, 
     const int64_t n = k * T;
     int32_t * slots = a->slot_scratch.data();
     gx_serve_stats sst{};
-    rc = arena_serve(a, layer, ids, (uint32_t)n, slots, a->last_ev[lp.li], s, &sst);
+    rc = arena_serve(a, layer, ids, (uint32_t)n, slots, a->last_ev[lp.li], s, &sst, (uint32_t)T, (uint32_t)k);
     if (rc != GX_OK) return rc;
     if (stats) *stats = sst;
 
@@ -1209,7 +1280,7 @@ int gx_stack_plan_run(gx_stack_plan * p, const int32_t * ids, void * stream, gx_
             gx_serve_stats st{};
             const uint32_t li = p->lps[i].li;
             const int rc = arena_serve(a, p->first + i, ids + (size_t)i * per, (uint32_t)per, h + (size_t)i * per,
-                                       a->last_ev[li], s, &st);
+                                       a->last_ev[li], s, &st, (uint32_t)p->T, (uint32_t)p->k);
             if (rc != GX_OK) return rc;
             sum.hits += st.hits;
             sum.misses += st.misses;

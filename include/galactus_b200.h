@@ -348,6 +348,18 @@ int gx_moe_ffn_noalloc(const gx_layer_desc * desc, const void * slot0_record, ui
                        const float * x, const int32_t * slots, const float * w, int64_t k, int64_t T, float * out,
                        void * stream);
 
+/* ---------------------------------------------------------- route trace
+ * The route observer of the reference (src/h4/h4-route-observer.hpp:58-304):
+ * every micro-batch served through an arena or a policy (layer, tokens, k,
+ * the expert ids in order, each with its residency bit sampled before the
+ * serve, the serve's clock and the host->HBM bytes it issued) is buffered in
+ * memory and written once, in the reference's "galactus.route-observer.v1"
+ * text format, at gx_route_observer_close or at exit. Also opened by
+ * GALACTUS_H4_ROUTES=<file> (GALACTUS_H4_ROUTES_CAP caps the entries), read at
+ * the first serve. Observational only: nothing it does changes a slot. */
+int gx_route_observer_open(const char * path, const char * arch, uint64_t entry_cap);
+int gx_route_observer_close(void);
+
 /* ------------------------------------------------------- expert parallel
  * The experts of a model shard over G ranks, one process per GPU: expert e
  * lives on rank e % G (GX_EP_MODULO) or e / ceil(E/G) (GX_EP_BLOCK), where

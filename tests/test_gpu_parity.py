@@ -278,6 +278,41 @@ def test_grouped_prefill_matches_oracle(gxlib, orc, dev, T):
     arena.close()
 
 
+def test_route_trace_of_layer_calls(gxlib, orc, dev, tmp_path):
+    """The arena path records each layer call with its (tokens, k) shape, the
+    residency sampled before the serve and whole records per miss."""
+    from galactus_b200.route_trace import close_trace, open_trace, read_trace
+    m = _small_model(gxlib, "qwen3-30b", experts=12, layers=2)
+    k = m.used
+    arena = gxlib.Arena(m, capacity_bytes=(k + 2) * m.record * m.layers, policy=gxlib.POLICY_AUTO, max_tokens=2)
+    for L in range(m.layers):
+        for e in range(m.experts):
+            arena.load_record(L, e, orc.synth_record(m, m.seed, L, e))
+    path = tmp_path / "routes.txt"
+    open_trace(str(path), arch="qwen3moe")
+    rng = np.random.default_rng(4)
+    stream = torch.cuda.current_stream()
+    calls = []
+    for step in range(8):
+        L = step % 2
+        ids, w = _zipf_routes(rng, 1, m.experts, k)
+        before = [arena.slot_of(L, int(e)) >= 0 for e in ids.ravel()]
+        x = rng.standard_normal((1, m.hidden)).astype(np.float32)
+        out = torch.zeros((1, m.hidden), dtype=torch.float32, device=dev)
+        s0 = arena.stats()["misses"]
+        arena.layer_forward(L, D(x), ids, D(w), out, stream=stream)
+        calls.append((L, ids.ravel().tolist(), before, arena.stats()["misses"] - s0))
+    torch.cuda.synchronize()
+    close_trace()
+    tr = read_trace(str(path))
+    assert len(tr["entries"]) == len(calls)
+    for e, (L, ids, before, misses) in zip(tr["entries"], calls):
+        assert (e["layer"], e["tokens"], e["k"]) == (L, 1, k)
+        assert e["ids"] == ids and e["resident"] == [int(b) for b in before]
+        assert e["bytes_read"] == misses * m.record
+    arena.close()
+
+
 def test_remap_serve_strided_and_slot_bytes(gxlib, orc, dev):
     """The remap node reads and writes through strides, and every served slot
     holds exactly its record's bytes after churn (the serve-check pattern)."""
