@@ -49,6 +49,15 @@ class gx_serve_stats(C.Structure):
 
 
 GX_EP_MODULO, GX_EP_BLOCK = 0, 1
+
+
+class gx_gguf_moe(C.Structure):
+    _fields_ = [("arch", C.c_char * 64), ("first_layer", C.c_uint32), ("last_layer", C.c_uint32),
+                ("experts", C.c_uint32), ("used", C.c_uint32), ("block_count", C.c_uint32),
+                ("type_gate", C.c_uint32), ("type_up", C.c_uint32), ("type_down", C.c_uint32),
+                ("hidden", C.c_uint64), ("intermediate", C.c_uint64),
+                ("record_bytes", C.c_uint64), ("record_bytes_raw", C.c_uint64)]
+
 GX_PLAN_TIMING = 1
 GX_PLAN_LAYERWISE = 2
 
@@ -123,6 +132,9 @@ _SIGS = {
     "gx_stack_plan_timing": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "gx_stack_plan_info_get": (C.c_int, [_P, C.POINTER(gx_stack_plan_info)]),
     "gx_stack_plan_destroy": (C.c_int, [_P]),
+    "gx_gguf_moe_info": (C.c_int, [C.c_char_p, _P]),
+    "gx_arena_load_gguf": (C.c_int, [_P, C.c_char_p, _P]),
+    "gx_fnv1a64": (C.c_uint64, [_P, C.c_uint64]),
     "gx_route_observer_open": (C.c_int, [C.c_char_p, C.c_char_p, C.c_uint64]),
     "gx_route_observer_close": (C.c_int, []),
     "gx_cache_plan_load": (C.c_int, [C.c_char_p, C.POINTER(_P)]),

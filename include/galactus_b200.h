@@ -348,6 +348,26 @@ int gx_moe_ffn_noalloc(const gx_layer_desc * desc, const void * slot0_record, ui
                        const float * x, const int32_t * slots, const float * w, int64_t k, int64_t T, float * out,
                        void * stream);
 
+/* ------------------------------------------------------------ GGUF tier
+ * Routed-expert weights read from a GGUF checkpoint (version 2/3): the
+ * blk.L.ffn_{down,gate,up}_exps.weight tensors ([ne0, ne1, n_expert], expert
+ * e's rows contiguous) give the record of (L, e) as down | gate | up, the
+ * layout of the reference's packs and profile (scripts/moe-profile.py:116-211,
+ * records padded to 16 KiB). gx_gguf_moe_info reads the geometry;
+ * gx_arena_load_gguf copies every record of the arena's layers into its host
+ * tier (as gx_load_record). gx_fnv1a64 is the record fingerprint of the
+ * reference's paranoia check (scripts/verify-paranoia-trace.py:8-20). */
+typedef struct gx_gguf_moe {
+    char arch[64];
+    uint32_t first_layer, last_layer, experts, used, block_count;
+    uint32_t type_gate, type_up, type_down;
+    uint64_t hidden, intermediate;
+    uint64_t record_bytes, record_bytes_raw;
+} gx_gguf_moe;
+int gx_gguf_moe_info(const char * path, gx_gguf_moe * info);
+int gx_arena_load_gguf(gx_arena * arena, const char * path, uint32_t * records_loaded);
+uint64_t gx_fnv1a64(const void * data, uint64_t n);
+
 /* ---------------------------------------------------------- route trace
  * The route observer of the reference (src/h4/h4-route-observer.hpp:58-304):
  * every micro-batch served through an arena or a policy (layer, tokens, k,
