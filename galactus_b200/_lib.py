@@ -60,6 +60,13 @@ class gx_gguf_moe(C.Structure):
 
 GX_PLAN_TIMING = 1
 GX_PLAN_LAYERWISE = 2
+GX_GATING_SOFTMAX, GX_GATING_SIGMOID, GX_GATING_SOFTMAX_WEIGHT = 0, 1, 2
+
+
+class gx_router_desc(C.Structure):
+    _fields_ = [("gating", C.c_int32), ("n_expert", C.c_int32), ("n_expert_used", C.c_int32),
+                ("n_groups", C.c_int32), ("n_group_used", C.c_int32), ("norm_w", C.c_int32),
+                ("scale_w", C.c_int32), ("w_scale", C.c_float)]
 
 
 class gx_stack_plan_info(C.Structure):
@@ -132,6 +139,10 @@ _SIGS = {
     "gx_stack_plan_timing": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "gx_stack_plan_info_get": (C.c_int, [_P, C.POINTER(gx_stack_plan_info)]),
     "gx_stack_plan_destroy": (C.c_int, [_P]),
+    "gx_stack_plan_run_routed": (C.c_int, [_P, C.POINTER(gx_router_desc), _P, _I64, _P, _P, _P,
+                                           C.POINTER(gx_serve_stats)]),
+    "gx_router_forward": (C.c_int, [C.POINTER(gx_router_desc), _P, _I64, _P, _I64, _I64, _P, _P, _P, _P, _P]),
+    "gx_arena_slot_table": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P, C.c_int, _P]),
     "gx_gguf_moe_info": (C.c_int, [C.c_char_p, _P]),
     "gx_arena_load_gguf": (C.c_int, [_P, C.c_char_p, _P]),
     "gx_fnv1a64": (C.c_uint64, [_P, C.c_uint64]),

@@ -1029,6 +1029,11 @@ struct gx_stack_plan {
     uint8_t * d_xq = nullptr;
     float * d_act = nullptr;
     uint8_t * d_actq = nullptr;
+    // device routing (gx_stack_plan_run_routed)
+    std::vector<const float *> wp;      // the plan's router weight pointers
+    int32_t * d_table = nullptr;        // [n, experts] slot of every expert, built once the layers are pinned
+    int32_t * d_ids = nullptr;          // [n, T, k] router ids when the caller keeps none
+    std::vector<int32_t> h_ids;         // ids read back for the route trace
 };
 
 namespace {
@@ -1179,6 +1184,8 @@ int gx_stack_plan_destroy(gx_stack_plan * p) {
     if (p->d_xq) cudaFree(p->d_xq);
     if (p->d_act) cudaFree(p->d_act);
     if (p->d_actq) cudaFree(p->d_actq);
+    if (p->d_table) cudaFree(p->d_table);
+    if (p->d_ids) cudaFree(p->d_ids);
     delete p;
     return GX_OK;
 }
@@ -1203,6 +1210,7 @@ int gx_stack_plan_create(gx_arena * a, uint32_t first_layer, uint32_t n_layers, 
         p->T = T;
         p->desc = *d;
         p->timing = timing ? 1 : 0;
+        p->wp.assign(w, w + n_layers);
         p->lps.resize(n_layers);
         for (uint32_t i = 0; i < n_layers; ++i) {
             const int r = plan_layer(a, first_layer + i, d, k, T, p->lps[i]);
@@ -1337,6 +1345,152 @@ int gx_stack_plan_info_get(const gx_stack_plan * p, gx_stack_plan_info * info) {
         info->smem_bytes = p->smem;
     }
     return GX_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- router
+
+namespace {
+
+bool router_valid(const gx_router_desc * d) {
+    if (d == nullptr) return false;
+    const int E = d->n_expert, k = d->n_expert_used;
+    if (d->gating < GX_GATING_SOFTMAX || d->gating > GX_GATING_SOFTMAX_WEIGHT) return false;
+    if (k < 1 || k > gx::kRouterMaxUsed || E < k || E > gx::kRouterMaxExperts) return false;
+    if (d->n_groups > 1) {
+        const int G = d->n_groups;
+        if (G > gx::kRouterMaxGroups || E % G != 0 || E / G < 2) return false;
+        if (d->n_group_used < 1 || d->n_group_used > G || d->n_group_used * (E / G) < k) return false;
+    }
+    return true;
+}
+
+gx::RouterLaunch router_launch(const gx_router_desc * d, const float * logits, int64_t ld, const float * bias,
+                               int64_t T, int64_t n_layers, int32_t * ids, float * w, const int32_t * table,
+                               int32_t * slots) {
+    gx::RouterLaunch r{};
+    r.logits = logits;
+    r.ld = ld;
+    r.bias = bias;
+    r.table = table;
+    r.ids = ids;
+    r.w = w;
+    r.slots = slots;
+    r.T = T;
+    r.n_layers = n_layers;
+    r.E = d->n_expert;
+    r.k = d->n_expert_used;
+    r.gating = d->gating;
+    r.groups = d->n_groups > 1 ? d->n_groups : 0;
+    r.group_used = d->n_group_used;
+    r.norm = d->norm_w ? 1 : 0;
+    r.scale_on = d->scale_w ? 1 : 0;
+    r.scale = d->w_scale;
+    return r;
+}
+
+// the slot of every expert of layers [first, first + n) into host [n, experts];
+// false when require_all and some expert has none
+bool collect_slot_table(const SlotPolicy & P, uint32_t first, uint32_t n, bool require_all, std::vector<int32_t> & h) {
+    const uint32_t E = P.experts();
+    h.assign((size_t)n * E, -1);
+    for (uint32_t i = 0; i < n; ++i)
+        for (uint32_t e = 0; e < E; ++e) {
+            const int32_t s = P.slot_of(first + i, e);
+            if (s < 0 && require_all) return false;
+            h[(size_t)i * E + e] = s;
+        }
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gx_router_forward(const gx_router_desc * d, const float * logits, int64_t ld, const float * bias, int64_t T,
+                      int64_t n_layers, int32_t * ids, float * weights, const int32_t * slot_table, int32_t * slots,
+                      void * stream) {
+    if (!router_valid(d) || T < 0 || n_layers < 0) return GX_ERR_INVALID;
+    if (T * n_layers == 0) return GX_OK;
+    if (logits == nullptr || ids == nullptr || weights == nullptr || ld < d->n_expert) return GX_ERR_INVALID;
+    if ((slot_table == nullptr) != (slots == nullptr)) return GX_ERR_INVALID;
+    return guarded([&] {
+        ck(gx::launch_router(router_launch(d, logits, ld, bias, T, n_layers, ids, weights, slot_table, slots),
+                             reinterpret_cast<cudaStream_t>(stream)));
+        return GX_OK;
+    });
+}
+
+int gx_arena_slot_table(gx_arena * a, uint32_t first_layer, uint32_t n_layers, int32_t * table, int require_all,
+                        void * stream) {
+    if (a == nullptr || table == nullptr || n_layers == 0) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        const SlotPolicy & P = a->policy->impl;
+        if (first_layer < P.first_layer() || first_layer + n_layers - 1 > P.last_layer()) return GX_ERR_INVALID;
+        std::vector<int32_t> h;
+        if (!collect_slot_table(P, first_layer, n_layers, require_all != 0, h)) return GX_ERR_STATE;
+        ck(cudaSetDevice(a->device));
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        ck(cudaMemcpyAsync(table, h.data(), h.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+        ck(cudaStreamSynchronize(s));
+        return GX_OK;
+    });
+}
+
+int gx_stack_plan_run_routed(gx_stack_plan * p, const gx_router_desc * d, const float * logits, int64_t ld,
+                             const float * bias, int32_t * ids_out, void * stream, gx_serve_stats * stats) {
+    if (p == nullptr || !router_valid(d) || logits == nullptr || ld < (d ? d->n_expert : 0)) return GX_ERR_INVALID;
+    gx_arena * a = p->a;
+    const SlotPolicy & P = a->policy->impl;
+    if ((uint32_t)d->n_expert != P.experts() || d->n_expert_used != p->k) return GX_ERR_INVALID;
+    const int64_t per = p->k * p->T;
+    for (uint32_t i = 1; i < p->n; ++i)
+        if (p->wp[i] != p->wp[0] + (size_t)i * per) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        ck(cudaSetDevice(a->device));
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        if (p->d_table == nullptr) {
+            // pinned layers keep every slot for good: the table is built once
+            std::vector<int32_t> h;
+            if (!collect_slot_table(P, p->first, p->n, true, h)) return GX_ERR_STATE;
+            ck(cudaMalloc(&p->d_table, h.size() * sizeof(int32_t)));
+            ck(cudaMemcpy(p->d_table, h.data(), h.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
+        }
+        int32_t * ids = ids_out;
+        if (ids == nullptr) {
+            if (p->d_ids == nullptr) ck(cudaMalloc(&p->d_ids, (size_t)p->n * per * sizeof(int32_t)));
+            ids = p->d_ids;
+        }
+        ck(gx::launch_router(router_launch(d, logits, ld, bias, p->T, p->n, ids, const_cast<float *>(p->wp[0]),
+                                           p->d_table, p->d_slots),
+                             s));
+        ck(cudaGraphLaunch(p->exec, s));
+        ck(cudaEventRecord(p->ev_graph, s));
+        for (uint32_t i = 0; i < p->n; ++i) a->last_ev[p->lps[i].li] = p->ev_graph;
+        const uint64_t hits = (uint64_t)p->n * per;
+        a->stats.serves += p->n;
+        a->stats.hits += hits;
+        if (stats) {
+            *stats = gx_serve_stats{};
+            stats->hits = hits;
+        }
+        if (gx::observer_enabled()) {
+            // the ids exist on the device only: read them back for the trace
+            p->h_ids.resize((size_t)p->n * per);
+            ck(cudaMemcpyAsync(p->h_ids.data(), ids, p->h_ids.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+            ck(cudaStreamSynchronize(s));
+            for (uint32_t i = 0; i < p->n; ++i)
+                observed(a->policy, p->first + i, p->h_ids.data() + (size_t)i * per, (uint32_t)per, (uint32_t)p->T,
+                         (uint32_t)p->k, [](uint64_t & bytes) {
+                             bytes = 0;
+                             return GX_OK;
+                         });
+        }
+        return GX_OK;
+    });
 }
 
 // --------------------------------------------------------------- synthetic

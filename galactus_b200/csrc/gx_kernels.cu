@@ -23,6 +23,7 @@
 #include "gx_moe.cuh"
 #include "gx_stack.cuh"
 #include "gx_prefill.cuh"
+#include "gx_router.cuh"
 
 namespace gx {
 
@@ -501,6 +502,33 @@ cudaError_t launch_move_rows(const float * src, const int32_t * idx, int64_t n, 
 cudaError_t launch_fill(float * dst, int64_t n, float v, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     k_fill<<<grid_1d(n, 256), 256, 0, stream>>>(dst, n, v);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_router(const RouterLaunch & r, cudaStream_t stream) {
+    const int64_t rows = r.T * r.n_layers;
+    if (rows <= 0) return cudaSuccess;
+    RouterParams p{};
+    p.logits = r.logits;
+    p.ld = r.ld;
+    p.bias = r.bias;
+    p.table = r.table;
+    p.ids = r.ids;
+    p.w = r.w;
+    p.slots = r.slots;
+    p.rows = rows;
+    p.T = r.T;
+    p.E = r.E;
+    p.k = r.k;
+    p.gating = r.gating;
+    p.groups = r.groups;
+    p.group_used = r.group_used;
+    p.norm = r.norm;
+    p.scale_on = r.scale_on;
+    p.scale = r.scale;
+    const size_t smem = (size_t)kRouterWarps * router_smem_floats(r.E) * sizeof(float);
+    const unsigned grid = (unsigned)((rows + kRouterWarps - 1) / kRouterWarps);
+    k_router<<<grid, 32 * kRouterWarps, smem, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -195,6 +195,24 @@ cudaError_t launch_combine(const float * y, const float * w, float * out, int64_
 cudaError_t launch_move_rows(const float * src, const int32_t * idx, int64_t n, int64_t H, float * dst, bool scatter,
                              cudaStream_t stream);
 cudaError_t launch_fill(float * dst, int64_t n, float v, cudaStream_t stream);
+// router: logits [rows, ld] -> ids/w [rows, k] (+ slots through table); rows = n_layers * T
+constexpr int kRouterWarps = 4;
+constexpr int kRouterMaxExperts = 1024;
+constexpr int kRouterMaxUsed = 32;
+constexpr int kRouterMaxGroups = 32;
+struct RouterLaunch {
+    const float * logits;
+    int64_t ld;
+    const float * bias;
+    const int32_t * table;
+    int32_t * ids;
+    float * w;
+    int32_t * slots;
+    int64_t T, n_layers;
+    int E, k, gating, groups, group_used, norm, scale_on;
+    float scale;
+};
+cudaError_t launch_router(const RouterLaunch & r, cudaStream_t stream);
 cudaError_t launch_synth_normal(float * dst, int64_t n, uint64_t seed, uint64_t stream_id, float sigma, cudaStream_t stream);
 cudaError_t launch_synth_weights(int type, void * dst, int64_t ne00, int64_t n_rows, uint64_t seed, uint64_t stream_id,
                                  float sigma, cudaStream_t stream);

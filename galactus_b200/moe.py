@@ -291,6 +291,18 @@ class StackPlan:
             raise L.GxError(rc, "gx_stack_plan_run")
         return self.st
 
+    def run_routed(self, desc: "L.gx_router_desc", logits, bias=None, ids_out=None, stream=None) -> L.gx_serve_stats:
+        """Route on the device (logits device f32 [n_layers*T, E], bias device
+        f32 [n_layers, E] or None) and run the stack, no host round trip;
+        the plan's weight pointers must be consecutive [T, k] slices of one
+        buffer and every layer pinned."""
+        ld = logits.stride(0) if hasattr(logits, "stride") else desc.n_expert
+        rc = self.arena._lib.gx_stack_plan_run_routed(self.h, C.byref(desc), _ptr(logits), ld, _ptr(bias),
+                                                      _ptr(ids_out), _stream(stream), C.byref(self.st))
+        if rc != L.GX_OK:
+            raise L.GxError(rc, "gx_stack_plan_run_routed")
+        return self.st
+
     def info(self) -> dict:
         """Launch shape: stack_kernel (one persistent kernel) or per-layer kernels."""
         i = L.gx_stack_plan_info()
@@ -314,6 +326,55 @@ class StackPlan:
             self.close()
         except Exception:
             pass
+
+
+def router_desc(gating: int, n_expert: int, k: int, *, groups: int = 0, group_used: int = 0, norm_w: bool = False,
+                w_scale: float | None = None) -> L.gx_router_desc:
+    return L.gx_router_desc(gating, n_expert, k, groups, group_used, 1 if norm_w else 0,
+                            0 if w_scale is None else 1, 1.0 if w_scale is None else w_scale)
+
+
+# the router of each model family (upstream build_moe_ffn's arguments for it)
+ROUTERS = {
+    "olmoe-1b-7b": dict(gating=L.GX_GATING_SOFTMAX),
+    "qwen3-30b-a3b": dict(gating=L.GX_GATING_SOFTMAX, norm_w=True),
+    "qwen3-235b-a22b": dict(gating=L.GX_GATING_SOFTMAX, norm_w=True),
+    "gpt-oss-120b": dict(gating=L.GX_GATING_SOFTMAX_WEIGHT),
+    "deepseek-v3": dict(gating=L.GX_GATING_SIGMOID, groups=8, group_used=4, norm_w=True, w_scale=2.5),
+}
+
+
+def model_router(model) -> L.gx_router_desc:
+    """The router description of a model family (softmax + renormalised top-k by default)."""
+    kw = ROUTERS.get(model.name, dict(gating=L.GX_GATING_SOFTMAX, norm_w=True))
+    return router_desc(n_expert=model.experts, k=model.used, **kw)
+
+
+def route(desc: L.gx_router_desc, logits, bias=None, n_layers: int = 1, ids=None, weights=None,
+          slot_table=None, slots=None, stream=None):
+    """gx_router_forward on device tensors: logits [n_layers*T, E] -> ids i32
+    and weights f32 [n_layers*T, k] (and slots through a device slot table)."""
+    import torch
+    rows = logits.shape[0]
+    T = rows // n_layers
+    k = desc.n_expert_used
+    if ids is None:
+        ids = torch.empty((rows, k), dtype=torch.int32, device=logits.device)
+    if weights is None:
+        weights = torch.empty((rows, k), dtype=torch.float32, device=logits.device)
+    L.check(L.lib().gx_router_forward(C.byref(desc), _ptr(logits), logits.stride(0), _ptr(bias), T, n_layers,
+                                      _ptr(ids), _ptr(weights), _ptr(slot_table), _ptr(slots), _stream(stream)),
+            "gx_router_forward")
+    return ids, weights
+
+
+def slot_table(arena: "Arena", first_layer: int, n_layers: int, require_all: bool = False, stream=None):
+    """Device i32 [n_layers, E]: the slot of every expert, -1 when not resident."""
+    import torch
+    t = torch.empty((n_layers, arena.model.experts), dtype=torch.int32, device="cuda")
+    L.check(L.lib().gx_arena_slot_table(arena.h, first_layer, n_layers, _ptr(t), 1 if require_all else 0,
+                                        _stream(stream)), "gx_arena_slot_table")
+    return t
 
 
 def ep_owner(placement: int, n_expert: int, world: int, expert: int) -> tuple[int, int]:

@@ -368,6 +368,66 @@ int gx_gguf_moe_info(const char * path, gx_gguf_moe * info);
 int gx_arena_load_gguf(gx_arena * arena, const char * path, uint32_t * records_loaded);
 uint64_t gx_fnv1a64(const void * data, uint64_t n);
 
+/* --------------------------------------------------------------- router
+ * The step before the routed-expert FFN, on the device: router logits
+ * [rows, n_expert] (rows = n_layers * T, layer-major) to the selected expert
+ * ids [rows, k] and their weights [rows, k], as upstream llama.cpp's
+ * build_moe_ffn computes them at the reference's pinned commit
+ * (patches/UPSTREAM-COMMIT.txt; the selection is the view the remap node
+ * receives, patches/galactus-h4-llamacpp.diff:2124-2150, docs/STUDY.md:74):
+ *   gating    SOFTMAX: probs = soft_max(logits); SIGMOID: probs = 1/(1+e^-x);
+ *             SOFTMAX_WEIGHT: probs = logits, softmax over the k weights;
+ *   bias      selection scores = probs + bias[layer] (bias may be NULL);
+ *   groups    n_groups > 1: the n_group_used groups with the largest sum of
+ *             their two best scores keep theirs, the others get -inf;
+ *   top-k     the k best selection scores, best first (a tie goes to the
+ *             lower expert id);
+ *   weights   probs at the selected ids; then SOFTMAX_WEIGHT's softmax; norm_w
+ *             divides by max(sum, 2^-14); scale_w multiplies by w_scale.
+ * Softmax is ggml's arm64 CPU order (exp of x - max, float sums of four
+ * consecutive values accumulated in double, times (float)(1/sum)), with the
+ * library's own expf; the oracle restates it bit for bit. slot_table
+ * [n_layers, n_expert] (device, or NULL) also maps each id to its slot
+ * (gx_arena_slot_table writes it; -1 = not resident, reported through the
+ * device error word). Limits: 1 <= k <= 32, k <= n_expert <= 1024,
+ * n_groups <= 32 with n_expert % n_groups == 0, at least two experts per group
+ * and n_group_used * n_expert / n_groups >= k. Logits must be finite. */
+#define GX_GATING_SOFTMAX 0
+#define GX_GATING_SIGMOID 1
+#define GX_GATING_SOFTMAX_WEIGHT 2
+typedef struct gx_router_desc {
+    int32_t gating;
+    int32_t n_expert;
+    int32_t n_expert_used;
+    int32_t n_groups;       /* <= 1: no group-limited selection */
+    int32_t n_group_used;
+    int32_t norm_w;
+    int32_t scale_w;
+    float w_scale;
+} gx_router_desc;
+/* logits: device f32, row stride ld elements; bias: device f32 [n_layers,
+ * n_expert] or NULL; ids/weights (and slots when slot_table is given): device
+ * [n_layers * T, k]. */
+int gx_router_forward(const gx_router_desc * desc, const float * logits, int64_t ld, const float * bias, int64_t T,
+                      int64_t n_layers, int32_t * ids, float * weights, const int32_t * slot_table, int32_t * slots,
+                      void * stream);
+/* The current slot of every expert of layers [first_layer, first_layer +
+ * n_layers), or -1, written to table (device i32 [n_layers, n_expert]) on
+ * the stream. Returns GX_ERR_STATE if a layer has a non-resident expert and
+ * require_all is set. */
+int gx_arena_slot_table(gx_arena * arena, uint32_t first_layer, uint32_t n_layers, int32_t * table, int require_all,
+                        void * stream);
+/* A stack plan routed on the device: the router writes the plan's ids, slots
+ * and weights (the plan's weight pointers must be consecutive [T, k] slices
+ * of one buffer, w[i] = w[0] + i*T*k), then the plan's graph runs; no host
+ * round trip. Every layer of the plan must be pinned (all of its experts
+ * resident, which holds for good once it does: a layer whose quota covers
+ * all experts never evicts), otherwise GX_ERR_STATE. stats counts every pair
+ * a hit. With a route trace open, the ids are read back after the step and
+ * recorded. ids_out (device i32 [n_layers * T, k] or NULL) receives the ids. */
+int gx_stack_plan_run_routed(gx_stack_plan * plan, const gx_router_desc * desc, const float * logits, int64_t ld,
+                             const float * bias, int32_t * ids_out, void * stream, gx_serve_stats * stats);
+
 /* ---------------------------------------------------------- route trace
  * The route observer of the reference (src/h4/h4-route-observer.hpp:58-304):
  * every micro-batch served through an arena or a policy (layer, tokens, k,

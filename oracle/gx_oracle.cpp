@@ -792,4 +792,131 @@ int orc_synth_weights(int type, void * vdst, int64_t ne00, int64_t n_rows, uint6
     return 0;
 }
 
+
+// ------------------------------------------------------------------ router
+// The router step of upstream llama.cpp's build_moe_ffn (third-party; the
+// reference pins commit da5b4486 in patches/UPSTREAM-COMMIT.txt and patches
+// the function right after it, patches/galactus-h4-llamacpp.diff:2124-2150).
+// Restated from the published graph of that function:
+//   probs = soft_max(logits) | sigmoid(logits) | logits (SOFTMAX_WEIGHT);
+//   selection = probs + exp_probs_b (when a bias is given);
+//   group-limited selection: score of a group = sum of its two best
+//     selection values, the n_group_used best groups kept, others -inf;
+//   selected = the first k of the descending argsort of selection (the view
+//     the remap node reads, docs/STUDY.md:74); ties go to the lower id (the
+//     argsort's comparator leaves them unordered, so this is our choice);
+//   weights = probs at the selected ids; SOFTMAX_WEIGHT: soft_max over the k;
+//     norm_w: divided by clamp(sum_rows, 6.103515625e-5, inf); scale_w: times
+//     w_scale.
+// soft_max is ggml's arm64 CPU order: max, e = exp(x - max) (the library's
+// expf above, in place of ggml's vector exp), float sums of four consecutive
+// e's as ((e0+e1)+(e2+e3)) (vaddvq_f32) accumulated in double in order, the
+// tail one by one, then every e times (float)(1.0/sum). sum_rows accumulates
+// in double in order (the non-Accelerate form); sigmoid is 1/(1+exp(-x)).
+struct orc_router_desc {
+    int32_t gating, n_expert, n_expert_used, n_groups, n_group_used, norm_w, scale_w;
+    float w_scale;
+};
+
+static void router_soft_max(const float * x, float * y, int n) {
+    float m = -INFINITY;
+    for (int i = 0; i < n; ++i) m = x[i] > m ? x[i] : m;
+    double sum = 0.0;
+    int i = 0;
+    for (; i + 3 < n; i += 4) {
+        float v[4];
+        for (int j = 0; j < 4; ++j) v[j] = orc_expf(x[i + j] - m);
+        for (int j = 0; j < 4; ++j) y[i + j] = v[j];
+        sum += (double)((v[0] + v[1]) + (v[2] + v[3]));
+    }
+    for (; i < n; ++i) {
+        const float v = orc_expf(x[i] - m);
+        y[i] = v;
+        sum += (double)v;
+    }
+    const float inv = (float)(1.0 / sum);
+    for (i = 0; i < n; ++i) y[i] = y[i] * inv;
+}
+
+static inline bool router_better(float a, int ia, float b, int ib) { return a > b || (a == b && ia < ib); }
+
+int orc_router_valid(const orc_router_desc * d) {
+    if (d == nullptr) return 0;
+    const int E = d->n_expert, k = d->n_expert_used;
+    if (d->gating < 0 || d->gating > 2) return 0;
+    if (k < 1 || k > 32 || E < k || E > 1024) return 0;
+    if (d->n_groups > 1) {
+        const int G = d->n_groups;
+        if (G > 32 || E % G != 0 || E / G < 2) return 0;
+        if (d->n_group_used < 1 || d->n_group_used > G || d->n_group_used * (E / G) < k) return 0;
+    }
+    return 1;
+}
+
+int orc_router(const orc_router_desc * d, const float * logits, int64_t ld, const float * bias, int64_t T,
+               int64_t n_layers, int32_t * ids, float * weights) {
+    if (!orc_router_valid(d) || T < 0 || n_layers < 0) return -1;
+    const int E = d->n_expert, k = d->n_expert_used;
+    std::vector<float> probs(E), sel(E), w(k);
+    std::vector<char> taken(E);
+    for (int64_t row = 0; row < T * n_layers; ++row) {
+        const float * x = logits + row * ld;
+        const int64_t layer = row / (T > 0 ? T : 1);
+        if (d->gating == 1) {
+            for (int j = 0; j < E; ++j) probs[j] = 1.0f / (1.0f + orc_expf(-x[j]));
+        } else {
+            for (int j = 0; j < E; ++j) probs[j] = x[j];
+            if (d->gating == 0) router_soft_max(probs.data(), probs.data(), E);
+        }
+        for (int j = 0; j < E; ++j) sel[j] = bias ? probs[j] + bias[layer * E + j] : probs[j];
+        if (d->n_groups > 1) {
+            const int G = d->n_groups, gs = E / G;
+            std::vector<float> score(G);
+            for (int g = 0; g < G; ++g) {
+                float t1 = -INFINITY, t2 = -INFINITY;
+                for (int j = 0; j < gs; ++j) {
+                    const float v = sel[g * gs + j];
+                    if (v > t1) {
+                        t2 = t1;
+                        t1 = v;
+                    } else if (v > t2) {
+                        t2 = v;
+                    }
+                }
+                score[g] = t1 + t2;
+            }
+            std::vector<char> keep(G, 0);
+            for (int r = 0; r < d->n_group_used; ++r) {
+                int best = -1;
+                for (int g = 0; g < G; ++g)
+                    if (!keep[g] && (best < 0 || router_better(score[g], g, score[best], best))) best = g;
+                keep[best] = 1;
+            }
+            for (int j = 0; j < E; ++j)
+                if (!keep[j / gs]) sel[j] = -INFINITY;
+        }
+        std::fill(taken.begin(), taken.end(), 0);
+        for (int r = 0; r < k; ++r) {
+            int best = -1;
+            for (int j = 0; j < E; ++j)
+                if (!taken[j] && (best < 0 || router_better(sel[j], j, sel[best], best))) best = j;
+            taken[best] = 1;
+            ids[row * k + r] = best;
+            w[r] = probs[best];
+        }
+        if (d->gating == 2) router_soft_max(w.data(), w.data(), k);
+        if (d->norm_w) {
+            double s = 0.0;
+            for (int r = 0; r < k; ++r) s += (double)w[r];
+            float sf = (float)s;
+            sf = sf > 6.103515625e-5f ? sf : 6.103515625e-5f;
+            for (int r = 0; r < k; ++r) w[r] = w[r] / sf;
+        }
+        if (d->scale_w)
+            for (int r = 0; r < k; ++r) w[r] = w[r] * d->w_scale;
+        for (int r = 0; r < k; ++r) weights[row * k + r] = w[r];
+    }
+    return 0;
+}
+
 }  // extern "C"

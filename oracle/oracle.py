@@ -35,6 +35,14 @@ class LayerDesc(C.Structure):
                 ("off_gate", C.c_int64), ("off_up", C.c_int64), ("record_bytes", C.c_int64), ("n_experts", C.c_int64)]
 
 
+class RouterDesc(C.Structure):
+    """gating (0 softmax, 1 sigmoid, 2 softmax over the selected), experts, k,
+    groups, groups kept, norm_w, scale_w, w_scale (layout of gx_router_desc)."""
+    _fields_ = [("gating", C.c_int32), ("n_expert", C.c_int32), ("n_expert_used", C.c_int32),
+                ("n_groups", C.c_int32), ("n_group_used", C.c_int32), ("norm_w", C.c_int32),
+                ("scale_w", C.c_int32), ("w_scale", C.c_float)]
+
+
 _P = C.c_void_p
 _I64 = C.c_int64
 _lib = None
@@ -67,6 +75,10 @@ def lib():
         h.orc_moe_layer.restype = C.c_int
         h.orc_moe_layer.argtypes = [C.POINTER(LayerDesc), _P, _P, _P, _P, _I64, _I64, _P, C.c_int]
         h.orc_set_iq1s_grid.argtypes = [_P]
+        h.orc_router_valid.restype = C.c_int
+        h.orc_router_valid.argtypes = [C.POINTER(RouterDesc)]
+        h.orc_router.restype = C.c_int
+        h.orc_router.argtypes = [C.POINTER(RouterDesc), _P, _I64, _P, _I64, _I64, _P, _P]
         h.orc_synth_normal.argtypes = [_P, _I64, C.c_uint64, C.c_uint64, C.c_float]
         h.orc_synth_weights.restype = C.c_int
         h.orc_synth_weights.argtypes = [C.c_int, _P, _I64, _I64, C.c_uint64, C.c_uint64, C.c_float]
@@ -144,6 +156,24 @@ def combine(y: np.ndarray, w: np.ndarray) -> np.ndarray:
     out = np.zeros((T, H), dtype=np.float32)
     lib().orc_combine(y.ctypes.data, w.ctypes.data, out.ctypes.data, H, k, T)
     return out
+
+
+def router(desc: RouterDesc, logits: np.ndarray, bias: np.ndarray | None = None,
+           n_layers: int = 1) -> tuple[np.ndarray, np.ndarray]:
+    """logits f32 [n_layers*T, E], bias f32 [n_layers, E] or None ->
+    ids int32 [n_layers*T, k], weights f32 [n_layers*T, k]"""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    rows, E = logits.shape
+    T = rows // n_layers
+    k = desc.n_expert_used
+    ids = np.zeros((rows, k), np.int32)
+    w = np.zeros((rows, k), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    rc = lib().orc_router(C.byref(desc), logits.ctypes.data, E, None if b is None else b.ctypes.data, T, n_layers,
+                          ids.ctypes.data, w.ctypes.data)
+    if rc != 0:
+        raise ValueError("oracle router: invalid description")
+    return ids, w
 
 
 def mul_mat_id(t: int, experts: np.ndarray, ne00: int, ne01: int, b: np.ndarray, ids: np.ndarray,

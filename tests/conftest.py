@@ -44,3 +44,11 @@ def orc():
     o.build()
     o.lib()
     return o
+
+
+@pytest.fixture(scope="session")
+def dev(gxlib):
+    """cuda:0 with the library's device state initialised."""
+    import torch
+    gxlib.check(gxlib.lib().gx_device_init(0), "gx_device_init")
+    return torch.device("cuda:0")

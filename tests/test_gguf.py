@@ -85,7 +85,8 @@ def test_gguf_rejects_non_gguf_and_dense(gxlib, tmp_path):
 @pytest.mark.parametrize("name", ["qwen3-30b", "gpt-oss-120b"])
 def test_gguf_loads_the_tier(gxlib, orc, dev, tmp_path, name):
     from galactus_b200.models import ModelShape
-    m = ModelShape(**{**gxlib.MODELS[name].__dict__, "experts": 5, "layers": 2})
+    base = gxlib.MODELS[name]
+    m = ModelShape(**{**base.__dict__, "experts": base.used + 2, "layers": 2})
     path = tmp_path / "m.gguf"
     _write_moe_gguf(path, m, orc, layers=2)
     arena = gxlib.Arena(m, capacity_bytes=m.experts * m.record * m.layers, policy=gxlib.POLICY_AUTO, max_tokens=1)

@@ -18,12 +18,6 @@ SHAPES = {
 }
 
 
-@pytest.fixture(scope="module")
-def dev(gxlib):
-    gxlib.check(gxlib.lib().gx_device_init(0), "gx_device_init")
-    return torch.device("cuda:0")
-
-
 def D(a):
     return torch.from_numpy(np.ascontiguousarray(a)).to("cuda")
 
