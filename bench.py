@@ -204,8 +204,8 @@ def run_ours(args):
     import torch.distributed as dist
 
     import galactus_b200 as gx
-    from galactus_b200.moe import StackCall, StackPlan, device_error
-    from galactus_b200.routing import routes
+    from galactus_b200.moe import StackCall, StackPlan, device_error, model_router
+    from galactus_b200.routing import logits, routes
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -384,6 +384,35 @@ def run_ours(args):
         results["e2e"] = {"value": world * args.steps / (ms_e2e / 1e3), "unit": "tok/s",
                           "h2d_bytes_per_step": NL * H * 4 + NL * k * 4, "d2h_bytes_per_step": NL * H * 4}
 
+        # ---------------- e2e with the router on the device: per step the
+        # hidden states and router logits go host->device, the router writes
+        # ids, slots and weights for the pinned layers, the stack runs, the
+        # outputs come back; no host remap in the loop
+        rdesc = model_router(model)
+        h_lg = torch.from_numpy(logits(model, P, NL, seed=model.seed * 1000 + 29 + rank, rho=0.7)).pin_memory()
+        lg_fix = torch.empty((NL, E), dtype=torch.float32, device=dev)
+
+        def run_routed(t_first, n):
+            for i in range(n):
+                t = t_first + i
+                x_fix.copy_(h_x[t % P], non_blocking=True)
+                lg_fix.copy_(h_lg[t % P], non_blocking=True)
+                plan.run_routed(rdesc, lg_fix, stream=stream)
+                h_out[t % P].copy_(out_dev, non_blocking=True)
+
+        run_routed(0, args.warmup)
+        torch.cuda.synchronize()
+        barrier()
+        ev0.record(stream)
+        run_routed(args.warmup, args.steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ms_routed = max_over_ranks(ev0.elapsed_time(ev1))
+        barrier()
+        results["e2e_device_router"] = {"value": world * args.steps / (ms_routed / 1e3), "unit": "tok/s",
+                                        "h2d_bytes_per_step": NL * H * 4 + NL * E * 4,
+                                        "d2h_bytes_per_step": NL * H * 4}
+
         plan_info = plan.info()
         results["layerwise_graph_tok_s"] = results["layer_path_tok_s"] = None
 
@@ -504,18 +533,24 @@ def run_ours(args):
     if tp.exists():
         traffic = json.loads(tp.read_text()).get(args.model, {}).get(dom.split(" ")[0])
 
+    tn = gx.TYPE_NAMES
+    wtypes = tn[model.type_gate] if model.type_gate == model.type_down else \
+        f"{tn[model.type_gate]} gate/up + {tn[model.type_down]} down"
+    atypes = "/".join(sorted({"q8_0" if t in (gx.TYPE_Q8_0, gx.TYPE_MXFP4) else "q8_K"
+                              for t in (model.type_gate, model.type_down)}))
     line = {
-        "metric": "MoE-layer decode tok/s (48-layer routed-expert FFN stack, full slot residency)",
+        "metric": f"MoE-layer decode tok/s ({NL}-layer routed-expert FFN stack, full slot residency)",
         "value": results["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": results["ms_per_step"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8 dot / f32 tail (Q8_0 weights, Q8_0 activations)",
-        "data": "synthetic (seeded N(0,0.02) weights quantized to Q8_0; Zipf(1.1)+AR(0.7) routes; N(0,1) states)",
+        "vs_baseline": None, "dtype": f"int8 dot / f32 tail ({wtypes} weights, {atypes} activations)",
+        "data": f"synthetic (seeded {wtypes} weights; Zipf(1.1)+AR(0.7) routes; N(0,1) states)",
         "config": {"workload": f"{model.name} MoE stack, batch-1 decode, {NL} layers, H {H}, E {E}, top-{k}, I {I}, "
-                               f"Q8_0, slot cache 100%", "model": model.name, "global_batch": world,
+                               f"{wtypes}, slot cache 100%", "model": model.name, "global_batch": world,
                    "seq_len": 1, "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": f"inputs larger than L2: ~{NL * k * model.record_raw / 1e9:.2f} GB of expert weights read "
                          f"per step vs 126 MB L2, no flush"},
         "e2e": results["e2e"],
+        "e2e_device_router": results["e2e_device_router"],
         "gpu_launches": (1 if plan_info["stack_kernel"] else 3 * NL) * args.steps,
         "plan": plan_info,
         "layerwise_graph_tok_s": results["layerwise_graph_tok_s"],

@@ -1086,6 +1086,10 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     sp.act = l0.g.act;
     sp.alpha = l0.g.alpha;
     sp.limit = l0.g.limit;
+    sp.row_mode = (l0.type_gate == gx::GX_T_Q8_0 && l0.type_down == gx::GX_T_Q8_0)   ? 0
+                  : (l0.type_gate == gx::GX_T_Q4_K && l0.type_down == gx::GX_T_Q6_K) ? 2
+                                                                                     : 1;
+    sp.gu_copies = sp.row_mode == 1 ? 2 : 4;
     int threads = 0;
     uint32_t smem = 0;
     if (!choose_stack_tiles(sp, threads, smem)) return GX_ERR_ALIGN;

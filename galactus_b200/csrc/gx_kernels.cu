@@ -728,34 +728,46 @@ cudaError_t launch_quant_split(int vdt, const float * src, int ne0, int64_t nrow
 
 int device_sms() { return device_sm_count(); }
 
-bool stack_types_supported(int type_gate, int type_down) { return type_gate == GX_T_Q8_0 && type_down == GX_T_Q8_0; }
+bool stack_types_supported(int type_gate, int type_down) {
+    return (type_gate == GX_T_Q8_0 && type_down == GX_T_Q8_0) || (type_gate == GX_T_Q4_K && type_down == GX_T_Q6_K) ||
+           (type_gate == GX_T_MXFP4 && type_down == GX_T_MXFP4) || (type_gate == GX_T_IQ1_S && type_down == GX_T_IQ1_S);
+}
 
 // Bulk-copy mode of one role: rows of a multiple of 128 bytes get 16 bytes of
-// padding against bank conflicts and one copy per row; other 16-byte rows
-// are copied as one tile per expert.
+// padding against bank conflicts and one copy per row; other rows are copied
+// as one tile of R rows per expert (R rows must make whole 16-byte chunks).
 static bool stack_copy_mode(int64_t nb01, int R, int32_t & row_copy, int32_t & pitch) {
-    if (nb01 % 16 != 0 || (R * nb01) % 16 != 0) return false;
+    if ((R * nb01) % 16 != 0) return false;
     row_copy = nb01 % 128 == 0 ? 1 : 0;
     pitch = (int32_t)(row_copy ? nb01 + 16 : nb01);
     return true;
 }
 
 // Shared-memory layout of the stack kernel; 0 when the shape is not covered.
-// Q8_0 jobs: 8 gate + 8 up rows (two lanes per row) or k*Rd = 32 down rows
-// (two rows per lane pair); rows of K % 256 == 0 elements, 16-byte aligned.
+// Jobs: 8 gate + 8 up rows, or k*Rd = 32 down rows. Row modes: 0 two-lane
+// Q8_0 rows, 2 two-lane Q4_K gate/up and Q6_K down rows (both in 4 staggered
+// gate/up tiles and rows of K % 256 == 0), 1 octet rows (any whole number
+// of their type's 64- or 256-element units, checked per layer; 2 gate/up copies).
 uint32_t stack_layout(StackParams & p, int & threads) {
     if (p.Rg != 8 || p.Rd < 1 || p.k * p.Rd != 32) return 0;
-    if (p.H % 256 || p.I % 256 || p.I % p.Rg || p.qblk % p.Rg || p.H % p.Rd) return 0;
+    if (p.row_mode < 0 || p.row_mode > 2 || p.gu_copies != (p.row_mode == 1 ? 2 : 4)) return 0;
+    const int ra = p.row_mode == 1 ? 64 : 256;
+    if (p.H % ra || p.I % ra || p.I % p.Rg || p.qblk % p.Rg || p.H % p.Rd) return 0;
     if (p.C < 1 || p.C > kStackMaxConsumers || p.NL < 1 || p.NL > kStackMaxLayers) return 0;
     if (p.W < 1 || p.W > kStackMaxWarps) return 0;
+    if (p.row_mode == 1 && (p.Rd & 1)) return 0;   // octet row pairs stay inside one expert
     threads = 96 + 32 * p.W;
-    if (p.nb01_g % 16 != 0) return 0;
     if (!stack_copy_mode(p.nb01_d, p.Rd, p.row_copy_d, p.pitch_d)) return 0;
-    // gate/up tiles: tile t starts at a 16-byte chunk index = {0, 1, 4, 5}[t]
-    // mod 8; a quarter warp reads one row of each tile at both parities
-    // (+32 bytes), i.e. chunk groups {0,2}, {1,3}, {4,6}, {5,7}
-    {
-        static const int xs[4] = {0, 1, 4, 5};
+    uint64_t gw;
+    if (p.gu_copies == 4) {
+        // gate/up tiles: tile t starts at a 16-byte chunk index xs[t] mod 8; a
+        // quarter warp reads one row of each tile at both lane halves. Q8_0
+        // halves are 32 bytes apart: xs = {0, 1, 4, 5} gives chunk groups
+        // {0,2}, {1,3}, {4,6}, {5,7}; Q4_K halves are 16 bytes apart:
+        // xs = {0, 2, 4, 6} gives {0,1}, {2,3}, {4,5}, {6,7}
+        if (p.nb01_g % 16 != 0) return 0;
+        static const int xs0[4] = {0, 1, 4, 5}, xs2[4] = {0, 2, 4, 6};
+        const int * xs = p.row_mode == 2 ? xs2 : xs0;
         const uint64_t tile = 4ull * (uint64_t)p.nb01_g;
         p.gu_tile[0] = 0;
         for (int t = 1; t < 4; ++t) {
@@ -763,9 +775,18 @@ uint32_t stack_layout(StackParams & p, int & threads) {
             while (c % 8 != (uint64_t)xs[t]) ++c;
             p.gu_tile[t] = (int32_t)(c * 16);
         }
+        gw = (uint64_t)p.gu_tile[3] + 4ull * (uint64_t)p.nb01_g;
+    } else {
+        // octet rows: the 8 gate rows, then the 8 up rows, one copy each
+        const uint64_t tile = 8ull * (uint64_t)p.nb01_g;
+        if (tile % 16 != 0) return 0;
+        p.gu_tile[0] = 0;
+        p.gu_tile[1] = (int32_t)tile;
+        p.gu_tile[2] = p.gu_tile[3] = 0;
+        gw = 2 * tile + 16;   // ld_words may read one word past a row
     }
-    const uint64_t gw = (uint64_t)p.gu_tile[3] + 4ull * (uint64_t)p.nb01_g;
-    const uint64_t dw = (uint64_t)p.k * p.Rd * (uint64_t)p.pitch_d;
+    // the unaligned row readers (octet rows, Q6_K) may read one word past the last row
+    const uint64_t dw = (uint64_t)p.k * p.Rd * (uint64_t)p.pitch_d + (p.row_mode != 0 ? 16 : 0);
     p.stage_bytes = (int32_t)align_up(gw > dw ? gw : dw, 128);
     p.bar_off = 0;      // 3*C + 2*kStackBufs mbarriers
     p.meta_off = 256;   // metadata word and release counter per stage, buffer counters
@@ -773,7 +794,8 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     p.xbuf_off = p.stage_off + (uint32_t)p.C * (uint32_t)p.stage_bytes;
     p.dbuf_off = p.xbuf_off + align_up((uint64_t)kStackBufs * p.alx.pitch, 128);
     p.wt_off = p.dbuf_off + align_up((uint64_t)kStackBufs * p.k * p.ald.pitch, 128);
-    p.slots_off = p.wt_off + (uint32_t)p.NL * 32u;   // per-layer weight bases
+    p.dots_off = p.wt_off + (uint32_t)p.NL * 32u;    // per-layer weight bases
+    p.slots_off = p.dots_off + (uint32_t)p.W * 32u * 4u;   // 32 down-row dots per consumer warp
     const uint32_t total = p.slots_off + align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
     return total <= kMaxSmem ? total : 0;
 }
@@ -799,6 +821,11 @@ static cudaError_t stack_dispatch(const StackParams * p, int grid, int threads, 
 static cudaError_t stack_switch(int tg, int td, const StackParams * p, int grid, int threads, uint32_t smem,
                                 cudaStream_t stream, int * per_sm) {
     if (tg == GX_T_Q8_0 && td == GX_T_Q8_0) return stack_dispatch<GX_T_Q8_0, GX_T_Q8_0>(p, grid, threads, smem, stream, per_sm);
+    if (tg == GX_T_Q4_K && td == GX_T_Q6_K) return stack_dispatch<GX_T_Q4_K, GX_T_Q6_K>(p, grid, threads, smem, stream, per_sm);
+    if (tg == GX_T_MXFP4 && td == GX_T_MXFP4)
+        return stack_dispatch<GX_T_MXFP4, GX_T_MXFP4>(p, grid, threads, smem, stream, per_sm);
+    if (tg == GX_T_IQ1_S && td == GX_T_IQ1_S)
+        return stack_dispatch<GX_T_IQ1_S, GX_T_IQ1_S>(p, grid, threads, smem, stream, per_sm);
     return cudaErrorInvalidValue;
 }
 

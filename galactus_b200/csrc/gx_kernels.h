@@ -116,7 +116,7 @@ struct StackLayer {
 };
 
 constexpr int kStackMaxConsumers = 8;   // ring stages
-constexpr int kStackMaxWarps = 10;      // consumer warps
+constexpr int kStackMaxWarps = 13;      // consumer warps
 constexpr int kStackMaxLayers = 128;   // the layer table travels in the kernel parameters
 constexpr int kStackBufs = 2;          // activation buffers per kind (gate/up inputs, down inputs)
 
@@ -131,15 +131,18 @@ struct StackParams {
     int32_t W;                 // consumer warps (may exceed C)
     int32_t skew;              // down jobs of layer L follow the gate/up jobs of layer L+skew
     int32_t row_copy_d, pitch_d;
-    int32_t gu_tile[4];        // gate/up job: 4 tiles of 4 rows (gate 0-3, 4-7, up 0-3, 4-7) at these
-                               // stage offsets, staggered so quarter-warp loads hit distinct bank groups
+    int32_t row_mode;          // 0: two-lane Q8_0 rows, 1: octet rows, 2: two-lane Q4_K/Q6_K rows
+    int32_t gu_copies;         // 4 (modes 0, 2): gate/up job in 4 tiles of 4 rows (gate 0-3, 4-7, up 0-3,
+                               //    4-7) at gu_tile[0..3], staggered so quarter-warp loads hit distinct
+                               //    bank groups; 2 (mode 1): gate rows 0-7 at gu_tile[0], up rows at gu_tile[1]
+    int32_t gu_tile[4];
     int32_t stage_bytes;       // weight rows of one job
     ActLayout alx, ald;        // layouts of xq rows and actq rows
     int32_t qblk;              // elements per Q8 block of the down input
     int32_t n_gu, n_d;         // gate/up and down jobs per layer
     int32_t act;
     float alpha, limit;
-    uint32_t bar_off, meta_off, stage_off, xbuf_off, dbuf_off, wt_off, slots_off;
+    uint32_t bar_off, meta_off, stage_off, xbuf_off, dbuf_off, wt_off, slots_off, dots_off;
     StackLayer layers[kStackMaxLayers];
 };
 

@@ -32,6 +32,13 @@
 // error, and on giving up records GX_DEVERR_TIMEOUT; producers then let their
 // copies in flight land (bounded) before the CTA exits.
 //
+// Other block types (Q4_K gate/up with Q6_K down, MXFP4, IQ1_S) use the
+// octet row dots of the per-layer kernels (eight lanes per row, two rows per
+// lane, gx_moe.cuh): a gate/up job is two passes over gate row i and up row i
+// together (octet g takes i = 4*pass + g), a down job four passes over row
+// pairs (2g, 2g+1) of one expert; the down dots go through a per-warp scratch
+// to the combine. Their activations are Q8_K (256-element blocks) or Q8_0.
+//
 // Q8_0 rows (the gate/up/down type of Q8_0 models): two lanes per weight row,
 // one per block parity. Lane p owns the four NEON accumulator chains of the
 // blocks 2u+p (diff:1049-1054: per-lane int32 partial of words j and 4+j,
@@ -157,7 +164,7 @@ struct StackWeights {
 // Row-copy geometry of the weight producer (registers).
 struct StackCopy {
     int64_t nb01_g, nb01_d;
-    int pitch_d, row_copy_d, T, k, Rg, Rd;
+    int pitch_d, row_copy_d, T, k, Rg, Rd, gu_copies;
     int tile[4];
 };
 
@@ -264,12 +271,20 @@ __device__ __forceinline__ void stack_issue_weights(const StackCopy & q, const S
     const StackWeights ly = wt[J.L];
     const int32_t * sl = slots + J.L * q.T * q.k;
     if (J.gu) {
-        // 4 tiles of 4 rows: gate rows r0..r0+3, r0+4..r0+7, then up rows
         const int64_t off = (int64_t)sl[J.pair] * ly.nb02 + (int64_t)J.r0 * q.nb01_g;
-        const uint32_t tile = (uint32_t)(4 * q.nb01_g);
-        tma_expect(bar, 4u * tile);
-        for (int t = 0; t < 4; ++t)
-            tma_load(stage + q.tile[t], (t < 2 ? ly.wg : ly.wu) + off + (int64_t)(t & 1) * tile, tile, bar);
+        if (q.gu_copies == 4) {
+            // 4 tiles of 4 rows: gate rows r0..r0+3, r0+4..r0+7, then up rows
+            const uint32_t tile = (uint32_t)(4 * q.nb01_g);
+            tma_expect(bar, 4u * tile);
+            for (int t = 0; t < 4; ++t)
+                tma_load(stage + q.tile[t], (t < 2 ? ly.wg : ly.wu) + off + (int64_t)(t & 1) * tile, tile, bar);
+        } else {
+            // gate rows r0..r0+7, then up rows r0..r0+7
+            const uint32_t tile = (uint32_t)(8 * q.nb01_g);
+            tma_expect(bar, 2u * tile);
+            tma_load(stage + q.tile[0], ly.wg + off, tile, bar);
+            tma_load(stage + q.tile[1], ly.wu + off, tile, bar);
+        }
     } else {
         const uint32_t bytes = (uint32_t)(q.Rd * q.nb01_d);
         tma_expect(bar, (uint32_t)q.k * bytes);
@@ -282,6 +297,188 @@ __device__ __forceinline__ void stack_issue_weights(const StackCopy & q, const S
             } else {
                 tma_load(dst, src, bytes, bar);
             }
+        }
+    }
+}
+
+// Q4_K row x Q8_K activation row (split layout), two lanes per row
+// (ggml_vec_dot_q4_K_q8_K, diff:1254-1259, 1300-1357). Lane half p takes
+// bytes 16p..16p+15 of every 32-byte quant group j, i.e. the 16-element runs
+// 64j+16p.. (low nibbles, sub-block 2j) and 64j+32+16p.. (high nibbles,
+// sub-block 2j+1), and the block sums bs[2o+p] of the mins. The exact integer
+// parts of a superblock are summed with the partner lane (lane ^ xm), then
+// both lanes run the superblock chain in order:
+//   sumf = fma(-(yd*fp16(dmin)), prod, sumf); sumf = fma(yd*fp16(d), sumi, sumf).
+__device__ __forceinline__ float q4k_row2(const uint8_t * row, const uint8_t * act, const ActLayout & al, int p, int nsb,
+                                          int xm) {
+    float sumf = 0.0f;
+    const uint8_t * aq = act + 16 * p;
+    for (int i = 0; i < nsb; ++i) {
+        const uint8_t * xb = row + 144 * i;
+        const uint4 hdr = lds128(xb);   // d | dmin, scale bytes 0-3, 4-7, 8-11
+        int sumi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint4 q = lds128(xb + 16 + 32 * j + 16 * p);
+            const uint4 lo = lds128(aq + 256 * i + 64 * j);
+            const uint4 hi = lds128(aq + 256 * i + 64 * j + 32);
+            int p1 = dp4a(q.x & 0x0f0f0f0fu, lo.x, 0);
+            p1 = dp4a(q.y & 0x0f0f0f0fu, lo.y, p1);
+            p1 = dp4a(q.z & 0x0f0f0f0fu, lo.z, p1);
+            p1 = dp4a(q.w & 0x0f0f0f0fu, lo.w, p1);
+            int p2 = dp4a((q.x >> 4) & 0x0f0f0f0fu, hi.x, 0);
+            p2 = dp4a((q.y >> 4) & 0x0f0f0f0fu, hi.y, p2);
+            p2 = dp4a((q.z >> 4) & 0x0f0f0f0fu, hi.z, p2);
+            p2 = dp4a((q.w >> 4) & 0x0f0f0f0fu, hi.w, p2);
+            const int a0 = 2 * j, a1 = 2 * j + 1;
+            const int sc0 = a0 < 4 ? (int)((hdr.y >> (8 * a0)) & 63u)
+                                   : (int)(((hdr.w >> (8 * (a0 - 4))) & 0x0fu) | (((hdr.y >> (8 * (a0 - 4) + 6)) & 3u) << 4));
+            const int sc1 = a1 < 4 ? (int)((hdr.y >> (8 * a1)) & 63u)
+                                   : (int)(((hdr.w >> (8 * (a1 - 4))) & 0x0fu) | (((hdr.y >> (8 * (a1 - 4) + 6)) & 3u) << 4));
+            sumi += p1 * sc0 + p2 * sc1;
+        }
+        int prod = 0;
+        const uint8_t * bsp = act + al.bs_off + 32 * i;
+#pragma unroll
+        for (int o = 0; o < 8; ++o) {
+            const int mn = o < 4 ? (int)((hdr.z >> (8 * o)) & 63u)
+                                 : (int)(((hdr.w >> (8 * (o - 4) + 4)) & 0x0fu) | (((hdr.z >> (8 * (o - 4) + 6)) & 3u) << 4));
+            const int bs = (int)(int16_t)((lds32(bsp + 4 * o) >> (16 * p)) & 0xffffu);
+            prod += bs * mn;
+        }
+        sumi += __shfl_xor_sync(0xffffffffu, sumi, xm);
+        prod += __shfl_xor_sync(0xffffffffu, prod, xm);
+        const float yd = __uint_as_float(lds32(act + al.d_off + 4 * i));
+        sumf = __fmaf_rn(-__fmul_rn(yd, h2f((uint16_t)(hdr.x >> 16))), (float)prod, sumf);
+        sumf = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(hdr.x & 0xffffu))), (float)sumi, sumf);
+    }
+    return sumf;
+}
+
+// Q6_K row x Q8_K activation row (split layout), two lanes per row
+// (ggml_vec_dot_q6_K_q8_K, diff:1366-1370, 1393-1446). Lane half p takes the
+// 32-element half p of every 64-element quarter j: groups 4j+2p and 4j+2p+1,
+// quants ql bytes 64(j/2)+32p.. (nibble 4*(j&1)) with qh bytes 128+32(j/2)..
+// (bits 4*(j&1)+2p). Superblocks are 210 bytes, so odd ones sit two bytes off
+// a word and are realigned with funnel shifts. isum and mins are summed with
+// the partner lane (lane ^ xm), then sumf = fma(yd*fp16(d), isum - 32*mins, sumf).
+__device__ __forceinline__ float q6k_row2(const uint8_t * row, const uint8_t * act, const ActLayout & al, int p, int nsb,
+                                          int xm) {
+    float sumf = 0.0f;
+    for (int i = 0; i < nsb; ++i) {
+        const int xo = 210 * i;
+        const uint8_t * wb = row + (xo & ~3);
+        const uint32_t sh = (uint32_t)(xo & 3) * 8u;   // 0 or 16
+        const int base = xo & 3;                       // bytes of the block start inside the first word
+        (void)base;
+        uint32_t sc4[4];
+        {
+            uint32_t w[5];
+#pragma unroll
+            for (int k = 0; k < 5; ++k) w[k] = lds32(wb + 192 + 4 * k);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sc4[k] = __funnelshift_r(w[k], w[k + 1], sh);
+        }
+        const uint32_t dw = __funnelshift_r(lds32(wb + 208), lds32(wb + 212), sh);
+        int isum = 0, mins = 0;
+        const uint8_t * bsp = act + al.bs_off + 32 * i;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t ql[8], qh[8];
+            {
+                uint32_t w[9];
+#pragma unroll
+                for (int k = 0; k < 9; ++k) w[k] = lds32(wb + 64 * h + 32 * p + 4 * k);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) ql[k] = __funnelshift_r(w[k], w[k + 1], sh);
+#pragma unroll
+                for (int k = 0; k < 9; ++k) w[k] = lds32(wb + 128 + 32 * h + 4 * k);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) qh[k] = __funnelshift_r(w[k], w[k + 1], sh);
+            }
+#pragma unroll
+            for (int odd = 0; odd < 2; ++odd) {
+                const int j = 2 * h + odd;
+                const uint8_t * ap = act + 256 * i + 64 * j + 32 * p;
+                const uint4 a0 = lds128(ap), a1 = lds128(ap + 16);
+                const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const uint32_t qsh = 4u * (uint32_t)odd + 2u * (uint32_t)p;
+                int pg[2] = {0, 0};
+#pragma unroll
+                for (int ww = 0; ww < 8; ++ww) {
+                    const uint32_t nib = (ql[ww] >> (4 * odd)) & 0x0f0f0f0fu;
+                    const uint32_t hb = (qh[ww] >> qsh) & 0x03030303u;
+                    pg[ww >> 2] = dp4a(nib | (hb << 4), aw[ww], pg[ww >> 2]);
+                }
+                // groups 4j+2p and 4j+2p+1: scale bytes 4j+2p, 4j+2p+1
+                const uint32_t sw = sc4[j] >> (16 * p);
+                const int s0 = (int)(int8_t)(sw & 0xffu), s1 = (int)(int8_t)((sw >> 8) & 0xffu);
+                const uint32_t bw = lds32(bsp + 8 * j + 4 * p);
+                isum += pg[0] * s0 + pg[1] * s1;
+                mins += (int)(int16_t)(bw & 0xffffu) * s0 + (int)(int16_t)(bw >> 16) * s1;
+            }
+        }
+        isum += __shfl_xor_sync(0xffffffffu, isum, xm);
+        mins += __shfl_xor_sync(0xffffffffu, mins, xm);
+        const float yd = __uint_as_float(lds32(act + al.d_off + 4 * i));
+        sumf = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dw & 0xffffu))), (float)(isum - 32 * mins), sumf);
+    }
+    return sumf;
+}
+
+// Octet gate/up job: gate row i and up row i (octet g, i = 4*pass + g)
+// against the token's activation row; every lane of octet g ends with the
+// two dots of row 4*pass + g.
+template <int TYPE>
+__device__ __forceinline__ void stack_gu_oct(const StackParams & p, const uint8_t * st, const uint8_t * xa, int lane,
+                                             float (&gd)[2], float (&ud)[2]) {
+    using Q = Oct<TYPE>;
+    const int o = lane & 7, g = lane >> 3;
+    const int U = p.H / Q::UNIT;
+    const typename Q::A al = Q::inita(xa, p.alx, o);
+#pragma unroll
+    for (int ps = 0; ps < 2; ++ps) {
+        const int row = 4 * ps + g;
+        typename Q::St acc[2];
+        const typename Q::W wl[2] = {Q::initw(st, p.gu_tile[0] + row * (int)p.nb01_g, o),
+                                     Q::initw(st, p.gu_tile[1] + row * (int)p.nb01_g, o)};
+        int v = 0;
+        for (; v + 1 < U; v += 2) {
+            Q::template unit<0>(wl, al, v, acc);
+            Q::template unit<1>(wl, al, v + 1, acc);
+        }
+        if (v < U) Q::template unit<0>(wl, al, v, acc);
+        gd[ps] = Q::finish(acc[0]);
+        ud[ps] = Q::finish(acc[1]);
+    }
+}
+
+// Octet down job: k*Rd rows in passes of eight; octet g takes rows
+// 8*pass + 2g and 8*pass + 2g + 1 (one expert, Rd even) against that
+// expert's activation row; lane 8g writes both dots to dots[row].
+template <int TYPE>
+__device__ __forceinline__ void stack_d_oct(const StackParams & p, const uint8_t * st, const uint8_t * da, int lane,
+                                            float * dots) {
+    using Q = Oct<TYPE>;
+    const int o = lane & 7, g = lane >> 3;
+    const int U = p.I / Q::UNIT;
+    const int passes = p.k * p.Rd / 8;
+    for (int ps = 0; ps < passes; ++ps) {
+        const int row = 8 * ps + 2 * g;
+        const typename Q::A al = Q::inita(da + (row / p.Rd) * p.ald.pitch, p.ald, o);
+        typename Q::St acc[2];
+        const typename Q::W wl[2] = {Q::initw(st, row * p.pitch_d, o), Q::initw(st, (row + 1) * p.pitch_d, o)};
+        int v = 0;
+        for (; v + 1 < U; v += 2) {
+            Q::template unit<0>(wl, al, v, acc);
+            Q::template unit<1>(wl, al, v + 1, acc);
+        }
+        if (v < U) Q::template unit<0>(wl, al, v, acc);
+        const float d0 = Q::finish(acc[0]);
+        const float d1 = Q::finish(acc[1]);
+        if (o == 0) {
+            dots[row] = d0;
+            dots[row + 1] = d1;
         }
     }
 }
@@ -372,7 +569,9 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
 
 template <int TG, int TD>
 __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __grid_constant__ StackParams p) {
-    static_assert(TG == GX_T_Q8_0 && TD == GX_T_Q8_0, "stack kernel rows: Q8_0");
+    // row mode: 0 two-lane Q8_0 rows, 2 two-lane Q4_K gate/up + Q6_K down rows, 1 octet rows
+    constexpr int kMode = (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0 : (TG == GX_T_Q4_K && TD == GX_T_Q6_K) ? 2 : 1;
+    constexpr int VG = Oct<TG>::VDT, VD = Oct<TD>::VDT;       // activation types of gate/up and down
     extern __shared__ __align__(128) uint8_t smem[];
     const int C = p.C;
     uint64_t * wfull = reinterpret_cast<uint64_t *>(smem + p.bar_off);
@@ -438,6 +637,7 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
         q.k = p.k;
         q.Rg = p.Rg;
         q.Rd = p.Rd;
+        q.gu_copies = kMode == 1 ? 2 : 4;
         for (int t = 0; t < 4; ++t) q.tile[t] = p.gu_tile[t];
         const int stage_bytes = p.stage_bytes;
         StackWalk walk{0, 0};
@@ -480,14 +680,13 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
     if (c >= W) return;
     // quantize the inputs of layers L = b, b+G, ... (one warp per Q8 block)
     {
-        const int nblk = p.H / 32;
+        const int nblk = p.H / (VG == GX_T_Q8_0 ? 32 : 256);
         bool any = false;
         for (int L = b; L < p.NL; L += G) {
             const StackLayer & ly = p.layers[L];
             for (int wi = c; wi < p.T * nblk; wi += W) {
                 const int t = wi / nblk, ib = wi - t * nblk;
-                quant_block_split<GX_T_Q8_0, false>(ly.x + (int64_t)t * p.H, ly.xq + (int64_t)t * p.alx.pitch, p.alx, ib,
-                                                    lane);
+                quant_block_split<VG, false>(ly.x + (int64_t)t * p.H, ly.xq + (int64_t)t * p.alx.pitch, p.alx, ib, lane);
             }
             any = true;
         }
@@ -534,30 +733,62 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
         const uint8_t * st = stages + cs * p.stage_bytes;
         int * done = bufdone + (J.gu ? 0 : kStackBufs) + bi;
         if (J.gu) {
-            // lane = qr*8 + tile*2 + gp: row qr of tile `tile` (gate rows 4*tile+qr
-            // for tiles 0, 1; up rows 4*(tile-2)+qr for tiles 2, 3), block parity gp
-            const int qr = lane >> 3, tl = (lane >> 1) & 3, gp = lane & 1;
             const uint8_t * xa = xbuf + bi * xbytes;
-            const uint8_t * rb[1] = {st + p.gu_tile[tl] + qr * (int)p.nb01_g + 32 * gp};
-            const uint8_t * ab[1] = {xa + 32 * gp};
-            const uint8_t * ad[1] = {xa + p.alx.d_off};
-            float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-            q8_0_rows<1>(rb, ab, ad, gp, p.H / 64, acc);
-            __syncwarp();
-            if (lane == 0) {
-                __threadfence_block();
-                atomicAdd(done, 1);
-                atomicAdd(rel + cs, 1);
-                mbar_arrive(empty + cs);   // stage and input buffer are free
+            if constexpr (kMode != 1) {
+                // lane = qr*8 + tile*2 + gp: row qr of tile `tile` (gate rows 4*tile+qr
+                // for tiles 0, 1; up rows 4*(tile-2)+qr for tiles 2, 3), lane half gp
+                const int qr = lane >> 3, tl = (lane >> 1) & 3, gp = lane & 1;
+                float dot;
+                if constexpr (kMode == 0) {
+                    const uint8_t * rb[1] = {st + p.gu_tile[tl] + qr * (int)p.nb01_g + 32 * gp};
+                    const uint8_t * ab[1] = {xa + 32 * gp};
+                    const uint8_t * ad[1] = {xa + p.alx.d_off};
+                    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+                    q8_0_rows<1>(rb, ab, ad, gp, p.H / 64, acc);
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence_block();
+                        atomicAdd(done, 1);
+                        atomicAdd(rel + cs, 1);
+                        mbar_arrive(empty + cs);   // stage and input buffer are free
+                    }
+                    dot = q8_0_finish_x1(acc[0]);
+                } else {
+                    dot = q4k_row2(st + p.gu_tile[tl] + qr * (int)p.nb01_g, xa, p.alx, gp, p.H / 256, 1);
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence_block();
+                        atomicAdd(done, 1);
+                        atomicAdd(rel + cs, 1);
+                        mbar_arrive(empty + cs);   // stage and input buffer are free
+                    }
+                }
+                // gate row i = 4*tl + qr (tl < 2) pairs with up row i in tile tl + 2 (lane + 4)
+                const float up = __shfl_down_sync(0xffffffffu, dot, 4);
+                if (gp == 0 && tl < 2) {
+                    const float a = p.act == 1 ? act_swiglu_oai(dot, up, p.alpha, p.limit) : act_swiglu(dot, up);
+                    ly.act[(int64_t)J.pair * p.I + J.r0 + 4 * tl + qr] = a;
+                }
+            } else {
+                float gd[2], ud[2];
+                stack_gu_oct<TG>(p, st, xa, lane, gd, ud);
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence_block();
+                    atomicAdd(done, 1);
+                    atomicAdd(rel + cs, 1);
+                    mbar_arrive(empty + cs);   // stage and input buffer are free
+                }
+                if ((lane & 7) == 0) {
+#pragma unroll
+                    for (int ps = 0; ps < 2; ++ps) {
+                        const float a = p.act == 1 ? act_swiglu_oai(gd[ps], ud[ps], p.alpha, p.limit)
+                                                   : act_swiglu(gd[ps], ud[ps]);
+                        ly.act[(int64_t)J.pair * p.I + J.r0 + 4 * ps + (lane >> 3)] = a;
+                    }
+                }
             }
-            const float dot = q8_0_finish_x1(acc[0]);
-            // gate row i = 4*tl + qr (tl < 2) pairs with up row i in tile tl + 2 (lane + 4)
-            const float up = __shfl_down_sync(0xffffffffu, dot, 4);
             const int nblk = p.I / p.qblk, blk = J.r0 / p.qblk;
-            if (gp == 0 && tl < 2) {
-                const float a = p.act == 1 ? act_swiglu_oai(dot, up, p.alpha, p.limit) : act_swiglu(dot, up);
-                ly.act[(int64_t)J.pair * p.I + J.r0 + 4 * tl + qr] = a;
-            }
             __syncwarp();
             int last = 0;
             if (lane == 0) {
@@ -567,8 +798,8 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
             if (__shfl_sync(0xffffffffu, last, 0)) {
                 // this job finished the Q8 block last: quantize it
                 fence_acq_rel_gpu();
-                quant_block_split<GX_T_Q8_0, true>(ly.act + (int64_t)J.pair * p.I, ly.actq + (int64_t)J.pair * p.ald.pitch,
-                                                   p.ald, blk, lane);
+                quant_block_split<VD, true>(ly.act + (int64_t)J.pair * p.I, ly.actq + (int64_t)J.pair * p.ald.pitch,
+                                            p.ald, blk, lane);
                 fence_proxy_async_global();
                 __syncwarp();
             }
@@ -576,6 +807,24 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
                 fence_acq_rel_gpu();
                 atomicAdd(p.gu_done + J.L * p.T + J.t, 1);
             }
+        } else if constexpr (kMode == 1) {
+            float * dts = reinterpret_cast<float *>(smem + p.dots_off) + c * 32;
+            stack_d_oct<TD>(p, st, dbuf + bi * dbytes, lane, dts);
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();
+                atomicAdd(done, 1);
+                atomicAdd(rel + cs, 1);
+                mbar_arrive(empty + cs);
+            }
+            // output row rr = lane < Rd: sum over slots m of w[m] * dot(m*Rd + rr), in slot order
+            if (lane < p.Rd) {
+                const float * wr = ly.rw + (int64_t)J.t * p.k;
+                float accf = __fmul_rn(dts[lane], wr[0]);
+                for (int mm = 1; mm < p.k; ++mm) accf = __fadd_rn(accf, __fmul_rn(dts[mm * p.Rd + lane], wr[mm]));
+                ly.out[(int64_t)J.t * p.H + J.r0 + lane] = accf;
+            }
+            __syncwarp();
         } else {
             // lane = par*16 + q: weight rows q and q+16 of the job's k*Rd rows
             // (row R is row R % Rd of expert R / Rd); eight consecutive lanes
@@ -584,22 +833,35 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
             const int q = lane & 15;
             const int m0 = q / p.Rd, m1 = (q + 16) / p.Rd;
             const uint8_t * da = dbuf + bi * dbytes;
-            const uint8_t * rb[2] = {st + q * p.pitch_d + 32 * par, st + (q + 16) * p.pitch_d + 32 * par};
             const uint8_t * a0 = da + m0 * p.ald.pitch;
             const uint8_t * a1 = da + m1 * p.ald.pitch;
-            const uint8_t * ab[2] = {a0 + 32 * par, a1 + 32 * par};
-            const uint8_t * ad[2] = {a0 + p.ald.d_off, a1 + p.ald.d_off};
-            float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            q8_0_rows<2>(rb, ab, ad, par, p.I / 64, acc);
-            __syncwarp();
-            if (lane == 0) {
-                __threadfence_block();
-                atomicAdd(done, 1);
-                atomicAdd(rel + cs, 1);
-                mbar_arrive(empty + cs);
+            float d0, d1;
+            if constexpr (kMode == 0) {
+                const uint8_t * rb[2] = {st + q * p.pitch_d + 32 * par, st + (q + 16) * p.pitch_d + 32 * par};
+                const uint8_t * ab[2] = {a0 + 32 * par, a1 + 32 * par};
+                const uint8_t * ad[2] = {a0 + p.ald.d_off, a1 + p.ald.d_off};
+                float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                q8_0_rows<2>(rb, ab, ad, par, p.I / 64, acc);
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence_block();
+                    atomicAdd(done, 1);
+                    atomicAdd(rel + cs, 1);
+                    mbar_arrive(empty + cs);
+                }
+                d0 = q8_0_finish(acc[0]);
+                d1 = q8_0_finish(acc[1]);
+            } else {
+                d0 = q6k_row2(st + q * p.pitch_d, a0, p.ald, par, p.I / 256, 16);
+                d1 = q6k_row2(st + (q + 16) * p.pitch_d, a1, p.ald, par, p.I / 256, 16);
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence_block();
+                    atomicAdd(done, 1);
+                    atomicAdd(rel + cs, 1);
+                    mbar_arrive(empty + cs);
+                }
             }
-            const float d0 = q8_0_finish(acc[0]);
-            const float d1 = q8_0_finish(acc[1]);
             // output row rr = lane < Rd: weight row R = m*Rd + rr of expert m
             // is d0 of lane R (R < 16) or d1 of lane R - 16
             const float * wr = ly.rw + (int64_t)J.t * p.k;

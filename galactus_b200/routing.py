@@ -32,6 +32,22 @@ def zipf_bias(rng: np.random.Generator, experts: int, s: float = 1.1) -> np.ndar
     return np.log(w)[rng.permutation(experts)]
 
 
+def logits(model, tokens: int, layers: int, seed: int, rho: float = 0.0, s: float = 1.1) -> np.ndarray:
+    """Router logits float32 [tokens, layers, E]: z + b with the Zipf rank bias
+    and the AR(1) noise described above (the same stream as routes())."""
+    rng = np.random.default_rng(seed)
+    E = model.experts
+    bias = np.stack([zipf_bias(rng, E, s) for _ in range(layers)])          # [layers, E]
+    z = rng.standard_normal((layers, E))
+    out = np.zeros((tokens, layers, E), np.float32)
+    c = np.sqrt(1.0 - rho * rho)
+    for t in range(tokens):
+        if t > 0:
+            z = rho * z + c * rng.standard_normal((layers, E))
+        out[t] = z + bias
+    return out
+
+
 def routes(model, tokens: int, layers: int, seed: int, rho: float = 0.0, s: float = 1.1,
            scheme: str | None = None) -> tuple[np.ndarray, np.ndarray]:
     """ids int32 [tokens, layers, k], weights float32 [tokens, layers, k]."""

@@ -344,7 +344,8 @@ def test_remap_serve_strided_and_slot_bytes(gxlib, orc, dev):
 @pytest.mark.parametrize("name,T,layers,layerwise", [
     ("qwen3-30b", 1, 3, False), ("olmoe", 1, 3, False), ("gpt-oss-120b", 1, 3, False),
     ("qwen3-235b", 1, 3, False), ("deepseek-v3", 1, 2, False), ("qwen3-30b", 1, 10, False),
-    ("qwen3-30b", 3, 3, False), ("gpt-oss-120b", 5, 3, False),
+    ("qwen3-30b", 3, 3, False), ("gpt-oss-120b", 5, 3, False), ("olmoe", 4, 3, False), ("olmoe", 1, 10, False),
+    ("qwen3-235b", 3, 2, False), ("deepseek-v3", 2, 2, False),
     ("qwen3-30b", 1, 3, True), ("olmoe", 2, 3, True),
 ])
 def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name, T, layers, layerwise):
@@ -368,7 +369,8 @@ def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name, T, layers, layer
     ptr = lambda t: [t[L].data_ptr() for L in range(m.layers)]
     plan = StackPlan(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, T, layerwise=layerwise)
     info = plan.info()
-    stack_types = {(gxlib.TYPE_Q8_0, gxlib.TYPE_Q8_0)}
+    stack_types = {(gxlib.TYPE_Q8_0, gxlib.TYPE_Q8_0), (gxlib.TYPE_Q4_K, gxlib.TYPE_Q6_K),
+                   (gxlib.TYPE_MXFP4, gxlib.TYPE_MXFP4), (gxlib.TYPE_IQ1_S, gxlib.TYPE_IQ1_S)}
     expect = not layerwise and (m.type_gate, m.type_down) in stack_types
     assert info["stack_kernel"] == (1 if expect else 0), info
     call = StackCall(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, T)
