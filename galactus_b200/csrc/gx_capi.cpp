@@ -1045,21 +1045,28 @@ namespace {
 bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
     if (sp.k <= 0 || 32 % sp.k != 0) return false;
     sp.Rg = 8;
-    sp.Rd = 32 / sp.k;
     int cap = gx::kStackMaxConsumers;
     if (const char * env = std::getenv("GX_STACK_STAGES")) {
         const int v = std::atoi(env);
         if (v >= 1 && v <= gx::kStackMaxConsumers) cap = v;
     }
-    sp.W = 8;
+    int wenv = 0;
     if (const char * env = std::getenv("GX_STACK_WARPS")) {
         const int v = std::atoi(env);
-        if (v >= 1 && v <= gx::kStackMaxWarps) sp.W = v;
+        if (v >= 1 && v <= gx::kStackMaxWarps) wenv = v;
     }
-    for (int C = cap; C >= 2; --C) {
-        sp.C = C;
-        smem = gx::stack_layout(sp, threads);
-        if (smem != 0) return true;
+    // the two-lane K-quant rows prefer 16-row down jobs (smaller stages, more
+    // of them in flight) where 2 rows of an expert make whole 16-byte chunks
+    for (int drows : {16, 32}) {
+        if (drows == 16 && (sp.row_mode != 2 || 16 % sp.k != 0)) continue;
+        sp.Rd = drows / sp.k;
+        for (int C = cap; C >= 2; --C) {
+            sp.C = C;
+            // one consumer warp per stage, at least 8
+            sp.W = wenv ? wenv : std::min(std::max(8, C), gx::kStackMaxWarps);
+            smem = gx::stack_layout(sp, threads);
+            if (smem != 0) return true;
+        }
     }
     return false;
 }

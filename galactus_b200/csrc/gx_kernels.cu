@@ -749,14 +749,14 @@ static bool stack_copy_mode(int64_t nb01, int R, int32_t & row_copy, int32_t & p
 // gate/up tiles and rows of K % 256 == 0), 1 octet rows (any whole number
 // of their type's 64- or 256-element units, checked per layer; 2 gate/up copies).
 uint32_t stack_layout(StackParams & p, int & threads) {
-    if (p.Rg != 8 || p.Rd < 1 || p.k * p.Rd != 32) return 0;
+    if (p.Rg != 8 || p.Rd < 1 || (p.k * p.Rd != 32 && !(p.row_mode == 2 && p.k * p.Rd == 16))) return 0;
     if (p.row_mode < 0 || p.row_mode > 2 || p.gu_copies != (p.row_mode == 1 ? 2 : 4)) return 0;
     const int ra = p.row_mode == 1 ? 64 : 256;
     if (p.H % ra || p.I % ra || p.I % p.Rg || p.qblk % p.Rg || p.H % p.Rd) return 0;
     if (p.C < 1 || p.C > kStackMaxConsumers || p.NL < 1 || p.NL > kStackMaxLayers) return 0;
     if (p.W < 1 || p.W > kStackMaxWarps) return 0;
     if (p.row_mode == 1 && (p.Rd & 1)) return 0;   // octet row pairs stay inside one expert
-    threads = 96 + 32 * p.W;
+    threads = 32 * (kStackProducers + 2) + 32 * p.W;
     if (!stack_copy_mode(p.nb01_d, p.Rd, p.row_copy_d, p.pitch_d)) return 0;
     uint64_t gw;
     if (p.gu_copies == 4) {
@@ -789,8 +789,9 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     const uint64_t dw = (uint64_t)p.k * p.Rd * (uint64_t)p.pitch_d + (p.row_mode != 0 ? 16 : 0);
     p.stage_bytes = (int32_t)align_up(gw > dw ? gw : dw, 128);
     p.bar_off = 0;      // 3*C + 2*kStackBufs mbarriers
-    p.meta_off = 256;   // metadata word and release counter per stage, buffer counters
-    p.stage_off = 384;
+    p.meta_off = (uint32_t)align_up(8ull * (3 * kStackMaxConsumers + 2 * kStackBufs), 128);
+    // metadata word and release counter per stage, buffer counters, next job
+    p.stage_off = p.meta_off + (uint32_t)align_up(4ull * (2 * kStackMaxConsumers + 2 * kStackBufs + 1), 128);
     p.xbuf_off = p.stage_off + (uint32_t)p.C * (uint32_t)p.stage_bytes;
     p.dbuf_off = p.xbuf_off + align_up((uint64_t)kStackBufs * p.alx.pitch, 128);
     p.wt_off = p.dbuf_off + align_up((uint64_t)kStackBufs * p.k * p.ald.pitch, 128);

@@ -115,18 +115,19 @@ struct StackLayer {
     int32_t pad;
 };
 
-constexpr int kStackMaxConsumers = 8;   // ring stages
-constexpr int kStackMaxWarps = 13;      // consumer warps
+constexpr int kStackMaxConsumers = 16;  // ring stages
+constexpr int kStackMaxWarps = 12;      // consumer warps
+constexpr int kStackProducers = 2;      // weight producer warps (even and odd jobs)
 constexpr int kStackMaxLayers = 128;   // the layer table travels in the kernel parameters
 constexpr int kStackBufs = 2;          // activation buffers per kind (gate/up inputs, down inputs)
 
 struct StackParams {
     int32_t * q_done;          // [NL]   1 once x_L is quantized
-    int32_t * gu_done;         // [NL*T] gate/up jobs finished per token
+    int32_t * gu_done;         // [NL*T] quantized down-input blocks per token (k*I/qblk when complete)
     int32_t NL, k, T, H, I;
     int64_t nb01_g, nb01_d;    // gate/up and down row bytes
     int32_t Rg;                // gate (and up) rows per gate/up job
-    int32_t Rd;                // output rows per down job (k*Rd weight rows)
+    int32_t Rd;                // output rows per down job (k*Rd = 32 weight rows, or 16 in row mode 2)
     int32_t C;                 // ring stages
     int32_t W;                 // consumer warps (may exceed C)
     int32_t skew;              // down jobs of layer L follow the gate/up jobs of layer L+skew

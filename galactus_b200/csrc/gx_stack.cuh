@@ -8,16 +8,19 @@
 //   [GU(0)] .. [GU(skew-1)] [GU(skew)] [D(0)] [GU(skew+1)] [D(1)] ... [D(NL-1)]
 // and CTA b takes jobs b, b+G, b+2G, ... ; its j-th job uses ring stage j % C.
 // Inside a CTA:
-//   warp 0        weight producer: as soon as a stage is released, bulk-TMA
-//                 copies the expert rows of the CTA's next job into it. Weights
+//   warps 0, 1    weight producers (even and odd jobs of the CTA, so that the
+//                 per-job issue work of one thread is not the limit): as soon
+//                 as a stage is released, bulk-TMA
+//                 copies the expert rows of the CTA's next job into it (one
+//                 lane per copy). Weights
 //                 never depend on earlier jobs, so the HBM stream runs ahead
 //                 across job, half-layer and layer boundaries;
-//   warp 1        gate/up input producer: once per (layer, token) that the
+//   warp 2        gate/up input producer: once per (layer, token) that the
 //                 CTA's jobs need, waits until x_L is quantized and copies the
-//                 row into one of two buffers; tells each job which buffer;
-//   warp 2        down input producer: the same for the k activation rows of
-//                 a token, after every gate/up job of that token finished;
-//   warps 3..C+2  consumers: warp c computes the jobs of stage c, releases the
+//                 row into buffer (L*T + t) % 2 (see stack_input_producer);
+//   warp 3        down input producer: the same for the k activation rows of
+//                 a token, once every Q8 block of them has been quantized;
+//   warps 4..     consumers: warp c computes the jobs of stage c, releases the
 //                 stage and the input buffer, then runs the job's epilogue
 //                 (activation and its Q8 quantization, or the combine).
 // The x_L quantization runs first, in the consumer warps of CTA L mod G. The
@@ -264,10 +267,12 @@ __device__ __forceinline__ float q8_0_finish_x1(const float (&a)[4]) {
     return __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
 }
 
-// Weight copies of job J into a stage, issued by one thread; slot ids and
+// Weight copies of job J into a stage, issued by the 32 lanes of the weight
+// producer warp: lane 0 arms the stage barrier with the job's bytes, then one
+// lane per copy issues it (the copies of a job go out together). Slot ids and
 // the layer's weight bases come from shared memory.
 __device__ __forceinline__ void stack_issue_weights(const StackCopy & q, const StackJob & J, const int32_t * slots,
-                                                    const StackWeights * wt, uint8_t * stage, uint64_t * bar) {
+                                                    const StackWeights * wt, uint8_t * stage, uint64_t * bar, int lane) {
     const StackWeights ly = wt[J.L];
     const int32_t * sl = slots + J.L * q.T * q.k;
     if (J.gu) {
@@ -275,155 +280,286 @@ __device__ __forceinline__ void stack_issue_weights(const StackCopy & q, const S
         if (q.gu_copies == 4) {
             // 4 tiles of 4 rows: gate rows r0..r0+3, r0+4..r0+7, then up rows
             const uint32_t tile = (uint32_t)(4 * q.nb01_g);
-            tma_expect(bar, 4u * tile);
-            for (int t = 0; t < 4; ++t)
-                tma_load(stage + q.tile[t], (t < 2 ? ly.wg : ly.wu) + off + (int64_t)(t & 1) * tile, tile, bar);
+            if (lane == 0) tma_expect(bar, 4u * tile);
+            __syncwarp();
+            if (lane < 4)
+                tma_load(stage + q.tile[lane], (lane < 2 ? ly.wg : ly.wu) + off + (int64_t)(lane & 1) * tile, tile, bar);
         } else {
             // gate rows r0..r0+7, then up rows r0..r0+7
             const uint32_t tile = (uint32_t)(8 * q.nb01_g);
-            tma_expect(bar, 2u * tile);
-            tma_load(stage + q.tile[0], ly.wg + off, tile, bar);
-            tma_load(stage + q.tile[1], ly.wu + off, tile, bar);
+            if (lane == 0) tma_expect(bar, 2u * tile);
+            __syncwarp();
+            if (lane < 2) tma_load(stage + q.tile[lane], (lane == 0 ? ly.wg : ly.wu) + off, tile, bar);
         }
     } else {
         const uint32_t bytes = (uint32_t)(q.Rd * q.nb01_d);
-        tma_expect(bar, (uint32_t)q.k * bytes);
-        for (int m = 0; m < q.k; ++m) {
-            const uint8_t * src = ly.wd + (int64_t)sl[J.pair + m] * ly.nb02 + (int64_t)J.r0 * q.nb01_d;
-            uint8_t * dst = stage + m * q.Rd * q.pitch_d;
-            if (q.row_copy_d) {
-                for (int r = 0; r < q.Rd; ++r)
-                    tma_load(dst + r * q.pitch_d, src + (int64_t)r * q.nb01_d, (uint32_t)q.nb01_d, bar);
-            } else {
-                tma_load(dst, src, bytes, bar);
+        if (lane == 0) tma_expect(bar, (uint32_t)q.k * bytes);
+        __syncwarp();
+        if (q.row_copy_d) {
+            for (int i = lane; i < q.k * q.Rd; i += 32) {
+                const int m = i / q.Rd, r = i - m * q.Rd;
+                tma_load(stage + (m * q.Rd + r) * q.pitch_d,
+                         ly.wd + (int64_t)sl[J.pair + m] * ly.nb02 + (int64_t)(J.r0 + r) * q.nb01_d, (uint32_t)q.nb01_d, bar);
             }
+        } else if (lane < q.k) {
+            tma_load(stage + lane * q.Rd * q.pitch_d, ly.wd + (int64_t)sl[J.pair + lane] * ly.nb02 + (int64_t)J.r0 * q.nb01_d,
+                     bytes, bar);
         }
     }
+}
+
+// unsigned-by-signed byte dot: a holds four unsigned bytes, b four signed
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// two signed 16-bit halves of a times bytes 0,1 (LO) or 2,3 (HI) of b, plus c
+__device__ __forceinline__ int dp2a_lo(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Superblocks whose integer parts a lane computes before their exchanges and
+// float chain (Q4_K rows), and whether Q6_K rows go by superblock pairs.
+constexpr int kQ4kGroup = 1;
+constexpr bool kQ6kPairs = true;
+
+// the exact integer parts of one Q4_K superblock half (see q4k_row2)
+__device__ __forceinline__ void q4k_half(const uint8_t * xb, const uint8_t * aq, const uint8_t * bsp, uint32_t sel,
+                                         int p, int & sumi, int & prod, uint32_t & dm) {
+    const uint4 hdr = lds128(xb);   // d | dmin, scale bytes 0-3, 4-7, 8-11
+    dm = hdr.x;
+    const uint32_t sc_lo = hdr.y & 0x3f3f3f3fu;
+    const uint32_t sc_hi = (hdr.w & 0x0f0f0f0fu) | ((hdr.y >> 2) & 0x30303030u);
+    const uint32_t mn_lo = hdr.z & 0x3f3f3f3fu;
+    const uint32_t mn_hi = ((hdr.w >> 4) & 0x0f0f0f0fu) | ((hdr.z >> 2) & 0x30303030u);
+    int si = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint4 q = lds128(xb + 16 + 32 * j + 16 * p);
+        const uint4 lo = lds128(aq + 64 * j);
+        const uint4 hi = lds128(aq + 64 * j + 32);
+        int p1 = dp4a(q.x & 0x0f0f0f0fu, lo.x, 0);
+        p1 = dp4a(q.y & 0x0f0f0f0fu, lo.y, p1);
+        p1 = dp4a(q.z & 0x0f0f0f0fu, lo.z, p1);
+        p1 = dp4a(q.w & 0x0f0f0f0fu, lo.w, p1);
+        int p2 = dp4a_us(q.x & 0xf0f0f0f0u, hi.x, 0);
+        p2 = dp4a_us(q.y & 0xf0f0f0f0u, hi.y, p2);
+        p2 = dp4a_us(q.z & 0xf0f0f0f0u, hi.z, p2);
+        p2 = dp4a_us(q.w & 0xf0f0f0f0u, hi.w, p2);
+        p2 >>= 4;
+        const uint32_t sw = j < 2 ? sc_lo : sc_hi;
+        const int s0 = (int)((sw >> (16 * (j & 1))) & 0xffu), s1 = (int)((sw >> (16 * (j & 1) + 8)) & 0xffu);
+        si += p1 * s0 + p2 * s1;
+    }
+    uint32_t bw[8];
+#pragma unroll
+    for (int o = 0; o < 8; ++o) bw[o] = lds32(bsp + 4 * o);
+    int pr = dp2a_lo(__byte_perm(bw[0], bw[1], sel), mn_lo, 0);
+    pr = dp2a_hi(__byte_perm(bw[2], bw[3], sel), mn_lo, pr);
+    pr = dp2a_lo(__byte_perm(bw[4], bw[5], sel), mn_hi, pr);
+    pr = dp2a_hi(__byte_perm(bw[6], bw[7], sel), mn_hi, pr);
+    sumi = si;
+    prod = pr;
 }
 
 // Q4_K row x Q8_K activation row (split layout), two lanes per row
 // (ggml_vec_dot_q4_K_q8_K, diff:1254-1259, 1300-1357). Lane half p takes
 // bytes 16p..16p+15 of every 32-byte quant group j, i.e. the 16-element runs
 // 64j+16p.. (low nibbles, sub-block 2j) and 64j+32+16p.. (high nibbles,
-// sub-block 2j+1), and the block sums bs[2o+p] of the mins. The exact integer
-// parts of a superblock are summed with the partner lane (lane ^ xm), then
-// both lanes run the superblock chain in order:
+// sub-block 2j+1), and the block sums bs[2o+p] of the mins. The high nibbles
+// are dotted in place (byte & 0xf0, unsigned) and the sum shifted down by 4,
+// exact since every term is a multiple of 16. The six-bit scales and mins of
+// the 12-byte packing are unpacked four at a time; the mins meet the 16-bit
+// block sums in dp2a. The exact integer parts of a superblock are summed with
+// the partner lane (lane ^ xm), then both lanes run the superblock chain:
 //   sumf = fma(-(yd*fp16(dmin)), prod, sumf); sumf = fma(yd*fp16(d), sumi, sumf).
 __device__ __forceinline__ float q4k_row2(const uint8_t * row, const uint8_t * act, const ActLayout & al, int p, int nsb,
                                           int xm) {
     float sumf = 0.0f;
     const uint8_t * aq = act + 16 * p;
-    for (int i = 0; i < nsb; ++i) {
-        const uint8_t * xb = row + 144 * i;
-        const uint4 hdr = lds128(xb);   // d | dmin, scale bytes 0-3, 4-7, 8-11
-        int sumi = 0;
+    const uint32_t sel = p ? 0x7632u : 0x5410u;   // half p of two block-sum words
+    int i = 0;
+    // kQ4kGroup superblocks' integer parts first (independent), then their
+    // exchanges, then the chain in superblock order
+    constexpr int NG = kQ4kGroup;
+    for (; NG > 1 && i + NG <= nsb; i += NG) {
+        int si[NG], pr[NG];
+        uint32_t dm[NG];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint4 q = lds128(xb + 16 + 32 * j + 16 * p);
-            const uint4 lo = lds128(aq + 256 * i + 64 * j);
-            const uint4 hi = lds128(aq + 256 * i + 64 * j + 32);
-            int p1 = dp4a(q.x & 0x0f0f0f0fu, lo.x, 0);
-            p1 = dp4a(q.y & 0x0f0f0f0fu, lo.y, p1);
-            p1 = dp4a(q.z & 0x0f0f0f0fu, lo.z, p1);
-            p1 = dp4a(q.w & 0x0f0f0f0fu, lo.w, p1);
-            int p2 = dp4a((q.x >> 4) & 0x0f0f0f0fu, hi.x, 0);
-            p2 = dp4a((q.y >> 4) & 0x0f0f0f0fu, hi.y, p2);
-            p2 = dp4a((q.z >> 4) & 0x0f0f0f0fu, hi.z, p2);
-            p2 = dp4a((q.w >> 4) & 0x0f0f0f0fu, hi.w, p2);
-            const int a0 = 2 * j, a1 = 2 * j + 1;
-            const int sc0 = a0 < 4 ? (int)((hdr.y >> (8 * a0)) & 63u)
-                                   : (int)(((hdr.w >> (8 * (a0 - 4))) & 0x0fu) | (((hdr.y >> (8 * (a0 - 4) + 6)) & 3u) << 4));
-            const int sc1 = a1 < 4 ? (int)((hdr.y >> (8 * a1)) & 63u)
-                                   : (int)(((hdr.w >> (8 * (a1 - 4))) & 0x0fu) | (((hdr.y >> (8 * (a1 - 4) + 6)) & 3u) << 4));
-            sumi += p1 * sc0 + p2 * sc1;
-        }
-        int prod = 0;
-        const uint8_t * bsp = act + al.bs_off + 32 * i;
+        for (int k = 0; k < NG; ++k)
+            q4k_half(row + 144 * (i + k), aq + 256 * (i + k), act + al.bs_off + 32 * (i + k), sel, p, si[k], pr[k], dm[k]);
 #pragma unroll
-        for (int o = 0; o < 8; ++o) {
-            const int mn = o < 4 ? (int)((hdr.z >> (8 * o)) & 63u)
-                                 : (int)(((hdr.w >> (8 * (o - 4) + 4)) & 0x0fu) | (((hdr.z >> (8 * (o - 4) + 6)) & 3u) << 4));
-            const int bs = (int)(int16_t)((lds32(bsp + 4 * o) >> (16 * p)) & 0xffffu);
-            prod += bs * mn;
+        for (int k = 0; k < NG; ++k) {
+            si[k] += __shfl_xor_sync(0xffffffffu, si[k], xm);
+            pr[k] += __shfl_xor_sync(0xffffffffu, pr[k], xm);
         }
-        sumi += __shfl_xor_sync(0xffffffffu, sumi, xm);
-        prod += __shfl_xor_sync(0xffffffffu, prod, xm);
+#pragma unroll
+        for (int k = 0; k < NG; ++k) {
+            const float yd = __uint_as_float(lds32(act + al.d_off + 4 * (i + k)));
+            sumf = __fmaf_rn(-__fmul_rn(yd, h2f((uint16_t)(dm[k] >> 16))), (float)pr[k], sumf);
+            sumf = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dm[k] & 0xffffu))), (float)si[k], sumf);
+        }
+    }
+    for (; i < nsb; ++i) {
+        int si, pr;
+        uint32_t dm;
+        q4k_half(row + 144 * i, aq + 256 * i, act + al.bs_off + 32 * i, sel, p, si, pr, dm);
+        si += __shfl_xor_sync(0xffffffffu, si, xm);
+        pr += __shfl_xor_sync(0xffffffffu, pr, xm);
         const float yd = __uint_as_float(lds32(act + al.d_off + 4 * i));
-        sumf = __fmaf_rn(-__fmul_rn(yd, h2f((uint16_t)(hdr.x >> 16))), (float)prod, sumf);
-        sumf = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(hdr.x & 0xffffu))), (float)sumi, sumf);
+        sumf = __fmaf_rn(-__fmul_rn(yd, h2f((uint16_t)(dm >> 16))), (float)pr, sumf);
+        sumf = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dm & 0xffffu))), (float)si, sumf);
     }
     return sumf;
 }
 
-// Q6_K row x Q8_K activation row (split layout), two lanes per row
-// (ggml_vec_dot_q6_K_q8_K, diff:1366-1370, 1393-1446). Lane half p takes the
-// 32-element half p of every 64-element quarter j: groups 4j+2p and 4j+2p+1,
-// quants ql bytes 64(j/2)+32p.. (nibble 4*(j&1)) with qh bytes 128+32(j/2)..
-// (bits 4*(j&1)+2p). Superblocks are 210 bytes, so odd ones sit two bytes off
-// a word and are realigned with funnel shifts. isum and mins are summed with
-// the partner lane (lane ^ xm), then sumf = fma(yd*fp16(d), isum - 32*mins, sumf).
-__device__ __forceinline__ float q6k_row2(const uint8_t * row, const uint8_t * act, const ActLayout & al, int p, int nsb,
-                                          int xm) {
-    float sumf = 0.0f;
-    for (int i = 0; i < nsb; ++i) {
-        const int xo = 210 * i;
-        const uint8_t * wb = row + (xo & ~3);
-        const uint32_t sh = (uint32_t)(xo & 3) * 8u;   // 0 or 16
-        const int base = xo & 3;                       // bytes of the block start inside the first word
-        (void)base;
-        uint32_t sc4[4];
-        {
-            uint32_t w[5];
+// N consecutive words at wb + off (wb 4-byte aligned) shifted right by SH bits
+template <int N, int SH>
+__device__ __forceinline__ void lds_words(const uint8_t * wb, int off, uint32_t (&out)[N]) {
+    if constexpr (SH == 0) {
 #pragma unroll
-            for (int k = 0; k < 5; ++k) w[k] = lds32(wb + 192 + 4 * k);
+        for (int k = 0; k < N; ++k) out[k] = lds32(wb + off + 4 * k);
+    } else {
+        uint32_t w0 = lds32(wb + off);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) sc4[k] = __funnelshift_r(w[k], w[k + 1], sh);
+        for (int k = 0; k < N; ++k) {
+            const uint32_t w1 = lds32(wb + off + 4 * (k + 1));
+            out[k] = __funnelshift_r(w0, w1, SH);
+            w0 = w1;
         }
-        const uint32_t dw = __funnelshift_r(lds32(wb + 208), lds32(wb + 212), sh);
-        int isum = 0, mins = 0;
-        const uint8_t * bsp = act + al.bs_off + 32 * i;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            uint32_t ql[8], qh[8];
-            {
-                uint32_t w[9];
-#pragma unroll
-                for (int k = 0; k < 9; ++k) w[k] = lds32(wb + 64 * h + 32 * p + 4 * k);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) ql[k] = __funnelshift_r(w[k], w[k + 1], sh);
-#pragma unroll
-                for (int k = 0; k < 9; ++k) w[k] = lds32(wb + 128 + 32 * h + 4 * k);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) qh[k] = __funnelshift_r(w[k], w[k + 1], sh);
-            }
-#pragma unroll
-            for (int odd = 0; odd < 2; ++odd) {
-                const int j = 2 * h + odd;
-                const uint8_t * ap = act + 256 * i + 64 * j + 32 * p;
-                const uint4 a0 = lds128(ap), a1 = lds128(ap + 16);
-                const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const uint32_t qsh = 4u * (uint32_t)odd + 2u * (uint32_t)p;
-                int pg[2] = {0, 0};
-#pragma unroll
-                for (int ww = 0; ww < 8; ++ww) {
-                    const uint32_t nib = (ql[ww] >> (4 * odd)) & 0x0f0f0f0fu;
-                    const uint32_t hb = (qh[ww] >> qsh) & 0x03030303u;
-                    pg[ww >> 2] = dp4a(nib | (hb << 4), aw[ww], pg[ww >> 2]);
-                }
-                // groups 4j+2p and 4j+2p+1: scale bytes 4j+2p, 4j+2p+1
-                const uint32_t sw = sc4[j] >> (16 * p);
-                const int s0 = (int)(int8_t)(sw & 0xffu), s1 = (int)(int8_t)((sw >> 8) & 0xffu);
-                const uint32_t bw = lds32(bsp + 8 * j + 4 * p);
-                isum += pg[0] * s0 + pg[1] * s1;
-                mins += (int)(int16_t)(bw & 0xffffu) * s0 + (int)(int16_t)(bw >> 16) * s1;
-            }
-        }
-        isum += __shfl_xor_sync(0xffffffffu, isum, xm);
-        mins += __shfl_xor_sync(0xffffffffu, mins, xm);
-        const float yd = __uint_as_float(lds32(act + al.d_off + 4 * i));
-        sumf = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dw & 0xffffu))), (float)(isum - 32 * mins), sumf);
     }
-    return sumf;
+}
+
+// One Q6_K superblock half of one row (see q6k_rows2); SH = 0 for a
+// word-aligned superblock, 16 for one two bytes off.
+template <int SH>
+__device__ __forceinline__ void q6k_half(const uint8_t * wb, const uint8_t * aq, const uint8_t * bsp, int p,
+                                         int & isum, int & mins, uint32_t & dw) {
+    uint32_t sc4[4], dd[1];
+    lds_words<4, SH>(wb, 192, sc4);
+    lds_words<1, SH>(wb, 208, dd);
+    dw = dd[0];
+    isum = 0;
+    mins = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        uint32_t ql[8], qh[8];
+        lds_words<8, SH>(wb, 64 * h + 32 * p, ql);
+        lds_words<8, SH>(wb, 128 + 32 * h, qh);
+        uint32_t aw[2][8];
+#pragma unroll
+        for (int odd = 0; odd < 2; ++odd) {
+            const uint8_t * ap = aq + 64 * (2 * h + odd);
+            const uint4 a0 = lds128(ap), a1 = lds128(ap + 16);
+            aw[odd][0] = a0.x; aw[odd][1] = a0.y; aw[odd][2] = a0.z; aw[odd][3] = a0.w;
+            aw[odd][4] = a1.x; aw[odd][5] = a1.y; aw[odd][6] = a1.z; aw[odd][7] = a1.w;
+        }
+        int pg[2][2] = {{0, 0}, {0, 0}};
+#pragma unroll
+        for (int ww = 0; ww < 8; ++ww) {
+            const uint32_t hp = qh[ww] >> (2 * p);   // the two bits of half p at 0-1 (odd 0) and 4-5 (odd 1)
+            const uint32_t q0 = (ql[ww] & 0x0f0f0f0fu) | ((hp << 4) & 0x30303030u);
+            const uint32_t q1 = ((ql[ww] >> 4) & 0x0f0f0f0fu) | (hp & 0x30303030u);
+            pg[0][ww >> 2] = dp4a(q0, aw[0][ww], pg[0][ww >> 2]);
+            pg[1][ww >> 2] = dp4a(q1, aw[1][ww], pg[1][ww >> 2]);
+        }
+#pragma unroll
+        for (int odd = 0; odd < 2; ++odd) {
+            const int j = 2 * h + odd;
+            // groups 4j+2p and 4j+2p+1: scale bytes 4j+2p, 4j+2p+1
+            const uint32_t sw = sc4[j] >> (16 * p);
+            const int s0 = (int)(int8_t)(sw & 0xffu), s1 = (int)(int8_t)((sw >> 8) & 0xffu);
+            const uint32_t bw = lds32(bsp + 8 * j + 4 * p);
+            isum += pg[odd][0] * s0 + pg[odd][1] * s1;
+            mins += (int)(int16_t)(bw & 0xffffu) * s0 + (int)(int16_t)(bw >> 16) * s1;
+        }
+    }
+}
+
+// Two Q6_K rows x their Q8_K activation rows (split layout), two lanes per
+// row (ggml_vec_dot_q6_K_q8_K, diff:1366-1370, 1393-1446). Lane half p takes
+// the 32-element half p of every 64-element quarter j: groups 4j+2p and
+// 4j+2p+1, quants ql bytes 64(j/2)+32p.. (nibble 4*(j&1)) with qh bytes
+// 128+32(j/2).. (bits 4*(j&1)+2p). Superblocks are 210 bytes, so the odd ones
+// sit two bytes off a word and are realigned with funnel shifts. isum and mins
+// are summed with the partner lane (lane ^ xm), then per superblock
+// sumf = fma(yd*fp16(d), isum - 32*mins, sumf). The two rows run in one loop.
+template <int NR>
+__device__ __forceinline__ void q6k_rows2(const uint8_t * row0, const uint8_t * row1, const uint8_t * act0,
+                                          const uint8_t * act1, const ActLayout & al, int p, int nsb, int xm,
+                                          float & d0, float & d1) {
+    const uint8_t * rows[2] = {row0, row1};
+    const uint8_t * acts[2] = {act0, act1};
+    float sums[2] = {0.0f, 0.0f};
+    int i = 0;
+    if constexpr (!kQ6kPairs) {
+        for (; i < nsb; ++i) {
+            const int off = (210 * i) & ~3;
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                int is, mn;
+                uint32_t dw;
+                if (i & 1)
+                    q6k_half<16>(rows[r] + off, acts[r] + 256 * i + 32 * p, acts[r] + al.bs_off + 32 * i, p, is, mn, dw);
+                else
+                    q6k_half<0>(rows[r] + off, acts[r] + 256 * i + 32 * p, acts[r] + al.bs_off + 32 * i, p, is, mn, dw);
+                is += __shfl_xor_sync(0xffffffffu, is, xm);
+                mn += __shfl_xor_sync(0xffffffffu, mn, xm);
+                const float yd = __uint_as_float(lds32(acts[r] + al.d_off + 4 * i));
+                sums[r] = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dw & 0xffffu))), (float)(is - 32 * mn), sums[r]);
+            }
+        }
+    }
+    // superblock pairs: the even one is word-aligned, the odd one two bytes off
+    for (; i + 2 <= nsb; i += 2) {
+        int is[2][2], mn[2][2];
+        uint32_t dw[2][2];
+        const int off0 = 210 * i, off1 = (210 * (i + 1)) & ~3;
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            q6k_half<0>(rows[r] + off0, acts[r] + 256 * i + 32 * p, acts[r] + al.bs_off + 32 * i, p, is[r][0], mn[r][0],
+                        dw[r][0]);
+            q6k_half<16>(rows[r] + off1, acts[r] + 256 * (i + 1) + 32 * p, acts[r] + al.bs_off + 32 * (i + 1), p,
+                         is[r][1], mn[r][1], dw[r][1]);
+        }
+#pragma unroll
+        for (int r = 0; r < NR; ++r)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                is[r][k] += __shfl_xor_sync(0xffffffffu, is[r][k], xm);
+                mn[r][k] += __shfl_xor_sync(0xffffffffu, mn[r][k], xm);
+            }
+#pragma unroll
+        for (int r = 0; r < NR; ++r)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const float yd = __uint_as_float(lds32(acts[r] + al.d_off + 4 * (i + k)));
+                sums[r] = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dw[r][k] & 0xffffu))), (float)(is[r][k] - 32 * mn[r][k]),
+                                    sums[r]);
+            }
+    }
+    if (i < nsb) {   // a last even superblock
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            int is, mn;
+            uint32_t dw;
+            q6k_half<0>(rows[r] + 210 * i, acts[r] + 256 * i + 32 * p, acts[r] + al.bs_off + 32 * i, p, is, mn, dw);
+            is += __shfl_xor_sync(0xffffffffu, is, xm);
+            mn += __shfl_xor_sync(0xffffffffu, mn, xm);
+            const float yd = __uint_as_float(lds32(acts[r] + al.d_off + 4 * i));
+            sums[r] = __fmaf_rn(__fmul_rn(yd, h2f((uint16_t)(dw & 0xffffu))), (float)(is - 32 * mn), sums[r]);
+        }
+    }
+    d0 = sums[0];
+    d1 = sums[1];
 }
 
 // Octet gate/up job: gate row i and up row i (octet g, i = 4*pass + g)
@@ -484,29 +620,28 @@ __device__ __forceinline__ void stack_d_oct(const StackParams & p, const uint8_t
 }
 
 // Input producer of one kind (0: gate/up inputs x_L, 1: down inputs).
-// Walks the CTA's jobs in order; for each job of its kind it makes sure the
-// job's input rows are in one of kStackBufs buffers (one bulk copy per new
-// (layer, token)), writes the buffer index and fill parity into the stage's
-// metadata word and arrives on the stage's input barrier.
-//
-// A producer skips the jobs of the other kind, so it can be two or more
-// phases ahead of a stage's "empty" mbarrier, where a parity wait would be
-// ambiguous; it waits instead on the stage's release counter rel[s] (jobs of
-// stage s whose consumer released it), which only grows.
+// The input rows of key K = L*T + t (a layer's token) go to buffer
+// K % kStackBufs. Walking the CTA's jobs of its kind in order (their keys
+// never decrease), the producer counts the jobs of each buffer; at each new
+// key it waits until every job of the buffer's previous key is done, waits
+// for the rows to exist (x_L quantized, or every Q8 block of the token's
+// activations), copies them in and publishes the fill word (K << 1 | phase
+// parity). A consumer spins until its buffer's fill word names its key, then
+// waits on the buffer barrier with that parity: the fill of K is issued only
+// after every job of the buffer's previous key has finished, so the barrier
+// is never two phases behind a waiting consumer and its parity is unambiguous.
 __device__ __forceinline__ void stack_input_producer(const StackParams & p, int kind, int mine, int b, int G,
-                                                     volatile int * rel, uint64_t * afull, uint64_t * bbar,
-                                                     int * meta, volatile int * bufdone, uint8_t * buf, int buf_bytes) {
-    const int C = p.C;
+                                                     uint64_t * bbar, volatile int * fillw, volatile int * bufdone,
+                                                     uint8_t * buf, int buf_bytes) {
     const StackGeom g = stack_geom(p);
-    const int gu_per_token = p.k * (p.I / p.Rg);
-    int key[kStackBufs], iss[kStackBufs], fills[kStackBufs];
+    const int blocks_per_token = p.k * (p.I / p.qblk);   // quantized down-input blocks of a token
+    int iss[kStackBufs], fills[kStackBufs];
 #pragma unroll
     for (int i = 0; i < kStackBufs; ++i) {
-        key[i] = -1;
         iss[i] = 0;
         fills[i] = 0;
     }
-    int cur = -1, next = 0;
+    int cur = -1;
     StackWalk walk{0, 0};
     walk.advance(g, b);
     for (int jl = 0; jl < mine; ++jl, walk.advance(g, G)) {
@@ -514,29 +649,15 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
         walk.kind(g, jL, jgu);
         if (jgu != (kind == 0 ? 1 : 0)) continue;
         const StackJob J = walk.job(g);
-        const int s = jl % C, n = jl / C;
-        // job jl - C (the previous job of stage s) has been released
-        bool freed = n == 0;
-        for (uint32_t i = 0; i < (1u << 23) && !freed; ++i) {
-            freed = rel[s] >= n;
-            if (!freed && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
-        }
-        if (!freed) {
-            record_error(GX_DEVERR_TIMEOUT);
-            break;
-        }
-        __threadfence_block();
-        const int k2 = J.L * p.T + J.t;
-        if (cur < 0 || key[cur] != k2) {
-            const int bi = next;
-            next = (next + 1) % kStackBufs;
+        const int K = J.L * p.T + J.t, bi = K % kStackBufs;
+        if (K != cur) {
             // every job that used the buffer before is done with it
             bool ok = false;
             for (uint32_t i = 0; i < (1u << 23) && !ok; ++i) {
                 ok = bufdone[bi] >= iss[bi];
                 if (!ok && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
             }
-            if (ok) ok = kind == 0 ? stack_wait(p.q_done + J.L, 1) : stack_wait(p.gu_done + k2, gu_per_token);
+            if (ok) ok = kind == 0 ? stack_wait(p.q_done + J.L, 1) : stack_wait(p.gu_done + K, blocks_per_token);
             if (!ok) {
                 record_error(GX_DEVERR_TIMEOUT);
                 break;
@@ -553,13 +674,11 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
                 tma_expect(bbar + bi, bytes);
                 tma_load(dst, ly.actq + (int64_t)J.t * p.k * p.ald.pitch, bytes, bbar + bi);
             }
-            key[bi] = k2;
             ++fills[bi];
-            cur = bi;
+            fillw[bi] = (K << 1) | ((fills[bi] - 1) & 1);
+            cur = K;
         }
-        ++iss[cur];
-        meta[s] = cur | (((fills[cur] - 1) & 1) << 8);
-        mbar_arrive(afull + s);
+        ++iss[bi];
     }
     // copies in flight land before the CTA can exit
 #pragma unroll
@@ -568,19 +687,18 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
 }
 
 template <int TG, int TD>
-__global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __grid_constant__ StackParams p) {
+__global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWarps, 1) k_stack(const __grid_constant__ StackParams p) {
     // row mode: 0 two-lane Q8_0 rows, 2 two-lane Q4_K gate/up + Q6_K down rows, 1 octet rows
     constexpr int kMode = (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0 : (TG == GX_T_Q4_K && TD == GX_T_Q6_K) ? 2 : 1;
     constexpr int VG = Oct<TG>::VDT, VD = Oct<TD>::VDT;       // activation types of gate/up and down
     extern __shared__ __align__(128) uint8_t smem[];
     const int C = p.C;
     uint64_t * wfull = reinterpret_cast<uint64_t *>(smem + p.bar_off);
-    uint64_t * afull = wfull + C;
-    uint64_t * empty = afull + C;
+    uint64_t * empty = wfull + C;
     uint64_t * xbar = empty + C;            // kStackBufs input-buffer barriers per kind
     uint64_t * dbar = xbar + kStackBufs;
-    int * meta = reinterpret_cast<int *>(smem + p.meta_off);
-    int * bufdone = meta + kStackMaxConsumers;       // [2][kStackBufs]
+    int * fillw = reinterpret_cast<int *>(smem + p.meta_off);   // [2][kStackBufs] fill words
+    int * bufdone = fillw + kStackMaxConsumers;      // [2][kStackBufs]
     int * rel = bufdone + 2 * kStackBufs;             // [C] releases per stage
     uint8_t * stages = smem + p.stage_off;
     uint8_t * xbuf = smem + p.xbuf_off;
@@ -613,20 +731,21 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
             wt[L] = w;
         }
         if (tid < 2 * kStackBufs + kStackMaxConsumers + 1) bufdone[tid] = 0;   // bufdone, rel, next job
+        if (tid < 2 * kStackBufs) fillw[tid] = -1;                                // no key filled yet
         if (__syncthreads_or(bad)) {
             if (tid == 0) record_error(GX_DEVERR_DOMAIN);
             return;
         }
     }
     if (tid == 0) {
-        for (int s = 0; s < 3 * C + 2 * kStackBufs; ++s) mbar_init(wfull + s, 1);
+        for (int s = 0; s < 2 * C + 2 * kStackBufs; ++s) mbar_init(wfull + s, 1);
         mbar_fence_init();
     }
     __syncthreads();
 
-    if (warp == 0) {
-        // ------------------------------------------------ weight producer
-        if (lane != 0) return;
+    if (warp < kStackProducers) {
+        // ------------------------------------------------ weight producers
+        // producer warp w issues the jobs jl = w, w + P, ... (P producers)
         const StackGeom g = stack_geom(p);
         StackCopy q;
         q.nb01_g = p.nb01_g;
@@ -641,31 +760,39 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
         for (int t = 0; t < 4; ++t) q.tile[t] = p.gu_tile[t];
         const int stage_bytes = p.stage_bytes;
         StackWalk walk{0, 0};
-        walk.advance(g, b);
-        int issued = 0, s = 0, n = 0;
-        for (int jl = 0; jl < mine; ++jl) {
-            if (n > 0 && !stack_mbar_wait(empty + s, (uint32_t)((n - 1) & 1))) {
-                record_error(GX_DEVERR_TIMEOUT);
+        walk.advance(g, b + warp * G);
+        int last = -1;   // the last job this warp issued
+        bool aborted = false;
+        for (int jl = warp; jl < mine; jl += kStackProducers) {
+            const int s = jl % C, n = jl / C;
+            int okw = 1;
+            if (n > 0) {
+                if (lane == 0) okw = stack_mbar_wait(empty + s, (uint32_t)((n - 1) & 1)) ? 1 : 0;
+                okw = __shfl_sync(0xffffffffu, okw, 0);
+            }
+            if (!okw) {
+                if (lane == 0) record_error(GX_DEVERR_TIMEOUT);
+                aborted = true;
                 break;
             }
-            stack_issue_weights(q, walk.job(g), slots, wt, stages + s * stage_bytes, wfull + s);
-            ++issued;
-            walk.advance(g, G);
-            if (++s == C) {
-                s = 0;
-                ++n;
-            }
+            stack_issue_weights(q, walk.job(g), slots, wt, stages + s * stage_bytes, wfull + s, lane);
+            last = jl;
+            walk.advance(g, kStackProducers * G);
         }
-        // let the last copy of every stage land before the CTA can exit
-        for (int jl = issued - C > 0 ? issued - C : 0; jl < issued; ++jl)
-            stack_mbar_wait(wfull + jl % C, (uint32_t)((jl / C) & 1));
+        // Let the copies of this warp that no later job consumed land before
+        // the CTA can exit: a stage's final job (jl + C >= mine); a job with a
+        // successor on its stage was consumed before the successor was issued.
+        // After an abort, every recent copy (bounded waits).
+        if (lane == 0)
+            for (int jl = last; jl >= 0 && jl > last - C; jl -= kStackProducers)
+                if (aborted || jl + C >= mine) stack_mbar_wait(wfull + jl % C, (uint32_t)((jl / C) & 1));
         return;
     }
-    if (warp == 1 || warp == 2) {
+    if (warp == kStackProducers || warp == kStackProducers + 1) {
         // -------------------------------------------------- input producers
         if (lane != 0) return;
-        const int kind = warp - 1;
-        stack_input_producer(p, kind, mine, b, G, rel, afull, kind == 0 ? xbar : dbar, meta,
+        const int kind = warp - kStackProducers;
+        stack_input_producer(p, kind, mine, b, G, kind == 0 ? xbar : dbar, fillw + kind * kStackBufs,
                              bufdone + kind * kStackBufs, kind == 0 ? xbuf : dbuf, kind == 0 ? xbytes : dbytes);
         return;
     }
@@ -676,7 +803,7 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
     // still uses stage jl % C, and each stage is consumed in job order: the
     // warp that takes job jl first waits until job jl - C was released.
     const int W = p.W;
-    const int c = warp - 3;
+    const int c = warp - kStackProducers - 2;
     if (c >= W) return;
     // quantize the inputs of layers L = b, b+G, ... (one warp per Q8 block)
     {
@@ -719,12 +846,26 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
             }
         }
         ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
-        ok = ok && stack_mbar_wait(wfull + cs, ph) && stack_mbar_wait(afull + cs, ph);
+        ok = ok && stack_mbar_wait(wfull + cs, ph);
         const StackJob J = stack_job(g, b + jl * G);
-        const int mt = ok ? *reinterpret_cast<volatile int *>(meta + cs) : 0;
-        const int bi = mt & 0xff;
+        // the job's input buffer: its fill word must name the job's key
+        const int key = J.L * p.T + J.t, bi = key % kStackBufs;
+        int fpar = 0;
+        if (lane == 0 && ok) {
+            const volatile int * fw = fillw + (J.gu ? 0 : kStackBufs) + bi;
+            bool got = false;
+            for (uint32_t i = 0; i < (1u << 23) && !got; ++i) {
+                const int v = *fw;
+                got = (v >> 1) == key;
+                fpar = v & 1;
+                if (!got && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+            }
+            ok = got;
+        }
+        ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+        fpar = __shfl_sync(0xffffffffu, fpar, 0);
         uint64_t * ibar = (J.gu ? xbar : dbar) + bi;
-        ok = ok && stack_mbar_wait(ibar, (uint32_t)(mt >> 8));
+        ok = ok && stack_mbar_wait(ibar, (uint32_t)fpar);
         if (__any_sync(0xffffffffu, !ok)) {
             if (lane == 0) record_error(GX_DEVERR_TIMEOUT);
             break;
@@ -790,22 +931,25 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
             }
             const int nblk = p.I / p.qblk, blk = J.r0 / p.qblk;
             __syncwarp();
+            // release this job's activation values, then count it into its
+            // Q8 block; the block's last arriver acquires everyone's values
             int last = 0;
             if (lane == 0) {
                 fence_acq_rel_gpu();
                 last = atomicAdd(ly.cnt + J.pair * nblk + blk, 1) == p.qblk / p.Rg - 1;
             }
             if (__shfl_sync(0xffffffffu, last, 0)) {
-                // this job finished the Q8 block last: quantize it
+                // this job finished the Q8 block last: quantize it and count the
+                // block into its token (the down inputs wait for k*I/qblk blocks)
                 fence_acq_rel_gpu();
                 quant_block_split<VD, true>(ly.act + (int64_t)J.pair * p.I, ly.actq + (int64_t)J.pair * p.ald.pitch,
                                             p.ald, blk, lane);
                 fence_proxy_async_global();
                 __syncwarp();
-            }
-            if (lane == 0) {
-                fence_acq_rel_gpu();
-                atomicAdd(p.gu_done + J.L * p.T + J.t, 1);
+                if (lane == 0) {
+                    fence_acq_rel_gpu();
+                    atomicAdd(p.gu_done + J.L * p.T + J.t, 1);
+                }
             }
         } else if constexpr (kMode == 1) {
             float * dts = reinterpret_cast<float *>(smem + p.dots_off) + c * 32;
@@ -852,8 +996,10 @@ __global__ void __launch_bounds__(96 + 32 * kStackMaxWarps, 1) k_stack(const __g
                 d0 = q8_0_finish(acc[0]);
                 d1 = q8_0_finish(acc[1]);
             } else {
-                d0 = q6k_row2(st + q * p.pitch_d, a0, p.ald, par, p.I / 256, 16);
-                d1 = q6k_row2(st + (q + 16) * p.pitch_d, a1, p.ald, par, p.I / 256, 16);
+                if (p.k * p.Rd == 16)   // one row per lane
+                    q6k_rows2<1>(st + q * p.pitch_d, st, a0, a0, p.ald, par, p.I / 256, 16, d0, d1);
+                else
+                    q6k_rows2<2>(st + q * p.pitch_d, st + (q + 16) * p.pitch_d, a0, a1, p.ald, par, p.I / 256, 16, d0, d1);
                 __syncwarp();
                 if (lane == 0) {
                     __threadfence_block();
