@@ -754,6 +754,13 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     const int ra = p.row_mode == 1 ? 64 : 256;
     if (p.H % ra || p.I % ra || p.I % p.Rg || p.qblk % p.Rg || p.H % p.Rd) return 0;
     if (p.C < 1 || p.C > kStackMaxConsumers || p.NL < 1 || p.NL > kStackMaxLayers) return 0;
+    // every stage belongs to one weight producer (stage s gets jobs s, s+C, ...,
+    // all of producer s % P): that producer issued the stage's previous job, so
+    // the stage's "empty" barrier is at most one phase behind when it waits on
+    // it and the parity wait is unambiguous. With C not a multiple of P two
+    // producers would share a stage and one could wait on a barrier two phases
+    // behind, read the older phase as complete and refill a stage in use.
+    if (p.C % kStackProducers != 0) return 0;
     if (p.W < 1 || p.W > kStackMaxWarps) return 0;
     if (p.row_mode == 1 && (p.Rd & 1)) return 0;   // octet row pairs stay inside one expert
     threads = 32 * (kStackProducers + 2) + 32 * p.W;

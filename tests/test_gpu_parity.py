@@ -373,6 +373,9 @@ def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name, T, layers, layer
                    (gxlib.TYPE_MXFP4, gxlib.TYPE_MXFP4), (gxlib.TYPE_IQ1_S, gxlib.TYPE_IQ1_S)}
     expect = not layerwise and (m.type_gate, m.type_down) in stack_types
     assert info["stack_kernel"] == (1 if expect else 0), info
+    if expect:
+        # each ring stage belongs to one of the two weight-producer warps
+        assert info["stages"] % 2 == 0, info
     call = StackCall(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, T)
     rng = np.random.default_rng(5 + T)
     stream = torch.cuda.current_stream()
