@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--prefill", type=int, default=512, help="prefill tokens at full residency (0 to skip)")
     ap.add_argument("--cpu-sample-layers", type=int, default=3)
     ap.add_argument("--layers", type=int, default=0, help="fewer layers (small profiling cases only)")
+    ap.add_argument("--ep", action="store_true",
+                    help="expert-parallel decode over the N GPUs of the launch (one line; not the headline)")
+    ap.add_argument("--ep-tokens", type=int, default=1, help="decode tokens per GPU per step in --ep mode")
     ap.add_argument("--headline-only", action="store_true",
                     help="time the headline and e2e lines only (profiling runs): skips the layerwise, per-layer-call "
                          "and prefill comparison sections, which lie outside the timed region")
@@ -197,6 +200,112 @@ def fill_tier(gx, torch, model, tier_np_ptr, tier_t, dev, seed):
         tier_t[L * E * model.record:(L + 1) * E * model.record].copy_(stage)
     torch.cuda.synchronize()
     del stage
+
+
+def fill_tier_owned(gx, torch, model, owned, tier_t, dev, seed):
+    """The records of the experts `owned` (global ids, in local order) of
+    every layer, with the global generator streams, into the pinned tier."""
+    lib = gx.lib()
+    E, n = model.experts, len(owned)
+    stage = torch.empty(n * model.record, dtype=torch.uint8, device=dev)
+    for L in range(model.layers):
+        stage.zero_()
+        base = stage.data_ptr()
+        for li, e in enumerate(owned):
+            sid = (L * E + e) * 3
+            r = base + li * model.record
+            gx.check(lib.gx_synth_weights(model.type_down, r, model.intermediate, model.hidden, seed, sid + 0, 0.02, None))
+            gx.check(lib.gx_synth_weights(model.type_gate, r + model.off_gate, model.hidden, model.intermediate, seed,
+                                          sid + 1, 0.02, None))
+            gx.check(lib.gx_synth_weights(model.type_up, r + model.off_up, model.hidden, model.intermediate, seed,
+                                          sid + 2, 0.02, None))
+        tier_t[L * n * model.record:(L + 1) * n * model.record].copy_(stage)
+    torch.cuda.synchronize()
+    del stage
+
+
+def run_ep(args):
+    """Expert-parallel decode: expert e of every layer lives on rank e % N
+    (its own arena, all of its experts resident); each rank serves its own
+    T tokens per step through every layer: NCCL dispatch of the (token, slot)
+    pairs to the owners, the owners' routed-expert FFN, NCCL combine back and
+    the weighted sum in slot order at home (gx_ep_layer_forward)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import galactus_b200 as gx
+    from galactus_b200.models import ModelShape
+    from galactus_b200.moe import ExpertParallel, device_error
+    from galactus_b200.routing import routes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    gx.check(gx.lib().gx_device_init(local))
+    model = gx.MODELS[args.model]
+    if args.layers:
+        model = model.with_layers(args.layers)
+    E, k, H, NL, T = model.experts, model.used, model.hidden, model.layers, args.ep_tokens
+    owned = [e for e in range(E) if e % world == rank]
+    lm = ModelShape(**{**model.__dict__, "experts": len(owned), "used": min(k, len(owned))})
+    tier = torch.empty(NL * len(owned) * model.record, dtype=torch.uint8, pin_memory=True)
+    fill_tier_owned(gx, torch, model, owned, tier, dev, model.seed)
+    arena = gx.Arena(lm, capacity_bytes=len(owned) * model.record * NL, policy=gx.POLICY_AUTO,
+                     max_tokens=world * T * k, host_tier_base=tier.data_ptr(), device=local)
+    stream = torch.cuda.Stream(device=dev)
+    arena.warm_all(stream)
+    torch.cuda.synchronize()
+    pg = dist.distributed_c10d._get_default_group()
+    ep = ExpertParallel(arena, pg._get_backend(dev)._comm_ptr(), rank, world, E, 0)   # expert e on rank e % N
+    n_steps = args.warmup + args.steps
+    ids_all, w_all = routes(model, n_steps * T, NL, seed=model.seed * 1000 + 31 + rank, rho=0.7)
+    ids_c = [[np.ascontiguousarray(ids_all[s * T:(s + 1) * T, L]) for L in range(NL)] for s in range(n_steps)]
+    w_dev = torch.from_numpy(np.ascontiguousarray(w_all.reshape(n_steps, T, NL, k).transpose(0, 2, 1, 3))).to(dev)
+    rng = np.random.default_rng(rank)
+    x_dev = torch.from_numpy(rng.standard_normal((NL, T, H)).astype(np.float32)).to(dev)
+    out = torch.empty((NL, T, H), dtype=torch.float32, device=dev)
+
+    def step(s):
+        for L in range(NL):
+            ep.layer_forward(L, x_dev[L], ids_c[s][L], w_dev[s, L], out[L], stream)
+
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            step(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local, pci_bus_id(torch, dev)) as clk:
+            ev0.record(stream)
+            for s in range(args.warmup, n_steps):
+                step(s)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    err = device_error()
+    ep.close()
+    arena.close()
+    if rank == 0:
+        tn = gx.TYPE_NAMES
+        print(json.dumps({
+            "metric": f"MoE-layer decode tok/s, expert-parallel over {world} GPU(s) ({NL}-layer routed-expert FFN stack)",
+            "value": world * T * args.steps / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 dot / f32 tail", "data": "synthetic (seeded weights and routes)",
+            "config": {"workload": f"{model.name} MoE stack, {T} decode token(s) per GPU, {NL} layers, H {H}, E {E} "
+                                   f"(expert e on GPU e mod {world}), top-{k}, {tn[model.type_gate]}/{tn[model.type_down]}",
+                       "model": model.name, "global_batch": world * T, "seq_len": 1, "parallelism": f"ep{world}",
+                       "experts_per_gpu": len(owned), "l2": "expert weights read per step exceed L2, no flush"},
+            "device_error": err, "clocks": clk.summary()}))
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def run_ours(args):
@@ -638,6 +747,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.ep:
+        run_ep(args)
     else:
         run_ours(args)
 

@@ -1062,8 +1062,9 @@ bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
         sp.Rd = drows / sp.k;
         for (int C = cap; C >= 2; --C) {
             sp.C = C;
-            // one consumer warp per stage, at least 8
-            sp.W = wenv ? wenv : std::min(std::max(8, C), gx::kStackMaxWarps);
+            // one consumer warp per stage (two for the split octet jobs), at least 8
+            const int per_stage = sp.row_mode == 1 ? 2 : 1;
+            sp.W = wenv ? wenv : std::min(std::max(8, per_stage * C), gx::kStackMaxWarps);
             smem = gx::stack_layout(sp, threads);
             if (smem != 0) return true;
         }

@@ -797,13 +797,13 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     p.stage_bytes = (int32_t)align_up(gw > dw ? gw : dw, 128);
     p.bar_off = 0;      // 3*C + 2*kStackBufs mbarriers
     p.meta_off = (uint32_t)align_up(8ull * (3 * kStackMaxConsumers + 2 * kStackBufs), 128);
-    // metadata word and release counter per stage, buffer counters, next job
-    p.stage_off = p.meta_off + (uint32_t)align_up(4ull * (2 * kStackMaxConsumers + 2 * kStackBufs + 1), 128);
+    // fill words, buffer counters, release counter per stage, next task, finished parts per stage
+    p.stage_off = p.meta_off + (uint32_t)align_up(4ull * (3 * kStackMaxConsumers + 2 * kStackBufs + 1), 128);
     p.xbuf_off = p.stage_off + (uint32_t)p.C * (uint32_t)p.stage_bytes;
     p.dbuf_off = p.xbuf_off + align_up((uint64_t)kStackBufs * p.alx.pitch, 128);
     p.wt_off = p.dbuf_off + align_up((uint64_t)kStackBufs * p.k * p.ald.pitch, 128);
     p.dots_off = p.wt_off + (uint32_t)p.NL * 32u;    // per-layer weight bases
-    p.slots_off = p.dots_off + (uint32_t)p.W * 32u * 4u;   // 32 down-row dots per consumer warp
+    p.slots_off = p.dots_off + (uint32_t)p.C * 32u * 4u;   // 32 down-row dots per stage
     const uint32_t total = p.slots_off + align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
     return total <= kMaxSmem ? total : 0;
 }

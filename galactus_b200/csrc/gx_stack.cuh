@@ -564,16 +564,16 @@ __device__ __forceinline__ void q6k_rows2(const uint8_t * row0, const uint8_t * 
 
 // Octet gate/up job: gate row i and up row i (octet g, i = 4*pass + g)
 // against the token's activation row; every lane of octet g ends with the
-// two dots of row 4*pass + g.
+// two dots of row 4*pass + g. Passes ps0, ps0 + pstep, ... (a split job's
+// warps take every pstep-th pass).
 template <int TYPE>
 __device__ __forceinline__ void stack_gu_oct(const StackParams & p, const uint8_t * st, const uint8_t * xa, int lane,
-                                             float (&gd)[2], float (&ud)[2]) {
+                                             float (&gd)[2], float (&ud)[2], int ps0, int pstep) {
     using Q = Oct<TYPE>;
     const int o = lane & 7, g = lane >> 3;
     const int U = p.H / Q::UNIT;
     const typename Q::A al = Q::inita(xa, p.alx, o);
-#pragma unroll
-    for (int ps = 0; ps < 2; ++ps) {
+    for (int ps = ps0; ps < 2; ps += pstep) {
         const int row = 4 * ps + g;
         typename Q::St acc[2];
         const typename Q::W wl[2] = {Q::initw(st, p.gu_tile[0] + row * (int)p.nb01_g, o),
@@ -594,12 +594,12 @@ __device__ __forceinline__ void stack_gu_oct(const StackParams & p, const uint8_
 // expert's activation row; lane 8g writes both dots to dots[row].
 template <int TYPE>
 __device__ __forceinline__ void stack_d_oct(const StackParams & p, const uint8_t * st, const uint8_t * da, int lane,
-                                            float * dots) {
+                                            float * dots, int ps0, int pstep) {
     using Q = Oct<TYPE>;
     const int o = lane & 7, g = lane >> 3;
     const int U = p.I / Q::UNIT;
     const int passes = p.k * p.Rd / 8;
-    for (int ps = 0; ps < passes; ++ps) {
+    for (int ps = ps0; ps < passes; ps += pstep) {
         const int row = 8 * ps + 2 * g;
         const typename Q::A al = Q::inita(da + (row / p.Rd) * p.ald.pitch, p.ald, o);
         typename Q::St acc[2];
@@ -691,6 +691,9 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
     // row mode: 0 two-lane Q8_0 rows, 2 two-lane Q4_K gate/up + Q6_K down rows, 1 octet rows
     constexpr int kMode = (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0 : (TG == GX_T_Q4_K && TD == GX_T_Q6_K) ? 2 : 1;
     constexpr int VG = Oct<TG>::VDT, VD = Oct<TD>::VDT;       // activation types of gate/up and down
+    // octet jobs are compute-bound: two warps share each (passes split
+    // between them), so twice as many warps compute for the same ring
+    constexpr int kSplit = kMode == 1 ? 2 : 1;
     extern __shared__ __align__(128) uint8_t smem[];
     const int C = p.C;
     uint64_t * wfull = reinterpret_cast<uint64_t *>(smem + p.bar_off);
@@ -730,7 +733,8 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
             w.nb02 = p.layers[L].nb02;
             wt[L] = w;
         }
-        if (tid < 2 * kStackBufs + kStackMaxConsumers + 1) bufdone[tid] = 0;   // bufdone, rel, next job
+        // bufdone, rel, next task, per-stage finished-part counters
+        if (tid < 2 * kStackBufs + 2 * kStackMaxConsumers + 1) bufdone[tid] = 0;
         if (tid < 2 * kStackBufs) fillw[tid] = -1;                                // no key filled yet
         if (__syncthreads_or(bad)) {
             if (tid == 0) record_error(GX_DEVERR_DOMAIN);
@@ -829,10 +833,13 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
     const StackGeom g = stack_geom(p);
     const int par = lane >> 4;   // block parity of this lane
     int * next_job = rel + kStackMaxConsumers;
+    int * parts = next_job + 1;                        // [C] finished parts of the stage's current job
+    float * sdots = reinterpret_cast<float *>(smem + p.dots_off);   // [C][32] down-row dots per stage
     for (;;) {
-        int jl = 0;
-        if (lane == 0) jl = atomicAdd(next_job, 1);
-        jl = __shfl_sync(0xffffffffu, jl, 0);
+        int task = 0;
+        if (lane == 0) task = atomicAdd(next_job, 1);
+        task = __shfl_sync(0xffffffffu, task, 0);
+        const int jl = task / kSplit, sub = task - jl * kSplit;
         if (jl >= mine) break;
         const int cs = jl % C, n = jl / C;
         const uint32_t ph = (uint32_t)(n & 1);
@@ -912,17 +919,21 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                 }
             } else {
                 float gd[2], ud[2];
-                stack_gu_oct<TG>(p, st, xa, lane, gd, ud);
+                stack_gu_oct<TG>(p, st, xa, lane, gd, ud, sub, kSplit);
                 __syncwarp();
                 if (lane == 0) {
+                    // the job's last part frees the stage and the input buffer
                     __threadfence_block();
-                    atomicAdd(done, 1);
-                    atomicAdd(rel + cs, 1);
-                    mbar_arrive(empty + cs);   // stage and input buffer are free
+                    if (atomicAdd(parts + cs, 1) == kSplit - 1) {
+                        parts[cs] = 0;
+                        __threadfence_block();
+                        atomicAdd(done, 1);
+                        atomicAdd(rel + cs, 1);
+                        mbar_arrive(empty + cs);
+                    }
                 }
                 if ((lane & 7) == 0) {
-#pragma unroll
-                    for (int ps = 0; ps < 2; ++ps) {
+                    for (int ps = sub; ps < 2; ps += kSplit) {
                         const float a = p.act == 1 ? act_swiglu_oai(gd[ps], ud[ps], p.alpha, p.limit)
                                                    : act_swiglu(gd[ps], ud[ps]);
                         ly.act[(int64_t)J.pair * p.I + J.r0 + 4 * ps + (lane >> 3)] = a;
@@ -936,7 +947,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
             int last = 0;
             if (lane == 0) {
                 fence_acq_rel_gpu();
-                last = atomicAdd(ly.cnt + J.pair * nblk + blk, 1) == p.qblk / p.Rg - 1;
+                last = atomicAdd(ly.cnt + J.pair * nblk + blk, 1) == kSplit * (p.qblk / p.Rg) - 1;
             }
             if (__shfl_sync(0xffffffffu, last, 0)) {
                 // this job finished the Q8 block last: quantize it and count the
@@ -952,21 +963,32 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                 }
             }
         } else if constexpr (kMode == 1) {
-            float * dts = reinterpret_cast<float *>(smem + p.dots_off) + c * 32;
-            stack_d_oct<TD>(p, st, dbuf + bi * dbytes, lane, dts);
+            float * dts = sdots + cs * 32;
+            stack_d_oct<TD>(p, st, dbuf + bi * dbytes, lane, dts, sub, kSplit);
             __syncwarp();
+            int lastp = 0;
             if (lane == 0) {
                 __threadfence_block();
-                atomicAdd(done, 1);
-                atomicAdd(rel + cs, 1);
-                mbar_arrive(empty + cs);
+                lastp = atomicAdd(parts + cs, 1) == kSplit - 1;
+                if (lastp) __threadfence_block();
             }
-            // output row rr = lane < Rd: sum over slots m of w[m] * dot(m*Rd + rr), in slot order
-            if (lane < p.Rd) {
-                const float * wr = ly.rw + (int64_t)J.t * p.k;
-                float accf = __fmul_rn(dts[lane], wr[0]);
-                for (int mm = 1; mm < p.k; ++mm) accf = __fadd_rn(accf, __fmul_rn(dts[mm * p.Rd + lane], wr[mm]));
-                ly.out[(int64_t)J.t * p.H + J.r0 + lane] = accf;
+            if (__shfl_sync(0xffffffffu, lastp, 0)) {
+                // the job's last part: every row dot is in the stage's scratch;
+                // output row rr = lane < Rd: sum over slots m of w[m] * dot(m*Rd + rr), in slot order
+                if (lane < p.Rd) {
+                    const float * wr = ly.rw + (int64_t)J.t * p.k;
+                    float accf = __fmul_rn(dts[lane], wr[0]);
+                    for (int mm = 1; mm < p.k; ++mm) accf = __fadd_rn(accf, __fmul_rn(dts[mm * p.Rd + lane], wr[mm]));
+                    ly.out[(int64_t)J.t * p.H + J.r0 + lane] = accf;
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    parts[cs] = 0;
+                    __threadfence_block();
+                    atomicAdd(done, 1);
+                    atomicAdd(rel + cs, 1);
+                    mbar_arrive(empty + cs);
+                }
             }
             __syncwarp();
         } else {
