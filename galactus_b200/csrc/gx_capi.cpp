@@ -1098,6 +1098,7 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
                   : (l0.type_gate == gx::GX_T_Q4_K && l0.type_down == gx::GX_T_Q6_K) ? 2
                                                                                      : 1;
     sp.gu_copies = sp.row_mode == 1 ? 2 : 4;
+    sp.need_grid = (l0.type_gate == gx::GX_T_IQ1_S || l0.type_down == gx::GX_T_IQ1_S) ? 1 : 0;
     int threads = 0;
     uint32_t smem = 0;
     if (!choose_stack_tiles(sp, threads, smem)) return GX_ERR_ALIGN;

@@ -804,7 +804,8 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     p.wt_off = p.dbuf_off + align_up((uint64_t)kStackBufs * p.k * p.ald.pitch, 128);
     p.dots_off = p.wt_off + (uint32_t)p.NL * 32u;    // per-layer weight bases
     p.slots_off = p.dots_off + (uint32_t)p.C * 32u * 4u;   // 32 down-row dots per stage
-    const uint32_t total = p.slots_off + align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
+    p.grid_off = p.slots_off + (uint32_t)align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
+    const uint32_t total = p.grid_off + (p.need_grid ? 2048u * 8u : 0u);
     return total <= kMaxSmem ? total : 0;
 }
 

@@ -326,14 +326,17 @@ template <> struct Oct<GX_T_IQ1_S> {
     static constexpr int UNIT = 256;
     struct St { float s = 0.0f; };
     struct W { const uint8_t * wb; int wo; };
-    struct A { const uint8_t * aq; const uint8_t * ar; ActLayout L; int o; };
+    // grid: the codebook, in global memory or a shared-memory copy
+    struct A { const uint8_t * aq; const uint8_t * ar; ActLayout L; int o; const uint2 * grid; };
     __device__ __forceinline__ static W initw(const uint8_t * wb, int wo, int) { return W{wb, wo}; }
-    __device__ __forceinline__ static A inita(const uint8_t * ar, const ActLayout & L, int o) {
+    __device__ __forceinline__ static A inita(const uint8_t * ar, const ActLayout & L, int o,
+                                              const uint2 * grid = g_iq1s_grid) {
         A a;
         a.aq = ar + 32 * o;
         a.ar = ar;
         a.L = L;
         a.o = o;
+        a.grid = grid;
         return a;
     }
     template <int PAR>
@@ -357,7 +360,7 @@ template <> struct Oct<GX_T_IQ1_S> {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const uint32_t gi = ((qsw[0] >> (8 * j)) & 0xffu) | (((qh >> (3 * j)) & 7u) << 8);
-                const uint2 g = g_iq1s_grid[gi];
+                const uint2 g = a.grid[gi];
                 p = dp4a(g.x, aw[2 * j], p);
                 p = dp4a(g.y, aw[2 * j + 1], p);
             }

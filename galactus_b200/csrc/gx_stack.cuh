@@ -567,12 +567,19 @@ __device__ __forceinline__ void q6k_rows2(const uint8_t * row0, const uint8_t * 
 // two dots of row 4*pass + g. Passes ps0, ps0 + pstep, ... (a split job's
 // warps take every pstep-th pass).
 template <int TYPE>
+__device__ __forceinline__ typename Oct<TYPE>::A oct_act(const uint8_t * ar, const ActLayout & L, int o,
+                                                        const uint2 * grid) {
+    if constexpr (TYPE == GX_T_IQ1_S) return Oct<TYPE>::inita(ar, L, o, grid);
+    else return Oct<TYPE>::inita(ar, L, o);
+}
+
+template <int TYPE>
 __device__ __forceinline__ void stack_gu_oct(const StackParams & p, const uint8_t * st, const uint8_t * xa, int lane,
-                                             float (&gd)[2], float (&ud)[2], int ps0, int pstep) {
+                                             float (&gd)[2], float (&ud)[2], int ps0, int pstep, const uint2 * grid) {
     using Q = Oct<TYPE>;
     const int o = lane & 7, g = lane >> 3;
     const int U = p.H / Q::UNIT;
-    const typename Q::A al = Q::inita(xa, p.alx, o);
+    const typename Q::A al = oct_act<TYPE>(xa, p.alx, o, grid);
     for (int ps = ps0; ps < 2; ps += pstep) {
         const int row = 4 * ps + g;
         typename Q::St acc[2];
@@ -594,14 +601,14 @@ __device__ __forceinline__ void stack_gu_oct(const StackParams & p, const uint8_
 // expert's activation row; lane 8g writes both dots to dots[row].
 template <int TYPE>
 __device__ __forceinline__ void stack_d_oct(const StackParams & p, const uint8_t * st, const uint8_t * da, int lane,
-                                            float * dots, int ps0, int pstep) {
+                                            float * dots, int ps0, int pstep, const uint2 * grid) {
     using Q = Oct<TYPE>;
     const int o = lane & 7, g = lane >> 3;
     const int U = p.I / Q::UNIT;
     const int passes = p.k * p.Rd / 8;
     for (int ps = ps0; ps < passes; ps += pstep) {
         const int row = 8 * ps + 2 * g;
-        const typename Q::A al = Q::inita(da + (row / p.Rd) * p.ald.pitch, p.ald, o);
+        const typename Q::A al = oct_act<TYPE>(da + (row / p.Rd) * p.ald.pitch, p.ald, o, grid);
         typename Q::St acc[2];
         const typename Q::W wl[2] = {Q::initw(st, row * p.pitch_d, o), Q::initw(st, (row + 1) * p.pitch_d, o)};
         int v = 0;
@@ -809,6 +816,11 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
     const int W = p.W;
     const int c = warp - kStackProducers - 2;
     if (c >= W) return;
+    if constexpr (TG == GX_T_IQ1_S || TD == GX_T_IQ1_S) {
+        uint2 * g2 = reinterpret_cast<uint2 *>(smem + p.grid_off);
+        for (int i = c * 32 + lane; i < 2048; i += 32 * W) g2[i] = g_iq1s_grid[i];
+        named_barrier(2, 32 * W);
+    }
     // quantize the inputs of layers L = b, b+G, ... (one warp per Q8 block)
     {
         const int nblk = p.H / (VG == GX_T_Q8_0 ? 32 : 256);
@@ -835,6 +847,9 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
     int * next_job = rel + kStackMaxConsumers;
     int * parts = next_job + 1;                        // [C] finished parts of the stage's current job
     float * sdots = reinterpret_cast<float *>(smem + p.dots_off);   // [C][32] down-row dots per stage
+    // IQ1_S: the codebook in shared memory (copied by the consumers before the
+    // input quantization barrier below, i.e. before their first job)
+    const uint2 * sgrid = reinterpret_cast<const uint2 *>(smem + p.grid_off);
     for (;;) {
         int task = 0;
         if (lane == 0) task = atomicAdd(next_job, 1);
@@ -919,7 +934,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                 }
             } else {
                 float gd[2], ud[2];
-                stack_gu_oct<TG>(p, st, xa, lane, gd, ud, sub, kSplit);
+                stack_gu_oct<TG>(p, st, xa, lane, gd, ud, sub, kSplit, sgrid);
                 __syncwarp();
                 if (lane == 0) {
                     // the job's last part frees the stage and the input buffer
@@ -964,7 +979,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
             }
         } else if constexpr (kMode == 1) {
             float * dts = sdots + cs * 32;
-            stack_d_oct<TD>(p, st, dbuf + bi * dbytes, lane, dts, sub, kSplit);
+            stack_d_oct<TD>(p, st, dbuf + bi * dbytes, lane, dts, sub, kSplit, sgrid);
             __syncwarp();
             int lastp = 0;
             if (lane == 0) {
