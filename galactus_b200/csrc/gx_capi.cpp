@@ -1062,8 +1062,8 @@ bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
         sp.Rd = drows / sp.k;
         for (int C = cap; C >= 2; --C) {
             sp.C = C;
-            // one consumer warp per stage (two for the split octet jobs), at least 8
-            const int per_stage = sp.row_mode == 1 ? 2 : 1;
+            // one consumer warp per stage (two for split jobs), at least 8
+            const int per_stage = (sp.row_mode == 1 || (sp.row_mode == 2 && drows == 32)) ? 2 : 1;
             sp.W = wenv ? wenv : std::min(std::max(8, per_stage * C), gx::kStackMaxWarps);
             smem = gx::stack_layout(sp, threads);
             if (smem != 0) return true;
@@ -1102,6 +1102,7 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     int threads = 0;
     uint32_t smem = 0;
     if (!choose_stack_tiles(sp, threads, smem)) return GX_ERR_ALIGN;
+    sp.split = (sp.row_mode == 1 || (sp.row_mode == 2 && sp.k * sp.Rd == 32)) ? 2 : 1;
     sp.n_gu = (int32_t)(p->T * p->k * (l0.I / sp.Rg));
     sp.n_d = (int32_t)(p->T * (l0.H / sp.Rd));
     int per_sm = 0;

@@ -145,6 +145,7 @@ struct StackParams {
     float alpha, limit;
     uint32_t bar_off, meta_off, stage_off, xbuf_off, dbuf_off, wt_off, slots_off, dots_off;
     int32_t need_grid;         // 1: IQ1_S rows, the 16 KB codebook copied to shared memory at grid_off
+    int32_t split;             // warps per job: 2 for octet jobs and 32-row two-lane K-quant down jobs, else 1
     uint32_t grid_off;
     StackLayer layers[kStackMaxLayers];
 };

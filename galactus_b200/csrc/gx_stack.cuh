@@ -698,9 +698,10 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
     // row mode: 0 two-lane Q8_0 rows, 2 two-lane Q4_K gate/up + Q6_K down rows, 1 octet rows
     constexpr int kMode = (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0 : (TG == GX_T_Q4_K && TD == GX_T_Q6_K) ? 2 : 1;
     constexpr int VG = Oct<TG>::VDT, VD = Oct<TD>::VDT;       // activation types of gate/up and down
-    // octet jobs are compute-bound: two warps share each (passes split
-    // between them), so twice as many warps compute for the same ring
-    constexpr int kSplit = kMode == 1 ? 2 : 1;
+    // warps per job (p.split): octet jobs are compute-bound and two warps
+    // share each (passes split between them); so do the 32-row down jobs of
+    // the two-lane K-quant rows (row q | row q + 16 of each lane pair), whose
+    // gate/up jobs stay whole (their second part only counts itself)
     extern __shared__ __align__(128) uint8_t smem[];
     const int C = p.C;
     uint64_t * wfull = reinterpret_cast<uint64_t *>(smem + p.bar_off);
@@ -854,7 +855,8 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
         int task = 0;
         if (lane == 0) task = atomicAdd(next_job, 1);
         task = __shfl_sync(0xffffffffu, task, 0);
-        const int jl = task / kSplit, sub = task - jl * kSplit;
+        const int split = kMode == 0 ? 1 : p.split;
+        const int jl = task / split, sub = task - jl * split;
         if (jl >= mine) break;
         const int cs = jl % C, n = jl / C;
         const uint32_t ph = (uint32_t)(n & 1);
@@ -917,14 +919,22 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                     }
                     dot = q8_0_finish_x1(acc[0]);
                 } else {
-                    dot = q4k_row2(st + p.gu_tile[tl] + qr * (int)p.nb01_g, xa, p.alx, gp, p.H / 256, 1);
+                    if (sub == 0) dot = q4k_row2(st + p.gu_tile[tl] + qr * (int)p.nb01_g, xa, p.alx, gp, p.H / 256, 1);
                     __syncwarp();
                     if (lane == 0) {
+                        // the job's last part frees the stage and the input buffer
                         __threadfence_block();
-                        atomicAdd(done, 1);
-                        atomicAdd(rel + cs, 1);
-                        mbar_arrive(empty + cs);   // stage and input buffer are free
+                        if (split == 1 || atomicAdd(parts + cs, 1) == split - 1) {
+                            if (split > 1) {
+                                parts[cs] = 0;
+                                __threadfence_block();
+                            }
+                            atomicAdd(done, 1);
+                            atomicAdd(rel + cs, 1);
+                            mbar_arrive(empty + cs);
+                        }
                     }
+                    if (sub != 0) continue;   // a whole gate/up job's second part only counts itself
                 }
                 // gate row i = 4*tl + qr (tl < 2) pairs with up row i in tile tl + 2 (lane + 4)
                 const float up = __shfl_down_sync(0xffffffffu, dot, 4);
@@ -934,12 +944,12 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                 }
             } else {
                 float gd[2], ud[2];
-                stack_gu_oct<TG>(p, st, xa, lane, gd, ud, sub, kSplit, sgrid);
+                stack_gu_oct<TG>(p, st, xa, lane, gd, ud, sub, split, sgrid);
                 __syncwarp();
                 if (lane == 0) {
                     // the job's last part frees the stage and the input buffer
                     __threadfence_block();
-                    if (atomicAdd(parts + cs, 1) == kSplit - 1) {
+                    if (atomicAdd(parts + cs, 1) == split - 1) {
                         parts[cs] = 0;
                         __threadfence_block();
                         atomicAdd(done, 1);
@@ -948,7 +958,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                     }
                 }
                 if ((lane & 7) == 0) {
-                    for (int ps = sub; ps < 2; ps += kSplit) {
+                    for (int ps = sub; ps < 2; ps += split) {
                         const float a = p.act == 1 ? act_swiglu_oai(gd[ps], ud[ps], p.alpha, p.limit)
                                                    : act_swiglu(gd[ps], ud[ps]);
                         ly.act[(int64_t)J.pair * p.I + J.r0 + 4 * ps + (lane >> 3)] = a;
@@ -962,7 +972,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
             int last = 0;
             if (lane == 0) {
                 fence_acq_rel_gpu();
-                last = atomicAdd(ly.cnt + J.pair * nblk + blk, 1) == kSplit * (p.qblk / p.Rg) - 1;
+                last = atomicAdd(ly.cnt + J.pair * nblk + blk, 1) == (kMode == 1 ? split : 1) * (p.qblk / p.Rg) - 1;
             }
             if (__shfl_sync(0xffffffffu, last, 0)) {
                 // this job finished the Q8 block last: quantize it and count the
@@ -979,12 +989,12 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
             }
         } else if constexpr (kMode == 1) {
             float * dts = sdots + cs * 32;
-            stack_d_oct<TD>(p, st, dbuf + bi * dbytes, lane, dts, sub, kSplit, sgrid);
+            stack_d_oct<TD>(p, st, dbuf + bi * dbytes, lane, dts, sub, split, sgrid);
             __syncwarp();
             int lastp = 0;
             if (lane == 0) {
                 __threadfence_block();
-                lastp = atomicAdd(parts + cs, 1) == kSplit - 1;
+                lastp = atomicAdd(parts + cs, 1) == split - 1;
                 if (lastp) __threadfence_block();
             }
             if (__shfl_sync(0xffffffffu, lastp, 0)) {
@@ -1033,6 +1043,42 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                 d0 = q8_0_finish(acc[0]);
                 d1 = q8_0_finish(acc[1]);
             } else {
+                if (split == 2) {
+                    // part sub: row R = q + 16*sub of each lane pair, into the stage's dot scratch
+                    const int R = q + 16 * sub;
+                    const uint8_t * ar = da + (R / p.Rd) * p.ald.pitch;
+                    float dd, unused;
+                    q6k_rows2<1>(st + R * p.pitch_d, st, ar, ar, p.ald, par, p.I / 256, 16, dd, unused);
+                    float * dts = sdots + cs * 32;
+                    if (par == 0) dts[R] = dd;
+                    __syncwarp();
+                    int lastp = 0;
+                    if (lane == 0) {
+                        __threadfence_block();
+                        lastp = atomicAdd(parts + cs, 1) == split - 1;
+                        if (lastp) __threadfence_block();
+                    }
+                    if (__shfl_sync(0xffffffffu, lastp, 0)) {
+                        // the last part: output row rr = lane < Rd, slots in order
+                        if (lane < p.Rd) {
+                            const float * wr = ly.rw + (int64_t)J.t * p.k;
+                            float accf = __fmul_rn(dts[lane], wr[0]);
+                            for (int mm = 1; mm < p.k; ++mm)
+                                accf = __fadd_rn(accf, __fmul_rn(dts[mm * p.Rd + lane], wr[mm]));
+                            ly.out[(int64_t)J.t * p.H + J.r0 + lane] = accf;
+                        }
+                        __syncwarp();
+                        if (lane == 0) {
+                            parts[cs] = 0;
+                            __threadfence_block();
+                            atomicAdd(done, 1);
+                            atomicAdd(rel + cs, 1);
+                            mbar_arrive(empty + cs);
+                        }
+                    }
+                    __syncwarp();
+                    continue;
+                }
                 if (p.k * p.Rd == 16)   // one row per lane
                     q6k_rows2<1>(st + q * p.pitch_d, st, a0, a0, p.ald, par, p.I / 256, 16, d0, d1);
                 else
