@@ -1063,7 +1063,7 @@ bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
         for (int C = cap; C >= 2; --C) {
             sp.C = C;
             // one consumer warp per stage (two for split jobs), at least 8
-            const int per_stage = (sp.row_mode == 1 || (sp.row_mode == 2 && drows == 32)) ? 2 : 1;
+            const int per_stage = (sp.row_mode == 1 || ((sp.row_mode == 2 || sp.row_mode == 3) && drows == 32)) ? 2 : 1;
             sp.W = wenv ? wenv : std::min(std::max(8, per_stage * C), gx::kStackMaxWarps);
             smem = gx::stack_layout(sp, threads);
             if (smem != 0) return true;
@@ -1094,15 +1094,16 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     sp.act = l0.g.act;
     sp.alpha = l0.g.alpha;
     sp.limit = l0.g.limit;
-    sp.row_mode = (l0.type_gate == gx::GX_T_Q8_0 && l0.type_down == gx::GX_T_Q8_0)   ? 0
-                  : (l0.type_gate == gx::GX_T_Q4_K && l0.type_down == gx::GX_T_Q6_K) ? 2
-                                                                                     : 1;
-    sp.gu_copies = sp.row_mode == 1 ? 2 : 4;
+    sp.row_mode = (l0.type_gate == gx::GX_T_Q8_0 && l0.type_down == gx::GX_T_Q8_0)     ? 0
+                  : (l0.type_gate == gx::GX_T_Q4_K && l0.type_down == gx::GX_T_Q6_K)   ? 2
+                  : (l0.type_gate == gx::GX_T_MXFP4 && l0.type_down == gx::GX_T_MXFP4) ? 3
+                                                                                       : 1;
+    sp.gu_copies = (sp.row_mode == 1 || sp.row_mode == 3) ? 2 : 4;
     sp.need_grid = (l0.type_gate == gx::GX_T_IQ1_S || l0.type_down == gx::GX_T_IQ1_S) ? 1 : 0;
     int threads = 0;
     uint32_t smem = 0;
     if (!choose_stack_tiles(sp, threads, smem)) return GX_ERR_ALIGN;
-    sp.split = (sp.row_mode == 1 || (sp.row_mode == 2 && sp.k * sp.Rd == 32)) ? 2 : 1;
+    sp.split = (sp.row_mode == 1 || ((sp.row_mode == 2 || sp.row_mode == 3) && sp.k * sp.Rd == 32)) ? 2 : 1;
     sp.n_gu = (int32_t)(p->T * p->k * (l0.I / sp.Rg));
     sp.n_d = (int32_t)(p->T * (l0.H / sp.Rd));
     int per_sm = 0;

@@ -750,8 +750,9 @@ static bool stack_copy_mode(int64_t nb01, int R, int32_t & row_copy, int32_t & p
 // of their type's 64- or 256-element units, checked per layer; 2 gate/up copies).
 uint32_t stack_layout(StackParams & p, int & threads) {
     if (p.Rg != 8 || p.Rd < 1 || (p.k * p.Rd != 32 && !(p.row_mode == 2 && p.k * p.Rd == 16))) return 0;
-    if (p.row_mode < 0 || p.row_mode > 2 || p.gu_copies != (p.row_mode == 1 ? 2 : 4)) return 0;
-    const int ra = p.row_mode == 1 ? 64 : 256;
+    const bool tiles8 = p.row_mode == 1 || p.row_mode == 3;   // gate/up as 2 copies of 8 rows
+    if (p.row_mode < 0 || p.row_mode > 3 || p.gu_copies != (tiles8 ? 2 : 4)) return 0;
+    const int ra = tiles8 ? 64 : 256;
     if (p.H % ra || p.I % ra || p.I % p.Rg || p.qblk % p.Rg || p.H % p.Rd) return 0;
     if (p.C < 1 || p.C > kStackMaxConsumers || p.NL < 1 || p.NL > kStackMaxLayers) return 0;
     // every stage belongs to one weight producer (stage s gets jobs s, s+C, ...,

@@ -326,6 +326,67 @@ __device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) {
     return d;
 }
 
+// prmt in its generic mode: each selector nibble's low three bits pick a byte
+// of {b:a}, its high bit replaces that byte by copies of the byte's sign bit
+__device__ __forceinline__ uint32_t prmt_sx(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// MXFP4 row x Q8_0 activation row (split layout), two lanes per row
+// (ggml_vec_dot_mxfp4_q8_0, diff:1167-1174, 1209-1240). Lane p takes block
+// 2u+p of every pair u (17 bytes: e8m0 scale, 16 bytes of 4-bit codes; code
+// byte j holds elements j and j+16). Codes decode four at a time: one prmt
+// maps the low three bits to the magnitudes {0,1,2,3,4,6,8,12}, a second in
+// sign-replicate mode turns each code's sign bit into a byte mask, and the
+// block's exact dot is dp4a(mag, a) - 2*dp4a(mag of the negative codes, a),
+// the activation bytes permuted into the codes' element order. The pair's
+// term t = fma(sc_e, p_e, sc_o*p_o) (sc = fp16(y.d) * e8m0/2) needs both
+// blocks: the partner lane (lane ^ xm) sends its block's dot and scale, both
+// lanes add t to the row's chain in pair order.
+__device__ __forceinline__ float mxfp4_row2(const uint8_t * row, const uint8_t * act, const ActLayout & al, int p,
+                                            int npairs, int xm) {
+    float sumf = 0.0f;
+    for (int u = 0; u < npairs; ++u) {
+        const int b = 2 * u + p;
+        const uint8_t * bp = row + 17 * b;
+        const uint8_t * wb = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(bp) & ~(uintptr_t)3);
+        const uint32_t sh = (uint32_t)(reinterpret_cast<uintptr_t>(bp) & 3) * 8u;
+        uint32_t w[5];
+#pragma unroll
+        for (int k = 0; k < 5; ++k) w[k] = lds32(wb + 4 * k);
+        const uint32_t e = __funnelshift_rc(w[0], w[1], sh) & 0xffu;
+        const uint4 a0 = lds128(act + 32 * b), a1 = lds128(act + 32 * b + 16);
+        const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        int pp = 0, pn = 0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t q = __funnelshift_rc(w[t], w[t + 1], sh + 8u);   // code bytes 4t..4t+3
+            // activation bytes in the codes' order: (4t, 16+4t, 4t+1, 16+4t+1), (4t+2, 16+4t+2, 4t+3, 16+4t+3)
+            const uint32_t x0 = __byte_perm(aw[t], aw[4 + t], 0x5140u), x1 = __byte_perm(aw[t], aw[4 + t], 0x7362u);
+            const uint32_t s0 = q & 0xffffu, s1 = q >> 16;
+            const uint32_t m0 = prmt_sx(0x03020100u, 0x0c080604u, s0 & 0x7777u);
+            const uint32_t m1 = prmt_sx(0x03020100u, 0x0c080604u, s1 & 0x7777u);
+            const uint32_t n0 = m0 & (prmt_sx(0x80808080u, 0x80808080u, s0) ^ 0x80808080u);
+            const uint32_t n1 = m1 & (prmt_sx(0x80808080u, 0x80808080u, s1) ^ 0x80808080u);
+            pp = dp4a(m0, x0, pp);
+            pn = dp4a(n0, x0, pn);
+            pp = dp4a(m1, x1, pp);
+            pn = dp4a(n1, x1, pn);
+        }
+        const int pb = pp - 2 * pn;
+        const uint32_t dw = lds32(act + al.d_off + 4 * (b >> 1));
+        const float sc = __fmul_rn(h2f((uint16_t)((dw >> (16 * (b & 1))) & 0xffffu)), e8m0_half(e));
+        const int po = __shfl_xor_sync(0xffffffffu, pb, xm);
+        const float so = __shfl_xor_sync(0xffffffffu, sc, xm);
+        const int pe_ = p ? po : pb, po_ = p ? pb : po;
+        const float sce = p ? so : sc, sco = p ? sc : so;
+        sumf = __fadd_rn(sumf, __fmaf_rn(sce, (float)pe_, __fmul_rn(sco, (float)po_)));
+    }
+    return sumf;
+}
+
 // Superblocks whose integer parts a lane computes before their exchanges and
 // float chain (Q4_K rows), and whether Q6_K rows go by superblock pairs.
 constexpr int kQ4kGroup = 1;
@@ -696,7 +757,10 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
 template <int TG, int TD>
 __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWarps, 1) k_stack(const __grid_constant__ StackParams p) {
     // row mode: 0 two-lane Q8_0 rows, 2 two-lane Q4_K gate/up + Q6_K down rows, 1 octet rows
-    constexpr int kMode = (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0 : (TG == GX_T_Q4_K && TD == GX_T_Q6_K) ? 2 : 1;
+    constexpr int kMode = (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0
+                          : (TG == GX_T_Q4_K && TD == GX_T_Q6_K) ? 2
+                          : (TG == GX_T_MXFP4 && TD == GX_T_MXFP4) ? 3
+                                                                  : 1;
     constexpr int VG = Oct<TG>::VDT, VD = Oct<TD>::VDT;       // activation types of gate/up and down
     // warps per job (p.split): octet jobs are compute-bound and two warps
     // share each (passes split between them); so do the 32-row down jobs of
@@ -768,7 +832,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
         q.k = p.k;
         q.Rg = p.Rg;
         q.Rd = p.Rd;
-        q.gu_copies = kMode == 1 ? 2 : 4;
+        q.gu_copies = (kMode == 1 || kMode == 3) ? 2 : 4;
         for (int t = 0; t < 4; ++t) q.tile[t] = p.gu_tile[t];
         const int stage_bytes = p.stage_bytes;
         StackWalk walk{0, 0};
@@ -899,7 +963,34 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
         int * done = bufdone + (J.gu ? 0 : kStackBufs) + bi;
         if (J.gu) {
             const uint8_t * xa = xbuf + bi * xbytes;
-            if constexpr (kMode != 1) {
+            if constexpr (kMode == 3) {
+                // lane = 2r + gp: row r (gate rows 0-7 of tile 0, up rows 0-7 of tile 1), lane half gp
+                const int r = lane >> 1, gp = lane & 1;
+                const uint8_t * row = st + (r < 8 ? p.gu_tile[0] + r * (int)p.nb01_g : p.gu_tile[1] + (r - 8) * (int)p.nb01_g);
+                float dot = 0.0f;
+                if (sub == 0) dot = mxfp4_row2(row, xa, p.alx, gp, p.H / 64, 1);
+                __syncwarp();
+                if (lane == 0) {
+                    // the job's last part frees the stage and the input buffer
+                    __threadfence_block();
+                    if (split == 1 || atomicAdd(parts + cs, 1) == split - 1) {
+                        if (split > 1) {
+                            parts[cs] = 0;
+                            __threadfence_block();
+                        }
+                        atomicAdd(done, 1);
+                        atomicAdd(rel + cs, 1);
+                        mbar_arrive(empty + cs);
+                    }
+                }
+                if (sub != 0) continue;   // a whole gate/up job's second part only counts itself
+                // gate row i (lane 2i) pairs with up row i (lane 2i + 16)
+                const float up = __shfl_down_sync(0xffffffffu, dot, 16);
+                if (gp == 0 && r < 8) {
+                    const float a = p.act == 1 ? act_swiglu_oai(dot, up, p.alpha, p.limit) : act_swiglu(dot, up);
+                    ly.act[(int64_t)J.pair * p.I + J.r0 + r] = a;
+                }
+            } else if constexpr (kMode != 1) {
                 // lane = qr*8 + tile*2 + gp: row qr of tile `tile` (gate rows 4*tile+qr
                 // for tiles 0, 1; up rows 4*(tile-2)+qr for tiles 2, 3), lane half gp
                 const int qr = lane >> 3, tl = (lane >> 1) & 3, gp = lane & 1;
@@ -1048,7 +1139,12 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                     const int R = q + 16 * sub;
                     const uint8_t * ar = da + (R / p.Rd) * p.ald.pitch;
                     float dd, unused;
-                    q6k_rows2<1>(st + R * p.pitch_d, st, ar, ar, p.ald, par, p.I / 256, 16, dd, unused);
+                    if constexpr (kMode == 3) {
+                        dd = mxfp4_row2(st + R * p.pitch_d, ar, p.ald, par, p.I / 64, 16);
+                        unused = 0.0f;
+                    } else {
+                        q6k_rows2<1>(st + R * p.pitch_d, st, ar, ar, p.ald, par, p.I / 256, 16, dd, unused);
+                    }
                     float * dts = sdots + cs * 32;
                     if (par == 0) dts[R] = dd;
                     __syncwarp();
