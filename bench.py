@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--prefill", type=int, default=512, help="prefill tokens at full residency (0 to skip)")
     ap.add_argument("--cpu-sample-layers", type=int, default=3)
     ap.add_argument("--layers", type=int, default=0, help="fewer layers (small profiling cases only)")
+    ap.add_argument("--experts", type=int, default=0,
+                    help="fewer experts per layer (small profiling cases only: keeps the resident arena small "
+                         "while each token still touches top-k experts per layer)")
     ap.add_argument("--ep", action="store_true",
                     help="expert-parallel decode over the N GPUs of the launch (one line; not the headline)")
     ap.add_argument("--ep-tokens", type=int, default=1, help="decode tokens per GPU per step in --ep mode")
@@ -171,6 +174,16 @@ def cpu_baseline(model, tier, routes, xs, n_layers: int, n_tokens: int = 1):
     return {"value": 1.0 / per_token, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
             "sample": f"{n_tokens} decode token(s) x {n_layers} of {model.layers} layers of the same workload "
                       f"(oracle moe_layer, {os.cpu_count()} threads), extrapolated to the full stack"}
+
+
+def shaped_model(gx, args):
+    """The model of --model, with --layers / --experts applied (profiling cases)."""
+    model = gx.MODELS[args.model]
+    if args.layers:
+        model = model.with_layers(args.layers)
+    if args.experts:
+        model = model.with_experts(args.experts)
+    return model
 
 
 def record_of(model, tier, L, e):
@@ -325,9 +338,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     gx.check(gx.lib().gx_device_init(local))
-    model = gx.MODELS[args.model]
-    if args.layers:
-        model = model.with_layers(args.layers)
+    model = shaped_model(gx, args)
     E, k, H, I, NL = model.experts, model.used, model.hidden, model.intermediate, model.layers
     stream = torch.cuda.Stream(device=dev)
 

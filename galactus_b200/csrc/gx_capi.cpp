@@ -1044,7 +1044,9 @@ namespace {
 // warps (default 8).
 bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
     if (sp.k <= 0 || 32 % sp.k != 0) return false;
-    sp.Rg = 8;
+    // MXFP4 gate/up jobs hold 16 gate + 16 up rows (the stage is sized by the
+    // 32-row down job anyway), computed by two warps of 8 + 8 rows each
+    sp.Rg = sp.row_mode == 3 ? 16 : 8;
     int cap = gx::kStackMaxConsumers;
     if (const char * env = std::getenv("GX_STACK_STAGES")) {
         const int v = std::atoi(env);

@@ -749,7 +749,9 @@ static bool stack_copy_mode(int64_t nb01, int R, int32_t & row_copy, int32_t & p
 // gate/up tiles and rows of K % 256 == 0), 1 octet rows (any whole number
 // of their type's 64- or 256-element units, checked per layer; 2 gate/up copies).
 uint32_t stack_layout(StackParams & p, int & threads) {
-    if (p.Rg != 8 || p.Rd < 1 || (p.k * p.Rd != 32 && !(p.row_mode == 2 && p.k * p.Rd == 16))) return 0;
+    if (!(p.Rg == 8 || (p.Rg == 16 && p.row_mode == 3)) || p.Rd < 1 ||
+        (p.k * p.Rd != 32 && !(p.row_mode == 2 && p.k * p.Rd == 16)))
+        return 0;
     const bool tiles8 = p.row_mode == 1 || p.row_mode == 3;   // gate/up as 2 copies of 8 rows
     if (p.row_mode < 0 || p.row_mode > 3 || p.gu_copies != (tiles8 ? 2 : 4)) return 0;
     const int ra = tiles8 ? 64 : 256;
@@ -785,8 +787,8 @@ uint32_t stack_layout(StackParams & p, int & threads) {
         }
         gw = (uint64_t)p.gu_tile[3] + 4ull * (uint64_t)p.nb01_g;
     } else {
-        // octet rows: the 8 gate rows, then the 8 up rows, one copy each
-        const uint64_t tile = 8ull * (uint64_t)p.nb01_g;
+        // octet and MXFP4 rows: the Rg gate rows, then the Rg up rows, one copy each
+        const uint64_t tile = (uint64_t)p.Rg * (uint64_t)p.nb01_g;
         if (tile % 16 != 0) return 0;
         p.gu_tile[0] = 0;
         p.gu_tile[1] = (int32_t)tile;

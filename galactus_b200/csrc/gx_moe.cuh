@@ -21,8 +21,14 @@
 
 namespace gx {
 
-// quantize block ib of an f32 row into the split layout, one warp
-template <int VDT, bool COHERENT>
+// position of element e of a 32-element Q8_0 block in "code order", the byte
+// order of an MXFP4 block's codes (code byte j holds elements j and j+16):
+// word t of the block holds elements 4(t/2) + 2(t%2) + {0, 16, 1, 17}
+__device__ __forceinline__ int mxfp4_code_pos(int e) { return 8 * ((e & 15) >> 2) + 2 * (e & 3) + (e >> 4); }
+
+// quantize block ib of an f32 row into the split layout, one warp; PERM
+// stores a Q8_0 block's quants in code order (same values and scale)
+template <int VDT, bool COHERENT, bool PERM = false>
 __device__ __forceinline__ void quant_block_split(const float * x, uint8_t * row, const ActLayout & L, int ib, int lane) {
     if (VDT == GX_T_Q8_0) {
         const float v = COHERENT ? __ldcg(x + 32 * ib + lane) : __ldg(x + 32 * ib + lane);
@@ -31,7 +37,7 @@ __device__ __forceinline__ void quant_block_split(const float * x, uint8_t * row
         for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
         const float d = __fdiv_rn(a, 127.0f);
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        row[32 * ib + lane] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v, id));
+        row[32 * ib + (PERM ? mxfp4_code_pos(lane) : lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v, id));
         if (lane == 0) *reinterpret_cast<uint16_t *>(row + L.d_off + 2 * ib) = f2h(d);
     } else {
         float v[8];

@@ -42,15 +42,15 @@ SlotPolicy::SlotPolicy(uint32_t first_layer, uint32_t last_layer, uint32_t exper
     for (uint64_t r : record_bytes)
         if (r == 0 || r % kRecordAlign != 0) throw PolicyError(GX_ERR_INVALID, "profile: record not a multiple of 16 KiB");
     if (policy < GX_POLICY_AUTO || policy > GX_POLICY_LRU) throw PolicyError(GX_ERR_INVALID, "unknown policy");
-    if (capacity_bytes == 0) throw PolicyError(GX_ERR_INVALID, "capacity must be positive");
+    if (capacity_bytes == 0) throw PolicyError(GX_ERR_INVALID, "policy: zero-byte arena");
     lru_ = policy == GX_POLICY_LRU;
     if (!lru_ && (protected_fraction <= 0.0 || protected_fraction >= 1.0))
-        throw PolicyError(GX_ERR_INVALID, "protected fraction must be in (0,1)");
+        throw PolicyError(GX_ERR_INVALID, "policy: protected share outside the open unit interval");
 
     uint64_t one_of_each = 0;
     for (uint64_t r : record_bytes) one_of_each += r;
     uint64_t q = capacity_bytes / one_of_each;
-    if (q == 0) throw PolicyError(GX_ERR_INVALID, "capacity below one expert per layer");
+    if (q == 0) throw PolicyError(GX_ERR_INVALID, "policy: arena smaller than one record per layer");
     if (q > experts) q = experts;
     quota_ = static_cast<uint32_t>(q);
     if (quota_ < 2) throw PolicyError(GX_ERR_INVALID, "quota below 2 slots per layer");

@@ -285,8 +285,8 @@ __device__ __forceinline__ void stack_issue_weights(const StackCopy & q, const S
             if (lane < 4)
                 tma_load(stage + q.tile[lane], (lane < 2 ? ly.wg : ly.wu) + off + (int64_t)(lane & 1) * tile, tile, bar);
         } else {
-            // gate rows r0..r0+7, then up rows r0..r0+7
-            const uint32_t tile = (uint32_t)(8 * q.nb01_g);
+            // gate rows r0..r0+Rg-1, then up rows r0..r0+Rg-1
+            const uint32_t tile = (uint32_t)(q.Rg * q.nb01_g);
             if (lane == 0) tma_expect(bar, 2u * tile);
             __syncwarp();
             if (lane < 2) tma_load(stage + q.tile[lane], (lane == 0 ? ly.wg : ly.wu) + off, tile, bar);
@@ -334,55 +334,67 @@ __device__ __forceinline__ uint32_t prmt_sx(uint32_t a, uint32_t b, uint32_t c) 
     return d;
 }
 
-// MXFP4 row x Q8_0 activation row (split layout), two lanes per row
-// (ggml_vec_dot_mxfp4_q8_0, diff:1167-1174, 1209-1240). Lane p takes block
-// 2u+p of every pair u (17 bytes: e8m0 scale, 16 bytes of 4-bit codes; code
-// byte j holds elements j and j+16). Codes decode four at a time: one prmt
-// maps the low three bits to the magnitudes {0,1,2,3,4,6,8,12}, a second in
-// sign-replicate mode turns each code's sign bit into a byte mask, and the
-// block's exact dot is dp4a(mag, a) - 2*dp4a(mag of the negative codes, a),
-// the activation bytes permuted into the codes' element order. The pair's
-// term t = fma(sc_e, p_e, sc_o*p_o) (sc = fp16(y.d) * e8m0/2) needs both
-// blocks: the partner lane (lane ^ xm) sends its block's dot and scale, both
-// lanes add t to the row's chain in pair order.
+// e2m1 magnitudes of codes 0..7, doubled (0, 0.5, 1, 1.5, 2, 3, 4, 6 -> 0..12):
+// bytes 0-3 and 4-7 of the prmt source pair
+constexpr uint32_t kE2m1Lo = 0x03020100u, kE2m1Hi = 0x0c080604u;
+
+// Exact dot of one MXFP4 block (16 code bytes at w >> sh + 8 bits; code byte j
+// holds elements j and j+16) with its Q8_0 activation block stored in code
+// order (quant_block_split<..., PERM>: word 2t = elements 4t, 4t+16, 4t+1,
+// 4t+17, word 2t+1 = 4t+2, 4t+18, 4t+3, 4t+19). prmt in its default mode
+// takes a selector nibble's low three bits as the byte index and its high bit
+// as "replace the byte by copies of its sign bit"; the table bytes are
+// non-negative, so prmt(table, q) gives the magnitudes of the positive codes
+// and zero for the negative ones, and prmt(table, q ^ 0x8888...) the
+// reverse. dot = dp4a(positive mags, a) - dp4a(negative mags, a), exact.
+__device__ __forceinline__ int mxfp4_block_dot(const uint32_t (&w)[5], uint32_t sh, const uint4 & a0, const uint4 & a1) {
+    const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    int pp0 = 0, pp1 = 0, pn0 = 0, pn1 = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const uint32_t q = __funnelshift_rc(w[t], w[t + 1], sh + 8u);
+        const uint32_t qx = q ^ 0x88888888u;
+        pp0 = dp4a(prmt_sx(kE2m1Lo, kE2m1Hi, q), aw[2 * t], pp0);
+        pn0 = dp4a(prmt_sx(kE2m1Lo, kE2m1Hi, qx), aw[2 * t], pn0);
+        pp1 = dp4a(prmt_sx(kE2m1Lo, kE2m1Hi, q >> 16), aw[2 * t + 1], pp1);
+        pn1 = dp4a(prmt_sx(kE2m1Lo, kE2m1Hi, qx >> 16), aw[2 * t + 1], pn1);
+    }
+    return (pp0 + pp1) - (pn0 + pn1);
+}
+
+// MXFP4 row x Q8_0 activation row (split layout, blocks in code order), two
+// lanes per row (ggml_vec_dot_mxfp4_q8_0, diff:1167-1174, 1209-1240). Lane p
+// takes block 2u+p of every pair u (17 bytes: e8m0 scale, 16 code bytes),
+// read as five aligned words at a byte offset that alternates between two
+// values along the row. The pair's term t = fma(sc_e, p_e, sc_o*p_o), with
+// sc = fp16(y.d) * e8m0/2: the odd lane sends sc_o*p_o to its partner
+// (lane ^ xm), the even lane forms t and adds it to the row's chain in pair
+// order. The row's dot is valid on the even-block lane (p == 0) only.
 __device__ __forceinline__ float mxfp4_row2(const uint8_t * row, const uint8_t * act, const ActLayout & al, int p,
                                             int npairs, int xm) {
     float sumf = 0.0f;
+    const uintptr_t rb = reinterpret_cast<uintptr_t>(row) + 17u * (uint32_t)p;
+    const uint8_t * wbase = reinterpret_cast<const uint8_t *>(rb & ~(uintptr_t)3);
+    const uint32_t off = (uint32_t)(rb & 3);            // block of pair u at wbase + off + 34u
+    const uint8_t * aq = act + 32 * p;                  // activation block 2u+p at aq + 64u
+    const uint8_t * ad = act + al.d_off;                // fp16 scales of pair u in word u
+    const uint32_t dsh = 16u * (uint32_t)p;
+#pragma unroll 2
     for (int u = 0; u < npairs; ++u) {
-        const int b = 2 * u + p;
-        const uint8_t * bp = row + 17 * b;
-        const uint8_t * wb = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(bp) & ~(uintptr_t)3);
-        const uint32_t sh = (uint32_t)(reinterpret_cast<uintptr_t>(bp) & 3) * 8u;
+        const uint32_t B = off + 34u * (uint32_t)u;
+        const uint8_t * wp = wbase + (B & ~3u);
+        const uint32_t sh = (B & 3u) * 8u;
         uint32_t w[5];
 #pragma unroll
-        for (int k = 0; k < 5; ++k) w[k] = lds32(wb + 4 * k);
-        const uint32_t e = __funnelshift_rc(w[0], w[1], sh) & 0xffu;
-        const uint4 a0 = lds128(act + 32 * b), a1 = lds128(act + 32 * b + 16);
-        const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        int pp = 0, pn = 0;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const uint32_t q = __funnelshift_rc(w[t], w[t + 1], sh + 8u);   // code bytes 4t..4t+3
-            // activation bytes in the codes' order: (4t, 16+4t, 4t+1, 16+4t+1), (4t+2, 16+4t+2, 4t+3, 16+4t+3)
-            const uint32_t x0 = __byte_perm(aw[t], aw[4 + t], 0x5140u), x1 = __byte_perm(aw[t], aw[4 + t], 0x7362u);
-            const uint32_t s0 = q & 0xffffu, s1 = q >> 16;
-            const uint32_t m0 = prmt_sx(0x03020100u, 0x0c080604u, s0 & 0x7777u);
-            const uint32_t m1 = prmt_sx(0x03020100u, 0x0c080604u, s1 & 0x7777u);
-            const uint32_t n0 = m0 & (prmt_sx(0x80808080u, 0x80808080u, s0) ^ 0x80808080u);
-            const uint32_t n1 = m1 & (prmt_sx(0x80808080u, 0x80808080u, s1) ^ 0x80808080u);
-            pp = dp4a(m0, x0, pp);
-            pn = dp4a(n0, x0, pn);
-            pp = dp4a(m1, x1, pp);
-            pn = dp4a(n1, x1, pn);
-        }
-        const int pb = pp - 2 * pn;
-        const uint32_t dw = lds32(act + al.d_off + 4 * (b >> 1));
-        const float sc = __fmul_rn(h2f((uint16_t)((dw >> (16 * (b & 1))) & 0xffffu)), e8m0_half(e));
-        const int po = __shfl_xor_sync(0xffffffffu, pb, xm);
-        const float so = __shfl_xor_sync(0xffffffffu, sc, xm);
-        const int pe_ = p ? po : pb, po_ = p ? pb : po;
-        const float sce = p ? so : sc, sco = p ? sc : so;
-        sumf = __fadd_rn(sumf, __fmaf_rn(sce, (float)pe_, __fmul_rn(sco, (float)po_)));
+        for (int i = 0; i < 5; ++i) w[i] = lds32(wp + 4 * i);
+        const uint4 a0 = lds128(aq + 64 * u), a1 = lds128(aq + 64 * u + 16);
+        const uint32_t dw = lds32(ad + 4 * u);
+        const int pb = mxfp4_block_dot(w, sh, a0, a1);
+        const uint32_t e = (w[0] >> sh) & 0xffu;
+        const float sc = __fmul_rn(h2f((uint16_t)((dw >> dsh) & 0xffffu)), e8m0_half(e));
+        const float z = (float)pb;
+        const float yo = __shfl_xor_sync(0xffffffffu, __fmul_rn(sc, z), xm);
+        sumf = __fadd_rn(sumf, __fmaf_rn(sc, z, yo));
     }
     return sumf;
 }
@@ -894,7 +906,8 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
             const StackLayer & ly = p.layers[L];
             for (int wi = c; wi < p.T * nblk; wi += W) {
                 const int t = wi / nblk, ib = wi - t * nblk;
-                quant_block_split<VG, false>(ly.x + (int64_t)t * p.H, ly.xq + (int64_t)t * p.alx.pitch, p.alx, ib, lane);
+                quant_block_split<VG, false, kMode == 3>(ly.x + (int64_t)t * p.H, ly.xq + (int64_t)t * p.alx.pitch, p.alx,
+                                                         ib, lane);
             }
             any = true;
         }
@@ -930,7 +943,8 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
             ok = n == 0;
             for (uint32_t i = 0; i < (1u << 23) && !ok; ++i) {
                 ok = *reinterpret_cast<volatile int *>(rel + cs) >= n;
-                if (!ok && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+                if (!ok && (i & 63u) == 63u && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+                if (!ok && i >= 16) __nanosleep(32);
             }
         }
         ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
@@ -946,7 +960,8 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                 const int v = *fw;
                 got = (v >> 1) == key;
                 fpar = v & 1;
-                if (!got && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+                if (!got && (i & 63u) == 63u && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+                if (!got && i >= 16) __nanosleep(32);
             }
             ok = got;
         }
@@ -964,31 +979,29 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
         if (J.gu) {
             const uint8_t * xa = xbuf + bi * xbytes;
             if constexpr (kMode == 3) {
-                // lane = 2r + gp: row r (gate rows 0-7 of tile 0, up rows 0-7 of tile 1), lane half gp
+                // part `sub` of a 16+16-row job: lane = 2r + gp, row r < 8 is gate
+                // row 8*sub + r (tile 0), row r >= 8 is up row 8*sub + r - 8 (tile 1)
                 const int r = lane >> 1, gp = lane & 1;
-                const uint8_t * row = st + (r < 8 ? p.gu_tile[0] + r * (int)p.nb01_g : p.gu_tile[1] + (r - 8) * (int)p.nb01_g);
-                float dot = 0.0f;
-                if (sub == 0) dot = mxfp4_row2(row, xa, p.alx, gp, p.H / 64, 1);
+                const int gr = 8 * sub + (r & 7);
+                const uint8_t * row = st + p.gu_tile[r >> 3] + gr * (int)p.nb01_g;
+                const float dot = mxfp4_row2(row, xa, p.alx, gp, p.H / 64, 1);
                 __syncwarp();
                 if (lane == 0) {
                     // the job's last part frees the stage and the input buffer
                     __threadfence_block();
-                    if (split == 1 || atomicAdd(parts + cs, 1) == split - 1) {
-                        if (split > 1) {
-                            parts[cs] = 0;
-                            __threadfence_block();
-                        }
+                    if (atomicAdd(parts + cs, 1) == split - 1) {
+                        parts[cs] = 0;
+                        __threadfence_block();
                         atomicAdd(done, 1);
                         atomicAdd(rel + cs, 1);
                         mbar_arrive(empty + cs);
                     }
                 }
-                if (sub != 0) continue;   // a whole gate/up job's second part only counts itself
-                // gate row i (lane 2i) pairs with up row i (lane 2i + 16)
+                // gate row gr (lane 2r, r < 8) pairs with up row gr (lane 2r + 16)
                 const float up = __shfl_down_sync(0xffffffffu, dot, 16);
                 if (gp == 0 && r < 8) {
                     const float a = p.act == 1 ? act_swiglu_oai(dot, up, p.alpha, p.limit) : act_swiglu(dot, up);
-                    ly.act[(int64_t)J.pair * p.I + J.r0 + r] = a;
+                    ly.act[(int64_t)J.pair * p.I + J.r0 + gr] = a;
                 }
             } else if constexpr (kMode != 1) {
                 // lane = qr*8 + tile*2 + gp: row qr of tile `tile` (gate rows 4*tile+qr
@@ -1063,14 +1076,15 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
             int last = 0;
             if (lane == 0) {
                 fence_acq_rel_gpu();
-                last = atomicAdd(ly.cnt + J.pair * nblk + blk, 1) == (kMode == 1 ? split : 1) * (p.qblk / p.Rg) - 1;
+                last = atomicAdd(ly.cnt + J.pair * nblk + blk, 1) ==
+                       (kMode == 1 || kMode == 3 ? split : 1) * (p.qblk / p.Rg) - 1;
             }
             if (__shfl_sync(0xffffffffu, last, 0)) {
                 // this job finished the Q8 block last: quantize it and count the
                 // block into its token (the down inputs wait for k*I/qblk blocks)
                 fence_acq_rel_gpu();
-                quant_block_split<VD, true>(ly.act + (int64_t)J.pair * p.I, ly.actq + (int64_t)J.pair * p.ald.pitch,
-                                            p.ald, blk, lane);
+                quant_block_split<VD, true, kMode == 3>(ly.act + (int64_t)J.pair * p.I,
+                                                         ly.actq + (int64_t)J.pair * p.ald.pitch, p.ald, blk, lane);
                 fence_proxy_async_global();
                 __syncwarp();
                 if (lane == 0) {

@@ -64,6 +64,9 @@ class ModelShape:
     def with_layers(self, layers: int) -> "ModelShape":
         return ModelShape(**{**self.__dict__, "layers": layers})
 
+    def with_experts(self, experts: int) -> "ModelShape":
+        return ModelShape(**{**self.__dict__, "experts": experts})
+
 
 MODELS = {
     # OLMoE-1B-7B: Q4_K gate/up, Q6_K down, SwiGLU

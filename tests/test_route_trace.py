@@ -1,7 +1,7 @@
 """Route traces: the observer records every served micro-batch in the
 reference's "galactus.route-observer.v1" format; the reference's own replay
-tool (scripts/replay-cache.py --verify, when the reference tree is present
-here) reads our trace and finds its replayed SLRU in agreement with every
+tool (scripts/replay-cache.py --verify, run when GALACTUS_REFERENCE_DIR names
+the reference tree) reads our trace and finds its replayed SLRU in agreement with every
 residency bit and every byte."""
 import os
 import subprocess
@@ -11,7 +11,8 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-REPLAY = Path("/root/reference/scripts/replay-cache.py")
+_REF = os.environ.get("GALACTUS_REFERENCE_DIR", "")
+REPLAY = Path(_REF) / "scripts" / "replay-cache.py" if _REF else None
 
 
 def _zipf_batches(rng, n_steps, layers, experts, k):
@@ -65,7 +66,7 @@ def test_trace_cap_truncates(gxlib, tmp_path):
     assert tr["n_entries"] == 5 and tr["truncated"]
 
 
-@pytest.mark.skipif(not REPLAY.exists(), reason="reference replay tool not present here")
+@pytest.mark.skipif(REPLAY is None or not REPLAY.exists(), reason="GALACTUS_REFERENCE_DIR unset or without the replay tool")
 def test_reference_replay_verifies_our_trace(gxlib, tmp_path):
     """The reference's replay-cache.py --verify replays its SLRU baseline over
     our trace: every recorded residency bit and the recorded bytes agree (the
