@@ -93,6 +93,10 @@ class gx_layer_desc(C.Structure):
                 ("off_gate", C.c_uint64), ("off_up", C.c_uint64)]
 
 
+class gx_shared_expert(C.Structure):
+    _fields_ = [("record", C.c_void_p), ("desc", gx_layer_desc)]
+
+
 _P = C.c_void_p
 _I64 = C.c_int64
 _SIGS = {
@@ -131,6 +135,8 @@ _SIGS = {
     "gx_expf": (C.c_int, [_P, _P, _I64, _P]),
     "gx_moe_layer_forward": (C.c_int, [_P, C.c_uint32, C.POINTER(gx_layer_desc), _P, _P, _P, _I64, _I64, _P, _P,
                                        C.POINTER(gx_serve_stats)]),
+    "gx_moe_layer_forward_shared": (C.c_int, [_P, C.c_uint32, C.POINTER(gx_layer_desc), _P, _P, _P, _I64, _I64,
+                                             C.POINTER(gx_shared_expert), _P, _P, C.POINTER(gx_serve_stats)]),
     "gx_moe_stack_forward": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.POINTER(gx_layer_desc), C.POINTER(_P), _P,
                                        C.POINTER(_P), _I64, _I64, C.POINTER(_P), _P, C.POINTER(gx_serve_stats)]),
     "gx_stack_plan_create": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.POINTER(gx_layer_desc), C.POINTER(_P),
@@ -163,6 +169,8 @@ _SIGS = {
     "gx_ep_combine": (C.c_int, [_P, _P, _P, _P]),
     "gx_ep_layer_forward": (C.c_int, [_P, C.c_uint32, C.POINTER(gx_layer_desc), _P, _P, _P, _I64, _I64, _P, _P,
                                       C.POINTER(gx_serve_stats)]),
+    "gx_ep_stack_forward": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.POINTER(gx_layer_desc), C.POINTER(_P), _P,
+                                     C.POINTER(_P), _I64, _I64, C.POINTER(_P), _P, C.POINTER(gx_serve_stats)]),
     "gx_moe_ffn_noalloc": (C.c_int, [C.POINTER(gx_layer_desc), _P, C.c_uint64, C.c_uint32, _P, _P, _P, _I64, _I64,
                                      _P, _P]),
     "gx_synth_normal": (C.c_int, [_P, _I64, C.c_uint64, C.c_uint64, C.c_float, _P]),

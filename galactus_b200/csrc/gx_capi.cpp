@@ -176,6 +176,17 @@ struct gx_arena {
     uint8_t * d_xq = nullptr;           // quantized layer inputs, split layout, one row per token
     uint8_t * d_actq = nullptr;         // quantized activations of the down projection, one row per (token, slot)
     int32_t * d_cnt = nullptr;          // per (token, slot, Q8 block) completion counters, zero between calls
+    // wave schedule (micro-batches whose distinct experts exceed the policy's
+    // batch bound): per-pair inputs and outputs in wave order, outputs in pair
+    // order, unit weights, gather/scatter indices (allocated on first use)
+    float * d_wx = nullptr;             // [pairs, H] input row of each pair, wave order
+    float * d_wy = nullptr;             // [pairs, H] down output of each pair, wave order
+    float * d_wfull = nullptr;          // [pairs, H] the same in (token, slot) order
+    float * d_ones = nullptr;           // [pairs] 1.0f
+    float * d_shy = nullptr;            // [max_tokens, H] shared-expert output
+    int32_t * d_widx = nullptr;         // [2, pairs] token of each wave-order pair | its pair index
+    int32_t * h_widx = nullptr;         // pinned staging of d_widx
+    cudaEvent_t ev_widx = nullptr;
     // expert-grouped (prefill) path: per-pair outputs and the pair grouping
     float * d_y = nullptr;              // [pairs, H] down output of each (token, slot)
     int32_t * h_grp = nullptr;          // pinned staging of the grouping arrays
@@ -313,6 +324,15 @@ int gx_arena_destroy(gx_arena * a) {
     if (a->d_actq) cudaFree(a->d_actq);
     if (a->d_cnt) cudaFree(a->d_cnt);
     if (a->d_y) cudaFree(a->d_y);
+    if (a->ev_widx) cudaEventSynchronize(a->ev_widx);
+    if (a->d_wx) cudaFree(a->d_wx);
+    if (a->d_wy) cudaFree(a->d_wy);
+    if (a->d_wfull) cudaFree(a->d_wfull);
+    if (a->d_shy) cudaFree(a->d_shy);
+    if (a->d_ones) cudaFree(a->d_ones);
+    if (a->d_widx) cudaFree(a->d_widx);
+    if (a->h_widx) cudaFreeHost(a->h_widx);
+    if (a->ev_widx) cudaEventDestroy(a->ev_widx);
     if (a->d_grp) cudaFree(a->d_grp);
     if (a->h_grp) cudaFreeHost(a->h_grp);
     if (a->ev_grp) cudaEventDestroy(a->ev_grp);
@@ -798,6 +818,108 @@ int plan_layer(gx_arena * a, uint32_t layer, const gx_layer_desc * d, int64_t k,
     return GX_OK;
 }
 
+// The layer plan of a shared expert: the routed plan's kernels on the
+// caller's resident record (one "slot", index 0), k = 1, the arena's scratch.
+int plan_shared(gx_arena * a, uint32_t layer, const gx_shared_expert * sh, int64_t T, LayerPlan & lp) {
+    const gx_layer_desc & d = sh->desc;
+    if (sh->record == nullptr) return GX_ERR_INVALID;
+    if (!gx::supported_weight_type(d.type_gate) || !gx::supported_weight_type(d.type_down)) return GX_ERR_TYPE;
+    if (d.type_up != d.type_gate) return GX_ERR_TYPE;
+    if (d.act != GX_ACT_SWIGLU && d.act != GX_ACT_SWIGLU_OAI) return GX_ERR_INVALID;
+    if (T < 1 || T > a->max_tokens || d.hidden != a->hidden || d.intermediate < 1 ||
+        d.intermediate > (int64_t)a->used * a->intermediate)
+        return GX_ERR_INVALID;
+    const int64_t H = d.hidden, I = d.intermediate;
+    if (H % gx::row_align(d.type_gate) != 0 || I % gx::row_align(d.type_down) != 0) return GX_ERR_ALIGN;
+    if (d.off_gate % 16 || d.off_up % 16 || (reinterpret_cast<uintptr_t>(sh->record) & 15u) != 0) return GX_ERR_ALIGN;
+    if ((uint64_t)gx::row_bytes(d.type_down, I) * H > d.off_gate ||
+        d.off_gate + gx::row_bytes(d.type_gate, H) * I > d.off_up)
+        return GX_ERR_INVALID;
+    // the scratch of the routed plan, sized for k*max_tokens pairs of the routed I
+    const int64_t pa_sh = std::max(gx::act_layout(gx::GX_T_Q8_0, (int)I).pitch, gx::act_layout(gx::GX_T_Q8_K, (int)I).pitch);
+    const int64_t pa = std::max(gx::act_layout(gx::GX_T_Q8_0, (int)a->intermediate).pitch,
+                                gx::act_layout(gx::GX_T_Q8_K, (int)a->intermediate).pitch);
+    if (T * pa_sh > (int64_t)a->used * a->max_tokens * pa) return GX_ERR_INVALID;
+    gx_layer_desc rd = d;
+    // plan_layer checks the routed geometry; plan with the shared one by hand
+    lp = LayerPlan{};
+    lp.layer = layer;
+    lp.li = a->L(layer);
+    lp.H = H;
+    lp.I = I;
+    lp.k = 1;
+    lp.T = T;
+    lp.type_gate = rd.type_gate;
+    lp.type_down = rd.type_down;
+    lp.vdt_g = gx::vec_dot_type(rd.type_gate);
+    lp.vdt_d = gx::vec_dot_type(rd.type_down);
+    const uint8_t * base = static_cast<const uint8_t *>(sh->record);
+    gx::DecodeParams & g = lp.g;
+    g = gx::DecodeParams{};
+    g.w0 = base + rd.off_gate;
+    g.w1 = base + rd.off_up;
+    g.nb01 = gx::row_bytes(rd.type_gate, H);
+    g.nb02 = 0;
+    g.ne00 = (int32_t)H;
+    g.ne01 = (int32_t)I;
+    g.n_as = 1;
+    g.k = 1;
+    g.T = (int32_t)T;
+    g.aq = a->d_xq;
+    g.al = gx::act_layout(lp.vdt_g, (int)H);
+    g.a_rows = 1;
+    g.act_f32 = a->d_act;
+    g.act_q = a->d_actq;
+    g.al2 = gx::act_layout(lp.vdt_d, (int)I);
+    g.vdt2 = lp.vdt_d;
+    g.qblk = lp.vdt_d == gx::GX_T_Q8_0 ? 32 : 256;
+    g.counters = a->d_cnt;
+    g.act = rd.act;
+    g.alpha = rd.alpha;
+    g.limit = rd.limit;
+    {
+        static const int cands[] = {8, 16, 4, 2, 1};
+        int threads = 0;
+        g.R = 0;
+        for (int R : cands) {
+            if (I % R || g.qblk % R) continue;
+            gx::DecodeParams t = g;
+            t.R = R;
+            if (gx::decode_layout(1, t, threads) == 0) continue;
+            g.R = R;
+            break;
+        }
+        if (g.R == 0) return GX_ERR_ALIGN;
+        g.n_units = (int32_t)(T * (I / g.R));
+    }
+    gx::DecodeParams & dn = lp.dn;
+    dn = g;
+    dn.w0 = base;
+    dn.w1 = nullptr;
+    dn.nb01 = gx::row_bytes(rd.type_down, I);
+    dn.ne00 = (int32_t)I;
+    dn.ne01 = (int32_t)H;
+    dn.aq = a->d_actq;
+    dn.al = gx::act_layout(lp.vdt_d, (int)I);
+    dn.a_rows = 1;
+    {
+        static const int cands[] = {32, 64, 16, 8, 4, 2};
+        int threads = 0;
+        dn.R = 0;
+        for (int R : cands) {
+            if (H % R) continue;
+            gx::DecodeParams t = dn;
+            t.R = R;
+            if (gx::decode_layout(2, t, threads) == 0) continue;
+            dn.R = R;
+            break;
+        }
+        if (dn.R == 0) return GX_ERR_ALIGN;
+        dn.n_units = (int32_t)(T * (H / dn.R));
+    }
+    return GX_OK;
+}
+
 // Enqueue the three kernels of a planned layer. Slot ids come either inline
 // (n <= kInlineIds) or from a device array [T, k].
 void enqueue_layer(const LayerPlan & lp, const float * x, const float * w, float * out, const int32_t * ids_dev,
@@ -947,6 +1069,9 @@ void prefill_layer(gx_arena * a, const LayerPlan & lp, const float * x, const in
     ck(gx::launch_combine(a->d_y, w, out, H, (int)k, T, s));
 }
 
+int layer_forward_waves(gx_arena * a, const LayerPlan & lp, const gx_layer_desc * d, const float * x,
+                        const int32_t * ids, const float * w, float * out, cudaStream_t s, gx_serve_stats * stats);
+
 int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x, const int32_t * ids,
                          const float * w, int64_t k, int64_t T, float * out, cudaStream_t s, gx_serve_stats * stats) {
     if (x == nullptr || ids == nullptr || w == nullptr || out == nullptr) return GX_ERR_INVALID;
@@ -955,6 +1080,21 @@ int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, 
     int rc = plan_layer(a, layer, d, k, T, lp);
     if (rc != GX_OK) return rc;
     const int64_t n = k * T;
+    {
+        // more distinct experts than the policy serves in one batch: waves
+        const SlotPolicy & P = a->policy->impl;
+        thread_local std::vector<uint8_t> seen;
+        seen.assign(P.experts(), 0);
+        uint32_t distinct = 0;
+        for (int64_t i = 0; i < n; ++i) {
+            if (ids[i] < 0 || (uint32_t)ids[i] >= P.experts()) return GX_ERR_DOMAIN;
+            if (!seen[(size_t)ids[i]]) {
+                seen[(size_t)ids[i]] = 1;
+                ++distinct;
+            }
+        }
+        if (distinct > P.batch_bound(layer)) return layer_forward_waves(a, lp, d, x, ids, w, out, s, stats);
+    }
     int32_t * slots = a->slot_scratch.data();
     gx_serve_stats sst{};
     rc = arena_serve(a, layer, ids, (uint32_t)n, slots, a->last_ev[lp.li], s, &sst, (uint32_t)T, (uint32_t)k);
@@ -999,6 +1139,87 @@ int layer_forward_locked(gx_arena * a, uint32_t layer, const gx_layer_desc * d, 
     enqueue_layer(lp, x, w, out, ids_dev, slots, s, pdl && sst.misses == 0 && ids_dev == nullptr, pdl, tv);
     ck(cudaEventRecord(a->ev_done[lp.li], s));
     a->last_ev[lp.li] = a->ev_done[lp.li];
+    return GX_OK;
+}
+
+// Expert-major waves for a micro-batch whose distinct experts exceed the
+// policy's batch bound min(quota, probation) (the reference bounds its
+// micro-batches by it: src/h4/h4-expert-cache.cpp:105-124). The distinct
+// experts, in order of first appearance, are cut into waves of at most
+// `bound`; the (token, slot) pairs are ordered by wave. Each wave is served
+// and computed as micro-batches of one expert per pair with unit router
+// weight, at most max_tokens pairs each (the result fl(1 * y) = y is the
+// pair's down projection, bit for bit); a later wave's misses may evict a
+// slot of an earlier wave only after the kernels that read it (the copy
+// stream waits for the layer's last kernels). The per-pair outputs go back
+// to (token, slot) order and the combine ((w0*y0 + w1*y1) + ...) runs in
+// slot order: the same bits as the one-shot path, for any wave schedule.
+int layer_forward_waves(gx_arena * a, const LayerPlan & lp, const gx_layer_desc * d, const float * x,
+                        const int32_t * ids, const float * w, float * out, cudaStream_t s, gx_serve_stats * stats) {
+    const SlotPolicy & P = a->policy->impl;
+    const int64_t k = lp.k, T = lp.T, n = k * T, H = lp.H;
+    const uint32_t bound = P.batch_bound(lp.layer);
+    if (bound == 0) return GX_ERR_BATCH;
+    const int64_t cap = (int64_t)a->used * a->max_tokens;   // pairs the scratch holds
+    if (a->d_wx == nullptr) {
+        ck(cudaMalloc(&a->d_wx, (size_t)cap * (size_t)a->hidden * sizeof(float)));
+        ck(cudaMalloc(&a->d_wy, (size_t)cap * (size_t)a->hidden * sizeof(float)));
+        ck(cudaMalloc(&a->d_wfull, (size_t)cap * (size_t)a->hidden * sizeof(float)));
+        ck(cudaMalloc(&a->d_ones, (size_t)cap * sizeof(float)));
+        ck(gx::launch_fill(a->d_ones, cap, 1.0f, s));
+        ck(cudaStreamSynchronize(s));   // the unit weights are read on whatever stream calls next
+        ck(cudaMalloc(&a->d_widx, (size_t)(2 * cap) * sizeof(int32_t)));
+        ck(cudaHostAlloc(&a->h_widx, (size_t)(2 * cap) * sizeof(int32_t), cudaHostAllocDefault));
+        ck(cudaEventCreateWithFlags(&a->ev_widx, cudaEventDisableTiming));
+    }
+    // wave of every distinct expert, in order of first appearance
+    thread_local std::vector<int32_t> wave_of;
+    wave_of.assign(P.experts(), -1);
+    int32_t nd = 0;
+    for (int64_t i = 0; i < n; ++i)
+        if (wave_of[(size_t)ids[i]] < 0) wave_of[(size_t)ids[i]] = nd++ / (int32_t)bound;
+    const int32_t nw = (nd + (int32_t)bound - 1) / (int32_t)bound;
+    // pairs in wave order (stable inside a wave)
+    thread_local std::vector<int32_t> start, order, wids;
+    start.assign((size_t)nw + 1, 0);
+    for (int64_t i = 0; i < n; ++i) ++start[(size_t)wave_of[(size_t)ids[i]] + 1];
+    for (int32_t v = 0; v < nw; ++v) start[(size_t)v + 1] += start[(size_t)v];
+    order.assign((size_t)n, 0);
+    {
+        std::vector<int32_t> fill(start.begin(), start.end() - 1);
+        for (int64_t i = 0; i < n; ++i) order[(size_t)fill[(size_t)wave_of[(size_t)ids[i]]]++] = (int32_t)i;
+    }
+    wids.resize((size_t)n);
+    for (int64_t j = 0; j < n; ++j) wids[(size_t)j] = ids[order[(size_t)j]];
+    // gather the input row of every pair in wave order
+    ck(cudaEventSynchronize(a->ev_widx));   // the previous upload out of h_widx has run
+    for (int64_t j = 0; j < n; ++j) {
+        a->h_widx[j] = order[(size_t)j] / (int32_t)k;
+        a->h_widx[n + j] = order[(size_t)j];
+    }
+    ck(cudaMemcpyAsync(a->d_widx, a->h_widx, (size_t)(2 * n) * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    ck(cudaEventRecord(a->ev_widx, s));
+    ck(gx::launch_move_rows(x, a->d_widx, n, H, a->d_wx, false, s));
+    gx_serve_stats sum{};
+    for (int32_t v = 0; v < nw; ++v) {
+        for (int64_t b = start[(size_t)v]; b < start[(size_t)v + 1]; b += a->max_tokens) {
+            const int64_t m = std::min<int64_t>(a->max_tokens, start[(size_t)v + 1] - b);
+            gx_serve_stats st{};
+            const int rc = layer_forward_locked(a, lp.layer, d, a->d_wx + b * H, wids.data() + b, a->d_ones, 1, m,
+                                                a->d_wy + b * H, s, &st);
+            if (rc != GX_OK) return rc;
+            sum.hits += st.hits;
+            sum.misses += st.misses;
+            sum.evictions += st.evictions;
+            sum.bytes_copied += st.bytes_copied;
+        }
+    }
+    sum.distinct = (uint32_t)nd;
+    ck(gx::launch_move_rows(a->d_wy, a->d_widx + n, n, H, a->d_wfull, true, s));
+    ck(gx::launch_combine(a->d_wfull, w, out, H, (int)k, T, s));
+    ck(cudaEventRecord(a->ev_done[lp.li], s));
+    a->last_ev[lp.li] = a->ev_done[lp.li];
+    if (stats) *stats = sum;
     return GX_OK;
 }
 
@@ -1055,7 +1276,7 @@ bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
     int wenv = 0;
     if (const char * env = std::getenv("GX_STACK_WARPS")) {
         const int v = std::atoi(env);
-        if (v >= 1 && v <= gx::kStackMaxWarps) wenv = v;
+        if (v >= 1 && v <= gx::stack_max_warps(sp.row_mode)) wenv = v;
     }
     // the two-lane K-quant rows prefer 16-row down jobs (smaller stages, more
     // of them in flight) where 2 rows of an expert make whole 16-byte chunks
@@ -1064,9 +1285,10 @@ bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
         sp.Rd = drows / sp.k;
         for (int C = cap; C >= 2; --C) {
             sp.C = C;
-            // one consumer warp per stage (two for split jobs), at least 8
-            const int per_stage = (sp.row_mode == 1 || ((sp.row_mode == 2 || sp.row_mode == 3) && drows == 32)) ? 2 : 1;
-            sp.W = wenv ? wenv : std::min(std::max(8, per_stage * C), gx::kStackMaxWarps);
+            // one consumer warp per stage (two for split jobs, four for MXFP4
+            // jobs), at least 8
+            const int per_stage = sp.row_mode == 3 ? 4 : (sp.row_mode == 1 || (sp.row_mode == 2 && drows == 32)) ? 2 : 1;
+            sp.W = wenv ? wenv : std::min(std::max(8, per_stage * C), gx::stack_max_warps(sp.row_mode));
             smem = gx::stack_layout(sp, threads);
             if (smem != 0) return true;
         }
@@ -1105,7 +1327,7 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     int threads = 0;
     uint32_t smem = 0;
     if (!choose_stack_tiles(sp, threads, smem)) return GX_ERR_ALIGN;
-    sp.split = (sp.row_mode == 1 || ((sp.row_mode == 2 || sp.row_mode == 3) && sp.k * sp.Rd == 32)) ? 2 : 1;
+    sp.split = sp.row_mode == 3 ? 4 : (sp.row_mode == 1 || (sp.row_mode == 2 && sp.k * sp.Rd == 32)) ? 2 : 1;
     sp.n_gu = (int32_t)(p->T * p->k * (l0.I / sp.Rg));
     sp.n_d = (int32_t)(p->T * (l0.H / sp.Rd));
     int per_sm = 0;
@@ -1159,6 +1381,53 @@ int gx_moe_layer_forward(gx_arena * a, uint32_t layer, const gx_layer_desc * d, 
         std::lock_guard<std::mutex> lock(a->mu);
         ck(cudaSetDevice(a->device));
         return layer_forward_locked(a, layer, d, x, ids, w, k, T, out, reinterpret_cast<cudaStream_t>(stream), stats);
+    });
+}
+
+int gx_moe_layer_forward_shared(gx_arena * a, uint32_t layer, const gx_layer_desc * d, const float * x,
+                                const int32_t * ids, const float * w, int64_t k, int64_t T,
+                                const gx_shared_expert * sh, float * out, void * stream, gx_serve_stats * stats) {
+    if (a == nullptr || sh == nullptr || x == nullptr || out == nullptr) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(a->mu);
+        ck(cudaSetDevice(a->device));
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        if (T == 0) return GX_OK;
+        LayerPlan sp;
+        int rc = plan_shared(a, layer, sh, T, sp);
+        if (rc != GX_OK) return rc;
+        // the routed experts, then the shared expert into its own buffer
+        rc = layer_forward_locked(a, layer, d, x, ids, w, k, T, out, s, stats);
+        if (rc != GX_OK) return rc;
+        if (a->d_shy == nullptr) ck(cudaMalloc(&a->d_shy, (size_t)a->max_tokens * (size_t)a->hidden * sizeof(float)));
+        if (a->d_ones == nullptr) {
+            const int64_t cap = (int64_t)a->used * a->max_tokens;
+            ck(cudaMalloc(&a->d_ones, (size_t)cap * sizeof(float)));
+            ck(gx::launch_fill(a->d_ones, cap, 1.0f, s));
+            ck(cudaStreamSynchronize(s));
+        }
+        static const int32_t zeros[gx::kInlineIds] = {};
+        const int32_t * slot0 = zeros;
+        const int32_t * ids_dev = nullptr;
+        if (T > gx::kInlineIds) {
+            // slot ids of more than kInlineIds tokens through the pinned ring
+            const int st = a->stage_next;
+            a->stage_next = (st + 1) % kStageRing;
+            const int64_t stride = (int64_t)a->used * a->max_tokens;
+            ck(cudaEventSynchronize(a->ev_stage[st]));
+            int32_t * h = a->h_ids + (size_t)st * stride;
+            int32_t * dd = a->d_ids + (size_t)st * stride;
+            std::memset(h, 0, (size_t)T * sizeof(int32_t));
+            ck(cudaMemcpyAsync(dd, h, (size_t)T * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+            ck(cudaEventRecord(a->ev_stage[st], s));
+            ids_dev = dd;
+        }
+        enqueue_layer(sp, x, a->d_ones, a->d_shy, ids_dev, slot0, s, false, false, nullptr);
+        // out = moe_out + shexp (ggml_add)
+        ck(gx::launch_add_inplace(out, a->d_shy, T * a->hidden, s));
+        ck(cudaEventRecord(a->ev_done[sp.li], s));
+        a->last_ev[sp.li] = a->ev_done[sp.li];
+        return GX_OK;
     });
 }
 

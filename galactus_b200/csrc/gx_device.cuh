@@ -498,6 +498,19 @@ __device__ __forceinline__ void bulk_g2s(void * dst_smem, const void * src_gmem,
         : "memory");
 }
 
+// The same with a suspend-time hint: a waiting thread sleeps in the barrier
+// until the phase completes or about `ns` nanoseconds pass, instead of
+// returning at once and spinning in the caller's loop.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t * bar, uint32_t parity, uint32_t ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
     uint32_t done;
     asm volatile(

@@ -2,24 +2,34 @@
 // a rank's tokens are dispatched to the ranks that own their experts, computed
 // there on the local slot arena, and combined at home in slot order.
 //
-// The exchange uses NCCL point-to-point calls grouped into one all-to-all per
+// The exchanges use NCCL point-to-point calls grouped into one all-to-all per
 // phase (ncclGroupStart/ncclSend/ncclRecv/ncclGroupEnd), on the caller's
 // communicator. The entry points are resolved at run time from the NCCL
 // library already loaded in the process (the one that created the caller's
 // communicator), else from libnccl.so.2 or $GX_NCCL_LIB, so the library does
 // not pin an NCCL version of its own.
 //
-// Per layer step:
-//   1. plan (host): pairs (t, s) grouped by the owner of ids[t, s];
-//   2. header all-to-all: per peer [count, expert ids...] (fixed size
-//      1 + max_pairs ints), then one stream synchronization: the host needs
-//      the received expert ids for the slot policy;
-//   3. row all-to-all: each pair's input row x[t] (H f32);
-//   4. local compute: the received pairs as a micro-batch of one slot each
-//      with unit router weight (gx_moe_layer_forward, k = 1), which leaves
-//      exactly the down projection of each pair: fl(1 * y) = y;
-//   5. row all-to-all back, scatter into [T, k, H] by pair, and the combine
-//      ((w0*y0 + w1*y1) + ...) of the single-GPU path.
+// One step covers n consecutive layers whose routes are known (one layer for
+// gx_ep_layer_forward / gx_ep_dispatch):
+//   1. shape all-to-all: 8 ints per peer [status, n, k, T, first layer, H,
+//      world, experts]; one stream synchronization. Every rank sees every
+//      rank's status and shape, so a call that one rank rejects (bad ids,
+//      mismatched layers or widths) ends with the same error on all ranks
+//      before any payload moves; T may differ between ranks;
+//   2. id all-to-all: per peer n counts and the local expert ids of the pairs
+//      (sized by the sender's own T); one stream synchronization: the owner's
+//      slot policy runs on its host;
+//   3. row all-to-all: each pair's input row x_L[t] (H f32), all layers in one
+//      exchange, rows grouped by peer then layer;
+//   4. owner compute, per layer with no host synchronization: the received
+//      rows of the layer as a micro-batch of one expert each with unit router
+//      weight (gx_moe_layer_forward, k = 1, expert-major waves when the slot
+//      cache cannot hold them at once): fl(1 * y) = y, the pair's down output;
+//   5. result all-to-all back, scatter to [n, T, k, H] by pair, and the
+//      combine ((w0*y0 + w1*y1) + ...) of the single-GPU path, per layer.
+// A failure on an owner after the exchanges began (a miss copy that fails)
+// does not stop the exchange: its result rows are NaN, the peers complete
+// their calls, and the owner returns the error.
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 
@@ -129,7 +139,7 @@ struct DevBuf {
         if (p) cudaFree(p);
         p = nullptr;
         n = 0;
-        ck(cudaMalloc(&p, want * sizeof(T)));
+        ck(cudaMalloc(&p, std::max<size_t>(want, 1) * sizeof(T)));
         n = want;
     }
     ~DevBuf() {
@@ -146,13 +156,15 @@ struct HostBuf {
         if (p) cudaFreeHost(p);
         p = nullptr;
         n = 0;
-        ck(cudaHostAlloc(&p, want * sizeof(T), cudaHostAllocDefault));
+        ck(cudaHostAlloc(&p, std::max<size_t>(want, 1) * sizeof(T), cudaHostAllocDefault));
         n = want;
     }
     ~HostBuf() {
         if (p) cudaFreeHost(p);
     }
 };
+
+constexpr int kShapeInts = 8;   // [status, n, k, T, first, H, world, experts]
 
 }  // namespace
 
@@ -163,44 +175,282 @@ struct gx_ep {
     uint32_t E = 0;
     int device = 0;
     std::mutex mu;
-    // the last dispatch
-    bool dispatched = false, computed = false;
-    uint32_t layer = 0;
-    int64_t k = 0, T = 0, H = 0, hdr = 0;   // hdr: ints per peer header
-    std::vector<int32_t> send_counts, recv_counts, send_off, recv_off;
-    std::vector<int32_t> send_pairs;        // pair index t*k+s, grouped by destination
-    std::vector<int32_t> recv_local;        // local expert id of each received pair
+    // the step in progress (0 idle, 1 dispatched, 2 computed)
+    int state = 0;
+    uint32_t first = 0, n = 0;
+    int64_t k = 0, T = 0, H = 0;
+    int err = GX_OK;                       // a failure on this owner during the step
+    std::vector<int32_t> peerT;            // T of each rank
+    // home side: the pairs sent to each peer, in send order (peer, layer, pair)
+    std::vector<int32_t> scount, soff;     // rows per peer, first row
+    std::vector<int32_t> send_L, send_pair;
+    // owner side: received rows, peer-major (peer, layer, in the sender's order)
+    std::vector<int32_t> rcount, roff;
+    std::vector<int32_t> recv_local;       // local expert id of each received row
+    std::vector<int32_t> lay_cnt, lay_off; // layer-major layout of the received rows
     int64_t n_recv = 0;
-    HostBuf<int32_t> h_hdr_send, h_hdr_recv, h_idx;
-    DevBuf<int32_t> d_hdr_send, d_hdr_recv, d_idx;
-    DevBuf<float> d_send, d_recv, d_recv_y, d_back, d_full, d_ones;
-    cudaEvent_t ev_hdr = nullptr;
+    // headers and index staging
+    HostBuf<int32_t> h_shape_s, h_shape_r, h_hdr_s, h_hdr_r, h_idx;
+    DevBuf<int32_t> d_shape_s, d_shape_r, d_hdr_s, d_hdr_r, d_idx;
+    HostBuf<const float *> h_ptrs;
+    DevBuf<const float *> d_ptrs;
+    // rows: sent inputs (peer-major), received inputs (peer-major), the same
+    // layer-major, owner outputs layer-major and peer-major, results back home
+    // (peer-major) and in [n, T, k, H] pair order
+    DevBuf<float> d_send, d_recv, d_xl, d_yl, d_yback, d_back, d_full, d_ones;
+    cudaEvent_t ev = nullptr;              // the last upload out of the pinned staging has run
+    gx_serve_stats st{};
 };
 
 namespace {
 
-// rows of the sent pairs: gather x[t] for each pair in send order, then one
-// grouped all-to-all of H-float rows
-void exchange_rows(gx_ep * ep, const float * src_rows, const std::vector<int32_t> & sc, const std::vector<int32_t> & so,
-                   float * dst_rows, const std::vector<int32_t> & rcnt, const std::vector<int32_t> & ro, int64_t H,
-                   cudaStream_t s) {
-    const int32_t G = ep->world;
-    if (G == 1) {
-        if (sc[0] > 0)
-            ck(cudaMemcpyAsync(dst_rows, src_rows, (size_t)sc[0] * (size_t)H * sizeof(float), cudaMemcpyDeviceToDevice, s));
-        return;
-    }
+// One grouped exchange: per peer r, send `scnt[r]` elements from src + soff[r]
+// and receive `rcnt[r]` into dst + roff[r] (elements of `width` values each).
+// The rank's own share is a device copy.
+template <typename V>
+void exchange(gx_ep * ep, const V * src, const std::vector<int32_t> & scnt, const std::vector<int32_t> & soff, V * dst,
+              const std::vector<int32_t> & rcnt, const std::vector<int32_t> & roff, int64_t width, int dtype,
+              cudaStream_t s) {
+    const int32_t G = ep->world, me = ep->rank;
+    if (scnt[(size_t)me] != rcnt[(size_t)me]) throw Invalid{GX_ERR_STATE};
+    if (scnt[(size_t)me] > 0)
+        ck(cudaMemcpyAsync(dst + (size_t)roff[(size_t)me] * (size_t)width, src + (size_t)soff[(size_t)me] * (size_t)width,
+                           (size_t)scnt[(size_t)me] * (size_t)width * sizeof(V), cudaMemcpyDeviceToDevice, s));
+    if (G == 1) return;
     const NcclApi & n = nccl();
     nk(n.group_start());
     for (int32_t r = 0; r < G; ++r) {
-        if (sc[(size_t)r] > 0)
-            nk(n.send(src_rows + (size_t)so[(size_t)r] * (size_t)H, (size_t)sc[(size_t)r] * (size_t)H, kNcclFloat32, r, ep->comm, s));
+        if (r == me) continue;
+        if (scnt[(size_t)r] > 0)
+            nk(n.send(src + (size_t)soff[(size_t)r] * (size_t)width, (size_t)scnt[(size_t)r] * (size_t)width, dtype, r,
+                      ep->comm, s));
         if (rcnt[(size_t)r] > 0)
-            nk(n.recv(dst_rows + (size_t)ro[(size_t)r] * (size_t)H, (size_t)rcnt[(size_t)r] * (size_t)H, kNcclFloat32, r, ep->comm, s));
+            nk(n.recv(dst + (size_t)roff[(size_t)r] * (size_t)width, (size_t)rcnt[(size_t)r] * (size_t)width, dtype, r,
+                      ep->comm, s));
     }
     nk(n.group_end());
 }
 
+// device -> pinned host copy, then wait for it (the host reads the result)
+void fetch(gx_ep * ep, int32_t * h, const int32_t * d, size_t count, cudaStream_t s) {
+    ck(cudaMemcpyAsync(h, d, count * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    ck(cudaEventRecord(ep->ev, s));
+    ck(cudaEventSynchronize(ep->ev));
+}
+
+// Steps 1-3 for n layers: shapes, ids, input rows. Every rank runs both
+// header exchanges, also when its own call is invalid (status != 0), and all
+// ranks return the same status.
+int ep_dispatch(gx_ep * ep, uint32_t first, uint32_t n, const float * const * x, const int32_t * ids, int64_t k,
+                int64_t T, int64_t H, cudaStream_t s) {
+    const int32_t G = ep->world, me = ep->rank;
+    ep->state = 0;
+    ep->err = GX_OK;
+    ep->st = gx_serve_stats{};
+    // local validation: the plan of every pair
+    int status = GX_OK;
+    if (n == 0 || k <= 0 || T < 0 || H <= 0 || x == nullptr || (T > 0 && ids == nullptr)) status = GX_ERR_INVALID;
+    const int64_t P = k * T;
+    std::vector<int32_t> dest, local;
+    if (status == GX_OK) {
+        dest.resize((size_t)(n * P));
+        local.resize((size_t)(n * P));
+        for (int64_t i = 0; i < (int64_t)n * P && status == GX_OK; ++i)
+            status = owner_of(ep->placement, ep->E, G, ids[i], dest[(size_t)i], local[(size_t)i]);
+    }
+    // 1. shapes
+    ep->h_shape_s.reserve((size_t)kShapeInts);
+    ep->h_shape_r.reserve((size_t)(G * kShapeInts));
+    ep->d_shape_s.reserve((size_t)(G * kShapeInts));
+    ep->d_shape_r.reserve((size_t)(G * kShapeInts));
+    const int32_t shape[kShapeInts] = {status, (int32_t)n, (int32_t)k, (int32_t)T, (int32_t)first, (int32_t)H, G,
+                                       (int32_t)ep->E};
+    ck(cudaEventSynchronize(ep->ev));   // the pinned staging is free
+    std::memcpy(ep->h_shape_s.p, shape, sizeof(shape));
+    ck(cudaMemcpyAsync(ep->d_shape_s.p, ep->h_shape_s.p, sizeof(shape), cudaMemcpyHostToDevice, s));
+    {
+        std::vector<int32_t> one((size_t)G, 1), zero((size_t)G, 0), offs((size_t)G, 0);
+        for (int32_t r = 0; r < G; ++r) offs[(size_t)r] = r;
+        // every peer gets the same 8 ints: send from offset 0, receive into slot r
+        exchange<int32_t>(ep, ep->d_shape_s.p, one, zero, ep->d_shape_r.p, one, offs, kShapeInts, kNcclInt32, s);
+    }
+    fetch(ep, ep->h_shape_r.p, ep->d_shape_r.p, (size_t)(G * kShapeInts), s);
+    ep->peerT.assign((size_t)G, 0);
+    int agreed = GX_OK;
+    for (int32_t r = 0; r < G; ++r) {
+        const int32_t * h = ep->h_shape_r.p + (size_t)r * kShapeInts;
+        if (h[0] != GX_OK && agreed == GX_OK) agreed = h[0];
+        if (h[1] != (int32_t)n || h[2] != (int32_t)k || h[4] != (int32_t)first || h[5] != (int32_t)H || h[6] != G ||
+            h[7] != (int32_t)ep->E || h[3] < 0)
+            if (agreed == GX_OK) agreed = GX_ERR_INVALID;
+        ep->peerT[(size_t)r] = h[3];
+    }
+    if (agreed != GX_OK) return agreed;
+
+    // 2. ids: per peer [n counts][local ids, layer by layer]
+    ep->first = first;
+    ep->n = n;
+    ep->k = k;
+    ep->T = T;
+    ep->H = H;
+    ep->scount.assign((size_t)G, 0);
+    std::vector<int32_t> cnt((size_t)G * n, 0);   // [peer][layer]
+    for (uint32_t L = 0; L < n; ++L)
+        for (int64_t i = 0; i < P; ++i) ++cnt[(size_t)dest[(size_t)(L * P + i)] * n + L];
+    for (int32_t r = 0; r < G; ++r)
+        for (uint32_t L = 0; L < n; ++L) ep->scount[(size_t)r] += cnt[(size_t)r * n + L];
+    ep->soff.assign((size_t)G, 0);
+    for (int32_t r = 1; r < G; ++r) ep->soff[(size_t)r] = ep->soff[(size_t)r - 1] + ep->scount[(size_t)r - 1];
+    // send order: peer, layer, pair
+    ep->send_L.assign((size_t)(n * P), 0);
+    ep->send_pair.assign((size_t)(n * P), 0);
+    const int64_t hs = (int64_t)n * (1 + P);         // ints this rank sends to each peer
+    std::vector<int64_t> hoff((size_t)G + 1, 0);     // ints received from each peer
+    for (int32_t r = 0; r < G; ++r) hoff[(size_t)r + 1] = hoff[(size_t)r] + (int64_t)n * (1 + k * ep->peerT[(size_t)r]);
+    ep->h_hdr_s.reserve((size_t)(G * hs));
+    ep->h_hdr_r.reserve((size_t)hoff[(size_t)G]);
+    ep->d_hdr_s.reserve((size_t)(G * hs));
+    ep->d_hdr_r.reserve((size_t)hoff[(size_t)G]);
+    {
+        std::vector<int32_t> fill(ep->soff);
+        for (int32_t r = 0; r < G; ++r) {
+            int32_t * h = ep->h_hdr_s.p + (size_t)r * hs;
+            int32_t * idp = h + n;
+            for (uint32_t L = 0; L < n; ++L) h[L] = cnt[(size_t)r * n + L];
+            for (uint32_t L = 0; L < n; ++L)
+                for (int64_t i = 0; i < P; ++i) {
+                    const size_t j = (size_t)(L * P + i);
+                    if (dest[j] != r) continue;
+                    *idp++ = local[j];
+                    ep->send_L[(size_t)fill[(size_t)r]] = (int32_t)L;
+                    ep->send_pair[(size_t)fill[(size_t)r]++] = (int32_t)i;
+                }
+        }
+    }
+    ck(cudaMemcpyAsync(ep->d_hdr_s.p, ep->h_hdr_s.p, (size_t)(G * hs) * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    {
+        std::vector<int32_t> sc((size_t)G, (int32_t)hs), so((size_t)G), rc((size_t)G), ro((size_t)G);
+        for (int32_t r = 0; r < G; ++r) {
+            so[(size_t)r] = (int32_t)(r * hs);
+            rc[(size_t)r] = (int32_t)(hoff[(size_t)r + 1] - hoff[(size_t)r]);
+            ro[(size_t)r] = (int32_t)hoff[(size_t)r];
+        }
+        exchange<int32_t>(ep, ep->d_hdr_s.p, sc, so, ep->d_hdr_r.p, rc, ro, 1, kNcclInt32, s);
+    }
+    fetch(ep, ep->h_hdr_r.p, ep->d_hdr_r.p, (size_t)hoff[(size_t)G], s);
+    // received rows: peer-major, layer, sender's order
+    ep->rcount.assign((size_t)G, 0);
+    ep->roff.assign((size_t)G, 0);
+    ep->recv_local.clear();
+    ep->lay_cnt.assign(n, 0);
+    std::vector<int32_t> rl;   // layer of each received row
+    for (int32_t r = 0; r < G; ++r) {
+        const int32_t * h = ep->h_hdr_r.p + hoff[(size_t)r];
+        const int32_t * idp = h + n;
+        ep->roff[(size_t)r] = (int32_t)ep->recv_local.size();
+        for (uint32_t L = 0; L < n; ++L) {
+            if (h[L] < 0 || h[L] > k * ep->peerT[(size_t)r]) throw Invalid{GX_ERR_STATE};
+            for (int32_t i = 0; i < h[L]; ++i) {
+                ep->recv_local.push_back(*idp++);
+                rl.push_back((int32_t)L);
+            }
+            ep->lay_cnt[L] += h[L];
+            ep->rcount[(size_t)r] += h[L];
+        }
+    }
+    ep->n_recv = (int64_t)ep->recv_local.size();
+    ep->lay_off.assign(n, 0);
+    for (uint32_t L = 1; L < n; ++L) ep->lay_off[L] = ep->lay_off[L - 1] + ep->lay_cnt[L - 1];
+
+    // 3. input rows: gather x_L[t] of every sent pair, exchange
+    const int64_t S = n * P, R = ep->n_recv;
+    ep->h_idx.reserve((size_t)(3 * S + R));
+    ep->d_idx.reserve((size_t)(3 * S + R));
+    ep->h_ptrs.reserve(n);
+    ep->d_ptrs.reserve(n);
+    int32_t * hL = ep->h_idx.p;             // [S] layer of each sent row
+    int32_t * hR = hL + S;                  // [S] token of each sent row
+    int32_t * hlm = hR + S;                 // [R] layer-major position of each received row
+    int32_t * hfull = hlm + R;              // [S] pair position in [n, T, k] of each sent row (results)
+    for (int64_t j = 0; j < S; ++j) {
+        hL[j] = ep->send_L[(size_t)j];
+        hR[j] = ep->send_pair[(size_t)j] / (int32_t)k;
+    }
+    {
+        std::vector<int32_t> lf(ep->lay_off);
+        for (int64_t j = 0; j < R; ++j) hlm[j] = lf[(size_t)rl[(size_t)j]]++;
+    }
+    for (int64_t j = 0; j < S; ++j) hfull[j] = (int32_t)(ep->send_L[(size_t)j] * P + ep->send_pair[(size_t)j]);
+    for (uint32_t L = 0; L < n; ++L) ep->h_ptrs.p[L] = x[L];
+    ck(cudaMemcpyAsync(ep->d_idx.p, ep->h_idx.p, (size_t)(3 * S + R) * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    ck(cudaMemcpyAsync(ep->d_ptrs.p, ep->h_ptrs.p, (size_t)n * sizeof(const float *), cudaMemcpyHostToDevice, s));
+    ck(cudaEventRecord(ep->ev, s));   // the staging is rewritten by the next step only after these uploads
+    ep->d_send.reserve((size_t)std::max<int64_t>(S, 1) * (size_t)H);
+    ep->d_recv.reserve((size_t)std::max<int64_t>(R, 1) * (size_t)H);
+    ck(gx::launch_gather_ptrs(ep->d_ptrs.p, ep->d_idx.p, ep->d_idx.p + S, S, H, ep->d_send.p, s));
+    exchange<float>(ep, ep->d_send.p, ep->scount, ep->soff, ep->d_recv.p, ep->rcount, ep->roff, H, kNcclFloat32, s);
+    ep->state = 1;
+    (void)me;
+    return GX_OK;
+}
+
+// Step 4: the received rows of every layer on the local arena. A failure is
+// recorded (ep->err) and leaves that layer's result rows NaN.
+void ep_compute(gx_ep * ep, const gx_layer_desc * desc, cudaStream_t s) {
+    const int64_t R = ep->n_recv, H = ep->H, S = (int64_t)ep->n * ep->k * ep->T;
+    ep->d_xl.reserve((size_t)std::max<int64_t>(R, 1) * (size_t)H);
+    ep->d_yl.reserve((size_t)std::max<int64_t>(R, 1) * (size_t)H);
+    ep->d_yback.reserve((size_t)std::max<int64_t>(R, 1) * (size_t)H);
+    const int32_t * dlm = ep->d_idx.p + 2 * S;   // layer-major position of each received row
+    if (R > 0) {
+        ck(gx::launch_move_rows(ep->d_recv.p, dlm, R, H, ep->d_xl.p, true, s));
+        int64_t mx = 0;
+        for (uint32_t L = 0; L < ep->n; ++L) mx = std::max<int64_t>(mx, ep->lay_cnt[L]);
+        if ((int64_t)ep->d_ones.n < mx) {
+            ep->d_ones.reserve((size_t)mx);
+            ck(gx::launch_fill(ep->d_ones.p, mx, 1.0f, s));
+        }
+        // local ids in layer-major order (rows arrive peer-major, layers in
+        // order inside each peer; hlm is the layer-major position of each)
+        std::vector<int32_t> lids((size_t)R);
+        const int32_t * hlm = ep->h_idx.p + 2 * S;
+        for (int64_t j = 0; j < R; ++j) lids[(size_t)hlm[j]] = ep->recv_local[(size_t)j];
+        for (uint32_t L = 0; L < ep->n; ++L) {
+            const int64_t c = ep->lay_cnt[L];
+            if (c == 0) continue;
+            gx_serve_stats st{};
+            const int64_t o = ep->lay_off[L];
+            const int rc = gx_moe_layer_forward(ep->arena, ep->first + L, desc, ep->d_xl.p + o * H, lids.data() + o,
+                                                ep->d_ones.p, 1, c, ep->d_yl.p + o * H, s, &st);
+            if (rc != GX_OK) {
+                if (ep->err == GX_OK) ep->err = rc;
+                ck(cudaMemsetAsync(ep->d_yl.p + o * H, 0xff, (size_t)(c * H) * sizeof(float), s));
+                continue;
+            }
+            ep->st.hits += st.hits;
+            ep->st.misses += st.misses;
+            ep->st.evictions += st.evictions;
+            ep->st.distinct += st.distinct;
+            ep->st.bytes_copied += st.bytes_copied;
+        }
+        // back to peer-major order for the results exchange
+        ck(gx::launch_move_rows(ep->d_yl.p, dlm, R, H, ep->d_yback.p, false, s));
+    }
+    ep->state = 2;
+}
+
+// Step 5: results home, scattered to pair order, combined per layer.
+void ep_combine(gx_ep * ep, const float * const * w, float * const * out, cudaStream_t s) {
+    const int64_t P = ep->k * ep->T, S = (int64_t)ep->n * P, H = ep->H;
+    ep->d_back.reserve((size_t)std::max<int64_t>(S, 1) * (size_t)H);
+    ep->d_full.reserve((size_t)std::max<int64_t>(S, 1) * (size_t)H);
+    exchange<float>(ep, ep->d_yback.p, ep->rcount, ep->roff, ep->d_back.p, ep->scount, ep->soff, H, kNcclFloat32, s);
+    const int32_t * dfull = ep->d_idx.p + 2 * S + ep->n_recv;   // pair positions, after the layer-major positions
+    if (S > 0) ck(gx::launch_move_rows(ep->d_back.p, dfull, S, H, ep->d_full.p, true, s));
+    for (uint32_t L = 0; L < ep->n; ++L)
+        if (ep->T > 0) ck(gx::launch_combine(ep->d_full.p + (size_t)L * P * H, w[L], out[L], H, (int)ep->k, ep->T, s));
+    ep->state = 0;
+}
 
 }  // namespace
 
@@ -249,7 +499,7 @@ int gx_ep_init(gx_arena * local_arena, void * nccl_comm, int32_t rank, int32_t w
         ep->E = n_expert;
         ep->placement = placement;
         ck(cudaGetDevice(&ep->device));
-        ck(cudaEventCreateWithFlags(&ep->ev_hdr, cudaEventDisableTiming));
+        ck(cudaEventCreateWithFlags(&ep->ev, cudaEventDisableTiming));
         return GX_OK;
     });
     if (rc != GX_OK) {
@@ -264,121 +514,31 @@ int gx_ep_destroy(gx_ep * ep) {
     if (ep == nullptr) return GX_OK;
     cudaSetDevice(ep->device);
     cudaDeviceSynchronize();
-    if (ep->ev_hdr) cudaEventDestroy(ep->ev_hdr);
+    if (ep->ev) cudaEventDestroy(ep->ev);
     delete ep;
     return GX_OK;
 }
 
 int gx_ep_dispatch(gx_ep * ep, uint32_t layer, const float * x, const int32_t * ids, int64_t k, int64_t T, int64_t H,
                    void * stream) {
-    if (ep == nullptr || x == nullptr || ids == nullptr || k <= 0 || T <= 0 || H <= 0) return GX_ERR_INVALID;
+    if (ep == nullptr) return GX_ERR_INVALID;
     return guarded([&] {
         std::lock_guard<std::mutex> lock(ep->mu);
         ck(cudaSetDevice(ep->device));
-        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-        const int32_t G = ep->world;
-        const int64_t P = k * T;
-        ep->dispatched = ep->computed = false;
-        ep->layer = layer;
-        ep->k = k;
-        ep->T = T;
-        ep->send_counts.assign((size_t)G, 0);
-        ep->send_pairs.assign((size_t)P, 0);
-        int rc = gx_ep_plan(ep->placement, ep->E, G, ids, k, T, ep->send_counts.data(), ep->send_pairs.data());
-        if (rc != GX_OK) throw Invalid{rc};
-        ep->send_off.assign((size_t)G, 0);
-        for (int32_t r = 1; r < G; ++r) ep->send_off[(size_t)r] = ep->send_off[(size_t)r - 1] + ep->send_counts[(size_t)r - 1];
-
-        // 2. headers: [count, global expert ids of the pairs] per peer
-        ep->hdr = 1 + P;
-        ep->h_hdr_send.reserve((size_t)(G * ep->hdr));
-        ep->h_hdr_recv.reserve((size_t)(G * ep->hdr));
-        ep->d_hdr_send.reserve((size_t)(G * ep->hdr));
-        ep->d_hdr_recv.reserve((size_t)(G * ep->hdr));
-        for (int32_t r = 0; r < G; ++r) {
-            int32_t * h = ep->h_hdr_send.p + (size_t)r * ep->hdr;
-            h[0] = ep->send_counts[(size_t)r];
-            for (int32_t i = 0; i < ep->send_counts[(size_t)r]; ++i) h[1 + i] = ids[ep->send_pairs[(size_t)(ep->send_off[(size_t)r] + i)]];
-        }
-        ck(cudaMemcpyAsync(ep->d_hdr_send.p, ep->h_hdr_send.p, (size_t)(G * ep->hdr) * sizeof(int32_t),
-                           cudaMemcpyHostToDevice, s));
-        if (G > 1) {
-            const NcclApi & n = nccl();
-            nk(n.group_start());
-            for (int32_t r = 0; r < G; ++r) {
-                nk(n.send(ep->d_hdr_send.p + (size_t)r * ep->hdr, (size_t)ep->hdr, kNcclInt32, r, ep->comm, s));
-                nk(n.recv(ep->d_hdr_recv.p + (size_t)r * ep->hdr, (size_t)ep->hdr, kNcclInt32, r, ep->comm, s));
-            }
-            nk(n.group_end());
-        } else {
-            ck(cudaMemcpyAsync(ep->d_hdr_recv.p, ep->d_hdr_send.p, (size_t)ep->hdr * sizeof(int32_t),
-                               cudaMemcpyDeviceToDevice, s));
-        }
-        ck(cudaMemcpyAsync(ep->h_hdr_recv.p, ep->d_hdr_recv.p, (size_t)(G * ep->hdr) * sizeof(int32_t),
-                           cudaMemcpyDeviceToHost, s));
-        ck(cudaEventRecord(ep->ev_hdr, s));
-        ck(cudaEventSynchronize(ep->ev_hdr));
-        ep->recv_counts.assign((size_t)G, 0);
-        ep->recv_off.assign((size_t)G, 0);
-        ep->recv_local.clear();
-        for (int32_t r = 0; r < G; ++r) {
-            const int32_t * h = ep->h_hdr_recv.p + (size_t)r * ep->hdr;
-            if (h[0] < 0 || h[0] > P) throw Invalid{GX_ERR_INVALID};
-            ep->recv_counts[(size_t)r] = h[0];
-            ep->recv_off[(size_t)r] = (int32_t)ep->recv_local.size();
-            for (int32_t i = 0; i < h[0]; ++i) {
-                int32_t owner = 0, local = 0;
-                rc = owner_of(ep->placement, ep->E, G, h[1 + i], owner, local);
-                if (rc != GX_OK || owner != ep->rank) throw Invalid{rc != GX_OK ? rc : GX_ERR_DOMAIN};
-                ep->recv_local.push_back(local);
-            }
-        }
-        ep->n_recv = (int64_t)ep->recv_local.size();
-
-        // 3. the input row of every sent pair, then one grouped all-to-all
-        ep->H = H;
-        ep->h_idx.reserve((size_t)P);
-        ep->d_idx.reserve((size_t)P);
-        for (int64_t i = 0; i < P; ++i) ep->h_idx.p[i] = ep->send_pairs[(size_t)i] / (int32_t)k;
-        ck(cudaMemcpyAsync(ep->d_idx.p, ep->h_idx.p, (size_t)P * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-        ep->d_send.reserve((size_t)(P * H));
-        ck(gx::launch_move_rows(x, ep->d_idx.p, P, H, ep->d_send.p, false, s));
-        ep->d_recv.reserve((size_t)std::max<int64_t>(ep->n_recv, 1) * (size_t)H);
-        exchange_rows(ep, ep->d_send.p, ep->send_counts, ep->send_off, ep->d_recv.p, ep->recv_counts, ep->recv_off, H, s);
-        // the pinned index buffer is rewritten by combine only after this copy ran
-        ck(cudaEventRecord(ep->ev_hdr, s));
-        ep->dispatched = true;
-        return GX_OK;
+        const float * xs[1] = {x};
+        return ep_dispatch(ep, layer, 1, xs, ids, k, T, H, reinterpret_cast<cudaStream_t>(stream));
     });
 }
-
-}  // extern "C"
-
-
-extern "C" {
 
 int gx_ep_compute(gx_ep * ep, const gx_layer_desc * desc, void * stream, gx_serve_stats * stats) {
     if (ep == nullptr || desc == nullptr) return GX_ERR_INVALID;
     return guarded([&] {
         std::lock_guard<std::mutex> lock(ep->mu);
-        if (!ep->dispatched) throw Invalid{GX_ERR_STATE};
+        if (ep->state != 1) throw Invalid{GX_ERR_STATE};
         if (desc->hidden != ep->H) throw Invalid{GX_ERR_INVALID};
         ck(cudaSetDevice(ep->device));
-        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-        const int64_t R = ep->n_recv, H = ep->H;
-        // 4. the received pairs as a micro-batch of one slot each, unit weight
-        ep->d_recv_y.reserve((size_t)std::max<int64_t>(R, 1) * (size_t)H);
-        gx_serve_stats st{};
-        if (R > 0) {
-            ep->d_ones.reserve((size_t)R);
-            ck(gx::launch_fill(ep->d_ones.p, R, 1.0f, s));
-            const int rc = gx_moe_layer_forward(ep->arena, ep->layer, desc, ep->d_recv.p, ep->recv_local.data(),
-                                                ep->d_ones.p, 1, R, ep->d_recv_y.p, stream, &st);
-            if (rc != GX_OK) throw Invalid{rc};
-        }
-        if (stats) *stats = st;
-        ep->dispatched = false;
-        ep->computed = true;
+        ep_compute(ep, desc, reinterpret_cast<cudaStream_t>(stream));
+        if (stats) *stats = ep->st;
         return GX_OK;
     });
 }
@@ -387,36 +547,42 @@ int gx_ep_combine(gx_ep * ep, const float * w, float * out, void * stream) {
     if (ep == nullptr || w == nullptr || out == nullptr) return GX_ERR_INVALID;
     return guarded([&] {
         std::lock_guard<std::mutex> lock(ep->mu);
-        if (!ep->computed) throw Invalid{GX_ERR_STATE};
+        if (ep->state != 2) throw Invalid{GX_ERR_STATE};
+        ck(cudaSetDevice(ep->device));
+        const float * ws[1] = {w};
+        float * os[1] = {out};
+        ep_combine(ep, ws, os, reinterpret_cast<cudaStream_t>(stream));
+        const int e = ep->err;
+        ep->err = GX_OK;
+        return e;
+    });
+}
+
+int gx_ep_stack_forward(gx_ep * ep, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * desc,
+                        const float * const * x, const int32_t * ids, const float * const * w, int64_t k, int64_t T,
+                        float * const * out, void * stream, gx_serve_stats * stats) {
+    if (ep == nullptr || desc == nullptr || w == nullptr || out == nullptr) return GX_ERR_INVALID;
+    return guarded([&] {
+        std::lock_guard<std::mutex> lock(ep->mu);
         ck(cudaSetDevice(ep->device));
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-        const int64_t P = ep->k * ep->T, H = ep->H;
-        // 5. outputs back to their home ranks, in the order the pairs were sent
-        ep->d_back.reserve((size_t)P * (size_t)H);
-        exchange_rows(ep, ep->d_recv_y.p, ep->recv_counts, ep->recv_off, ep->d_back.p, ep->send_counts, ep->send_off, H, s);
-        // scatter to [T, k, H] by pair index, then the slot-order combine
-        ep->d_full.reserve((size_t)P * (size_t)H);
-        ck(cudaEventSynchronize(ep->ev_hdr));   // the dispatch's index copy has run
-        for (int64_t i = 0; i < P; ++i) ep->h_idx.p[i] = ep->send_pairs[(size_t)i];
-        ck(cudaMemcpyAsync(ep->d_idx.p, ep->h_idx.p, (size_t)P * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-        ck(gx::launch_move_rows(ep->d_back.p, ep->d_idx.p, P, H, ep->d_full.p, true, s));
-        ck(gx::launch_combine(ep->d_full.p, w, out, H, (int)ep->k, ep->T, s));
-        // the pinned index buffer is rewritten by the next call only after this copy ran
-        ck(cudaEventRecord(ep->ev_hdr, s));
-        ck(cudaEventSynchronize(ep->ev_hdr));
-        ep->computed = false;
-        return GX_OK;
+        const int rc = ep_dispatch(ep, first_layer, n_layers, x, ids, k, T, desc->hidden, s);
+        if (rc != GX_OK) return rc;
+        ep_compute(ep, desc, s);
+        ep_combine(ep, w, out, s);
+        if (stats) *stats = ep->st;
+        const int e = ep->err;
+        ep->err = GX_OK;
+        return e;
     });
 }
 
 int gx_ep_layer_forward(gx_ep * ep, uint32_t layer, const gx_layer_desc * desc, const float * x, const int32_t * ids,
                         const float * w, int64_t k, int64_t T, float * out, void * stream, gx_serve_stats * stats) {
-    if (desc == nullptr) return GX_ERR_INVALID;
-    int rc = gx_ep_dispatch(ep, layer, x, ids, k, T, desc->hidden, stream);
-    if (rc != GX_OK) return rc;
-    rc = gx_ep_compute(ep, desc, stream, stats);
-    if (rc != GX_OK) return rc;
-    return gx_ep_combine(ep, w, out, stream);
+    const float * xs[1] = {x};
+    const float * ws[1] = {w};
+    float * os[1] = {out};
+    return gx_ep_stack_forward(ep, layer, 1, desc, xs, ids, ws, k, T, os, stream, stats);
 }
 
 }  // extern "C"

@@ -220,6 +220,19 @@ __global__ void k_move_rows(const float * src, const int32_t * idx, int64_t n, i
     }
 }
 
+__global__ void k_gather_ptrs(const float * const * ptrs, const int32_t * layers, const int32_t * rows, int64_t n,
+                              int64_t H, float * dst) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n * H; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / H, c = i - j * H;
+        dst[i] = ptrs[layers[j]][(int64_t)rows[j] * H + c];
+    }
+}
+
+__global__ void k_add_inplace(float * out, const float * b, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = __fadd_rn(out[i], b[i]);
+}
+
 __global__ void k_fill(float * dst, int64_t n, float v) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) dst[i] = v;
 }
@@ -499,6 +512,19 @@ cudaError_t launch_move_rows(const float * src, const int32_t * idx, int64_t n, 
     return cudaGetLastError();
 }
 
+cudaError_t launch_gather_ptrs(const float * const * ptrs, const int32_t * layers, const int32_t * rows, int64_t n,
+                               int64_t H, float * dst, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    k_gather_ptrs<<<grid_1d(n * H, 256), 256, 0, stream>>>(ptrs, layers, rows, n, H, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add_inplace(float * out, const float * b, int64_t n, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    k_add_inplace<<<grid_1d(n, 256), 256, 0, stream>>>(out, b, n);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_fill(float * dst, int64_t n, float v, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     k_fill<<<grid_1d(n, 256), 256, 0, stream>>>(dst, n, v);
@@ -764,7 +790,7 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     // producers would share a stage and one could wait on a barrier two phases
     // behind, read the older phase as complete and refill a stage in use.
     if (p.C % kStackProducers != 0) return 0;
-    if (p.W < 1 || p.W > kStackMaxWarps) return 0;
+    if (p.W < 1 || p.W > stack_max_warps(p.row_mode)) return 0;
     if (p.row_mode == 1 && (p.Rd & 1)) return 0;   // octet row pairs stay inside one expert
     threads = 32 * (kStackProducers + 2) + 32 * p.W;
     if (!stack_copy_mode(p.nb01_d, p.Rd, p.row_copy_d, p.pitch_d)) return 0;

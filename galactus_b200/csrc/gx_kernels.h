@@ -116,7 +116,10 @@ struct StackLayer {
 };
 
 constexpr int kStackMaxConsumers = 16;  // ring stages
-constexpr int kStackMaxWarps = 12;      // consumer warps
+constexpr int kStackMaxWarps = 16;      // consumer warps (any row mode)
+// consumer warps of a row mode: the MXFP4 rows (mode 3) run four warps per
+// 32-row job, the others at most twelve (their register budgets)
+GX_HD constexpr int stack_max_warps(int row_mode) { return row_mode == 3 ? 16 : 12; }
 constexpr int kStackProducers = 2;      // weight producer warps (even and odd jobs)
 constexpr int kStackMaxLayers = 128;   // the layer table travels in the kernel parameters
 constexpr int kStackBufs = 2;          // activation buffers per kind (gate/up inputs, down inputs)
@@ -145,7 +148,8 @@ struct StackParams {
     float alpha, limit;
     uint32_t bar_off, meta_off, stage_off, xbuf_off, dbuf_off, wt_off, slots_off, dots_off;
     int32_t need_grid;         // 1: IQ1_S rows, the 16 KB codebook copied to shared memory at grid_off
-    int32_t split;             // warps per job: 2 for octet jobs and 32-row two-lane K-quant down jobs, else 1
+    int32_t split;             // warps per job: 4 for MXFP4 jobs, 2 for octet jobs and 32-row two-lane K-quant
+                               // down jobs, else 1
     uint32_t grid_off;
     StackLayer layers[kStackMaxLayers];
 };
@@ -202,6 +206,11 @@ cudaError_t launch_combine(const float * y, const float * w, float * out, int64_
 cudaError_t launch_move_rows(const float * src, const int32_t * idx, int64_t n, int64_t H, float * dst, bool scatter,
                              cudaStream_t stream);
 cudaError_t launch_fill(float * dst, int64_t n, float v, cudaStream_t stream);
+// dst[j] = row rows[j] of the [*, H] matrix at ptrs[layers[j]] (gather over a pointer table)
+cudaError_t launch_gather_ptrs(const float * const * ptrs, const int32_t * layers, const int32_t * rows, int64_t n,
+                               int64_t H, float * dst, cudaStream_t stream);
+// out[i] = out[i] + b[i] (one rounding per element)
+cudaError_t launch_add_inplace(float * out, const float * b, int64_t n, cudaStream_t stream);
 // router: logits [rows, ld] -> ids/w [rows, k] (+ slots through table); rows = n_layers * T
 constexpr int kRouterWarps = 4;
 constexpr int kRouterMaxExperts = 1024;

@@ -35,12 +35,20 @@
 // error, and on giving up records GX_DEVERR_TIMEOUT; producers then let their
 // copies in flight land (bounded) before the CTA exits.
 //
-// Other block types (Q4_K gate/up with Q6_K down, MXFP4, IQ1_S) use the
-// octet row dots of the per-layer kernels (eight lanes per row, two rows per
-// lane, gx_moe.cuh): a gate/up job is two passes over gate row i and up row i
-// together (octet g takes i = 4*pass + g), a down job four passes over row
-// pairs (2g, 2g+1) of one expert; the down dots go through a per-warp scratch
-// to the combine. Their activations are Q8_K (256-element blocks) or Q8_0.
+// IQ1_S rows use the octet row dots of the per-layer kernels (eight lanes per
+// row, two rows per lane, gx_moe.cuh): a gate/up job is two passes over gate
+// row i and up row i together (octet g takes i = 4*pass + g), a down job four
+// passes over row pairs (2g, 2g+1) of one expert; the down dots go through a
+// per-warp scratch to the combine. Their activations are Q8_K.
+//
+// MXFP4 rows (gpt-oss-shaped models): a job is 32 rows (16 gate + 16 up, or
+// 32/k rows of each of the k experts), four warps per job. Lane r of each
+// warp takes row r; warp `sub` computes the pair terms t_u of the pairs
+// u = sub, sub+4, ... (every integer dot exact, each term in the reference's
+// float order) and parks each term in a word of the stage that only its pair
+// occupies; the job's last warp folds every row's terms in pair order,
+// releases the stage and runs the epilogue. The Q8_0 activation rows these
+// jobs read are stored in the codes' byte order.
 //
 // Q8_0 rows (the gate/up/down type of Q8_0 models): two lanes per weight row,
 // one per block parity. Lane p owns the four NEON accumulator chains of the
@@ -79,17 +87,20 @@ __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_re
 __device__ __forceinline__ bool stack_wait(const int32_t * p, int32_t target) {
     for (uint32_t i = 0; i < (1u << 23); ++i) {
         if (*reinterpret_cast<const volatile int32_t *>(p) >= target) return true;
-        if (*reinterpret_cast<volatile int *>(&g_dev_error) != 0) return false;
-        if (i >= 64) __nanosleep(64);
+        if ((i & 15u) == 15u && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) return false;
+        if (i >= 8) __nanosleep(64);
     }
     return false;
 }
 
 // Bounded mbarrier wait that also stops once another CTA recorded an error.
+// Each poll sleeps in the barrier for up to 0.5 us (it wakes when the phase
+// completes), so waiting warps leave the issue slots to the working ones; the
+// bound is 2^20 polls (about half a second).
 __device__ __forceinline__ bool stack_mbar_wait(uint64_t * bar, uint32_t parity) {
-    for (uint32_t i = 0; i < (1u << 22); ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 255u && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) return false;
+    for (uint32_t i = 0; i < (1u << 20); ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 500u)) return true;
+        if ((i & 63u) == 63u && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) return false;
     }
     return false;
 }
@@ -338,8 +349,9 @@ __device__ __forceinline__ uint32_t prmt_sx(uint32_t a, uint32_t b, uint32_t c) 
 // bytes 0-3 and 4-7 of the prmt source pair
 constexpr uint32_t kE2m1Lo = 0x03020100u, kE2m1Hi = 0x0c080604u;
 
-// Exact dot of one MXFP4 block (16 code bytes at w >> sh + 8 bits; code byte j
-// holds elements j and j+16) with its Q8_0 activation block stored in code
+// Exact dot of the 16 code bytes at words W0.. of w, shifted right by cs bits
+// (a clamped funnel shift: cs = 32 takes the next word whole; code byte j
+// holds elements j and j+16), with its Q8_0 activation block stored in code
 // order (quant_block_split<..., PERM>: word 2t = elements 4t, 4t+16, 4t+1,
 // 4t+17, word 2t+1 = 4t+2, 4t+18, 4t+3, 4t+19). prmt in its default mode
 // takes a selector nibble's low three bits as the byte index and its high bit
@@ -347,12 +359,13 @@ constexpr uint32_t kE2m1Lo = 0x03020100u, kE2m1Hi = 0x0c080604u;
 // non-negative, so prmt(table, q) gives the magnitudes of the positive codes
 // and zero for the negative ones, and prmt(table, q ^ 0x8888...) the
 // reverse. dot = dp4a(positive mags, a) - dp4a(negative mags, a), exact.
-__device__ __forceinline__ int mxfp4_block_dot(const uint32_t (&w)[5], uint32_t sh, const uint4 & a0, const uint4 & a1) {
+template <int W0>
+__device__ __forceinline__ int mxfp4_codes_dot(const uint32_t (&w)[9], uint32_t cs, const uint4 & a0, const uint4 & a1) {
     const uint32_t aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     int pp0 = 0, pp1 = 0, pn0 = 0, pn1 = 0;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-        const uint32_t q = __funnelshift_rc(w[t], w[t + 1], sh + 8u);
+        const uint32_t q = __funnelshift_rc(w[W0 + t], w[W0 + t + 1], cs);
         const uint32_t qx = q ^ 0x88888888u;
         pp0 = dp4a(prmt_sx(kE2m1Lo, kE2m1Hi, q), aw[2 * t], pp0);
         pn0 = dp4a(prmt_sx(kE2m1Lo, kE2m1Hi, qx), aw[2 * t], pn0);
@@ -362,42 +375,67 @@ __device__ __forceinline__ int mxfp4_block_dot(const uint32_t (&w)[5], uint32_t 
     return (pp0 + pp1) - (pn0 + pn1);
 }
 
-// MXFP4 row x Q8_0 activation row (split layout, blocks in code order), two
-// lanes per row (ggml_vec_dot_mxfp4_q8_0, diff:1167-1174, 1209-1240). Lane p
-// takes block 2u+p of every pair u (17 bytes: e8m0 scale, 16 code bytes),
-// read as five aligned words at a byte offset that alternates between two
-// values along the row. The pair's term t = fma(sc_e, p_e, sc_o*p_o), with
-// sc = fp16(y.d) * e8m0/2: the odd lane sends sc_o*p_o to its partner
-// (lane ^ xm), the even lane forms t and adds it to the row's chain in pair
-// order. The row's dot is valid on the even-block lane (p == 0) only.
-__device__ __forceinline__ float mxfp4_row2(const uint8_t * row, const uint8_t * act, const ActLayout & al, int p,
-                                            int npairs, int xm) {
-    float sumf = 0.0f;
-    const uintptr_t rb = reinterpret_cast<uintptr_t>(row) + 17u * (uint32_t)p;
-    const uint8_t * wbase = reinterpret_cast<const uint8_t *>(rb & ~(uintptr_t)3);
-    const uint32_t off = (uint32_t)(rb & 3);            // block of pair u at wbase + off + 34u
-    const uint8_t * aq = act + 32 * p;                  // activation block 2u+p at aq + 64u
-    const uint8_t * ad = act + al.d_off;                // fp16 scales of pair u in word u
-    const uint32_t dsh = 16u * (uint32_t)p;
-#pragma unroll 2
-    for (int u = 0; u < npairs; ++u) {
-        const uint32_t B = off + 34u * (uint32_t)u;
-        const uint8_t * wp = wbase + (B & ~3u);
-        const uint32_t sh = (B & 3u) * 8u;
-        uint32_t w[5];
+// The term of block pair u of one MXFP4 row (ggml_vec_dot_mxfp4_q8_0's
+// t = fma(sc_e, p_e, sc_o*p_o), diff:1209-1240), computed by one lane from the
+// pair's 34 bytes at `pr` (an even byte offset: row pitches and pair sizes are
+// even), read as nine aligned words, against the activation pair at `ap`
+// (64 quants in code order) and its two fp16 scales in word `dw`.
+__device__ __forceinline__ float mxfp4_pair_term(const uint8_t * pr, const uint8_t * ap, uint32_t dw) {
+    const uintptr_t P = reinterpret_cast<uintptr_t>(pr);
+    const uint8_t * wp = reinterpret_cast<const uint8_t *>(P & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(P & 3) * 8u;   // 0 or 16
+    uint32_t w[9];
 #pragma unroll
-        for (int i = 0; i < 5; ++i) w[i] = lds32(wp + 4 * i);
-        const uint4 a0 = lds128(aq + 64 * u), a1 = lds128(aq + 64 * u + 16);
-        const uint32_t dw = lds32(ad + 4 * u);
-        const int pb = mxfp4_block_dot(w, sh, a0, a1);
-        const uint32_t e = (w[0] >> sh) & 0xffu;
-        const float sc = __fmul_rn(h2f((uint16_t)((dw >> dsh) & 0xffffu)), e8m0_half(e));
-        const float z = (float)pb;
-        const float yo = __shfl_xor_sync(0xffffffffu, __fmul_rn(sc, z), xm);
-        sumf = __fadd_rn(sumf, __fmaf_rn(sc, z, yo));
+    for (int i = 0; i < 9; ++i) w[i] = lds32(wp + 4 * i);
+    const uint4 a0 = lds128(ap), a1 = lds128(ap + 16), a2 = lds128(ap + 32), a3 = lds128(ap + 48);
+    // even block: scale at byte sh/8, codes from byte sh/8 + 1; odd block:
+    // scale at byte 17 + sh/8 (word 4), codes from byte 18 + sh/8
+    const int pe = mxfp4_codes_dot<0>(w, sh + 8u, a0, a1);
+    const int po = mxfp4_codes_dot<4>(w, sh + 16u, a2, a3);
+    const float sce = __fmul_rn(h2f((uint16_t)(dw & 0xffffu)), e8m0_half((w[0] >> sh) & 0xffu));
+    const float sco = __fmul_rn(h2f((uint16_t)(dw >> 16)), e8m0_half((w[4] >> (sh + 8u)) & 0xffu));
+    return __fmaf_rn(sce, (float)pe, __fmul_rn(sco, (float)po));
+}
+
+// Where a lane parks the term of pair u: a word strictly inside the pair's
+// own bytes that no other pair's nine-word window touches (windows reach at
+// most two bytes past their pair), so the stage holds the terms once the
+// pair has been read.
+__device__ __forceinline__ float * mxfp4_term_slot(const uint8_t * pr) {
+    const uintptr_t P = reinterpret_cast<uintptr_t>(pr);
+    return reinterpret_cast<float *>(((P + 3) & ~(uintptr_t)3) + 4);
+}
+
+// Part `sub` of a 32-row MXFP4 job (`split` parts): lane r takes row r
+// (base row_r) and the pairs u = sub, sub + split, ... of it, and parks each
+// pair's term in the stage. act(r) is the row's activation row.
+__device__ __forceinline__ void mxfp4_rows_part(const uint8_t * row_r, const uint8_t * act_r, const ActLayout & al,
+                                                int npairs, int sub, int split) {
+    const uint8_t * ad = act_r + al.d_off;
+#pragma unroll 2
+    for (int u = sub; u < npairs; u += split) {
+        const float t = mxfp4_pair_term(row_r + 34 * u, act_r + 64 * u, lds32(ad + 4 * u));
+        *mxfp4_term_slot(row_r + 34 * u) = t;
     }
+}
+
+// The row's dot: its pair terms folded in pair order (the reference chain sumf += t).
+__device__ __forceinline__ float mxfp4_rows_fold(const uint8_t * row_r, int npairs) {
+    float sumf = 0.0f;
+    int u = 0;
+    for (; u + 8 <= npairs; u += 8) {   // eight loads in flight, then the chain
+        float t[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] = *mxfp4_term_slot(row_r + 34 * (u + i));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sumf = __fadd_rn(sumf, t[i]);
+    }
+    for (; u < npairs; ++u) sumf = __fadd_rn(sumf, *mxfp4_term_slot(row_r + 34 * u));
     return sumf;
 }
+
+// async-proxy (bulk copy) writes after generic-proxy accesses of shared memory
+__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Superblocks whose integer parts a lane computes before their exchanges and
 // float chain (Q4_K rows), and whether Q6_K rows go by superblock pairs.
@@ -735,7 +773,8 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
             bool ok = false;
             for (uint32_t i = 0; i < (1u << 23) && !ok; ++i) {
                 ok = bufdone[bi] >= iss[bi];
-                if (!ok && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+                if (!ok && (i & 63u) == 63u && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
+                if (!ok && i >= 16) __nanosleep(64);
             }
             if (ok) ok = kind == 0 ? stack_wait(p.q_done + J.L, 1) : stack_wait(p.gu_done + K, blocks_per_token);
             if (!ok) {
@@ -767,7 +806,8 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
 }
 
 template <int TG, int TD>
-__global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWarps, 1) k_stack(const __grid_constant__ StackParams p) {
+__global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_warps(TG == GX_T_MXFP4 ? 3 : 0), 1)
+    k_stack(const __grid_constant__ StackParams p) {
     // row mode: 0 two-lane Q8_0 rows, 2 two-lane Q4_K gate/up + Q6_K down rows, 1 octet rows
     constexpr int kMode = (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0
                           : (TG == GX_T_Q4_K && TD == GX_T_Q6_K) ? 2
@@ -979,29 +1019,33 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
         if (J.gu) {
             const uint8_t * xa = xbuf + bi * xbytes;
             if constexpr (kMode == 3) {
-                // part `sub` of a 16+16-row job: lane = 2r + gp, row r < 8 is gate
-                // row 8*sub + r (tile 0), row r >= 8 is up row 8*sub + r - 8 (tile 1)
-                const int r = lane >> 1, gp = lane & 1;
-                const int gr = 8 * sub + (r & 7);
-                const uint8_t * row = st + p.gu_tile[r >> 3] + gr * (int)p.nb01_g;
-                const float dot = mxfp4_row2(row, xa, p.alx, gp, p.H / 64, 1);
+                // 16 gate rows (tile 0) + 16 up rows (tile 1): lane r takes row r;
+                // part `sub` computes pairs sub, sub + split, ... and parks their terms
+                const uint8_t * row = st + p.gu_tile[lane >> 4] + (lane & 15) * (int)p.nb01_g;
+                mxfp4_rows_part(row, xa, p.alx, p.H / 64, sub, split);
+                __syncwarp();
+                int lastp = 0;
+                if (lane == 0) {
+                    __threadfence_block();
+                    lastp = atomicAdd(parts + cs, 1) == split - 1;
+                    if (lastp) __threadfence_block();
+                }
+                if (!__shfl_sync(0xffffffffu, lastp, 0)) continue;   // the last part folds and runs the epilogue
+                const float dot = mxfp4_rows_fold(row, p.H / 64);
+                fence_proxy_async_shared();   // terms written into the stage before its refill
                 __syncwarp();
                 if (lane == 0) {
-                    // the job's last part frees the stage and the input buffer
+                    parts[cs] = 0;
                     __threadfence_block();
-                    if (atomicAdd(parts + cs, 1) == split - 1) {
-                        parts[cs] = 0;
-                        __threadfence_block();
-                        atomicAdd(done, 1);
-                        atomicAdd(rel + cs, 1);
-                        mbar_arrive(empty + cs);
-                    }
+                    atomicAdd(done, 1);
+                    atomicAdd(rel + cs, 1);
+                    mbar_arrive(empty + cs);
                 }
-                // gate row gr (lane 2r, r < 8) pairs with up row gr (lane 2r + 16)
+                // gate row r (lane r < 16) pairs with up row r (lane r + 16)
                 const float up = __shfl_down_sync(0xffffffffu, dot, 16);
-                if (gp == 0 && r < 8) {
+                if (lane < 16) {
                     const float a = p.act == 1 ? act_swiglu_oai(dot, up, p.alpha, p.limit) : act_swiglu(dot, up);
-                    ly.act[(int64_t)J.pair * p.I + J.r0 + gr] = a;
+                    ly.act[(int64_t)J.pair * p.I + J.r0 + lane] = a;
                 }
             } else if constexpr (kMode != 1) {
                 // lane = qr*8 + tile*2 + gp: row qr of tile `tile` (gate rows 4*tile+qr
@@ -1077,7 +1121,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
             if (lane == 0) {
                 fence_acq_rel_gpu();
                 last = atomicAdd(ly.cnt + J.pair * nblk + blk, 1) ==
-                       (kMode == 1 || kMode == 3 ? split : 1) * (p.qblk / p.Rg) - 1;
+                       (kMode == 1 ? split : 1) * (p.qblk / p.Rg) - 1;
             }
             if (__shfl_sync(0xffffffffu, last, 0)) {
                 // this job finished the Q8 block last: quantize it and count the
@@ -1121,6 +1165,39 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                 }
             }
             __syncwarp();
+        } else if constexpr (kMode == 3) {
+            // k*Rd = 32 weight rows (row r: row r % Rd of expert r / Rd): lane r
+            // takes row r against its expert's activation row
+            const uint8_t * da = dbuf + bi * dbytes;
+            const uint8_t * row = st + lane * p.pitch_d;
+            mxfp4_rows_part(row, da + (lane / p.Rd) * p.ald.pitch, p.ald, p.I / 64, sub, split);
+            __syncwarp();
+            int lastp = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                lastp = atomicAdd(parts + cs, 1) == split - 1;
+                if (lastp) __threadfence_block();
+            }
+            if (!__shfl_sync(0xffffffffu, lastp, 0)) continue;
+            const float dot = mxfp4_rows_fold(row, p.I / 64);
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+                parts[cs] = 0;
+                __threadfence_block();
+                atomicAdd(done, 1);
+                atomicAdd(rel + cs, 1);
+                mbar_arrive(empty + cs);
+            }
+            // output row rr = lane < Rd: sum over slots m of w[m] * dot(m*Rd + rr), in slot order
+            const float * wr = ly.rw + (int64_t)J.t * p.k;
+            float accf = 0.0f;
+            for (int mm = 0; mm < p.k; ++mm) {
+                const float v = __shfl_sync(0xffffffffu, dot, (mm * p.Rd + lane) & 31);
+                const float prod = __fmul_rn(v, lane < p.Rd ? wr[mm] : 0.0f);
+                accf = mm == 0 ? prod : __fadd_rn(accf, prod);
+            }
+            if (lane < p.Rd) ly.out[(int64_t)J.t * p.H + J.r0 + lane] = accf;
         } else {
             // lane = par*16 + q: weight rows q and q+16 of the job's k*Rd rows
             // (row R is row R % Rd of expert R / Rd); eight consecutive lanes
@@ -1153,12 +1230,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * kStackMaxWar
                     const int R = q + 16 * sub;
                     const uint8_t * ar = da + (R / p.Rd) * p.ald.pitch;
                     float dd, unused;
-                    if constexpr (kMode == 3) {
-                        dd = mxfp4_row2(st + R * p.pitch_d, ar, p.ald, par, p.I / 64, 16);
-                        unused = 0.0f;
-                    } else {
-                        q6k_rows2<1>(st + R * p.pitch_d, st, ar, ar, p.ald, par, p.I / 256, 16, dd, unused);
-                    }
+                    q6k_rows2<1>(st + R * p.pitch_d, st, ar, ar, p.ald, par, p.I / 256, 16, dd, unused);
                     float * dts = sdots + cs * 32;
                     if (par == 0) dts[R] = dd;
                     __syncwarp();

@@ -239,6 +239,34 @@ class Arena:
                 "gx_moe_layer_forward")
         return st
 
+    def layer_forward_shared(self, layer: int, x, ids: np.ndarray, w, shared: "L.gx_shared_expert", out,
+                             stream=None) -> L.gx_serve_stats:
+        """layer_forward plus a shared expert: out = moe_out + shexp(x)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        T, k = ids.shape
+        st = L.gx_serve_stats()
+        L.check(self._lib.gx_moe_layer_forward_shared(self.h, layer, C.byref(self.desc), _ptr(x), ids.ctypes.data,
+                                                      _ptr(w), k, T, C.byref(shared), _ptr(out), _stream(stream),
+                                                      C.byref(st)), "gx_moe_layer_forward_shared")
+        return st
+
+
+def shared_expert(record, type_gate: int, type_down: int, hidden: int, intermediate: int,
+                  act: int = L.ACT_SWIGLU) -> L.gx_shared_expert:
+    """A shared expert whose record (down | gate | up, 16-byte aligned roles)
+    lies at device address `record`."""
+    down = L.row_bytes(type_down, intermediate) * hidden
+    gate = L.row_bytes(type_gate, hidden) * intermediate
+    off_gate = (down + 15) // 16 * 16
+    off_up = (off_gate + gate + 15) // 16 * 16
+    d = L.gx_layer_desc(type_gate, type_gate, type_down, act, 1.702, 7.0, hidden, intermediate, off_gate, off_up)
+    return L.gx_shared_expert(_ptr(record), d)
+
+
+def shared_record_bytes(type_gate: int, type_down: int, hidden: int, intermediate: int) -> int:
+    sh = shared_expert(0, type_gate, type_down, hidden, intermediate)
+    return sh.desc.off_up + L.row_bytes(type_gate, hidden) * intermediate
+
 
 class StackCall:
     """A prepared gx_moe_stack_forward call: fixed device pointers per layer,
@@ -417,6 +445,22 @@ class ExpertParallel:
                                                     _ptr(w), k, T, _ptr(out), _stream(stream), C.byref(self.st)),
                 "gx_ep_layer_forward")
         return self.st
+
+    def stack_forward(self, first_layer: int, x_ptrs, ids: np.ndarray, w_ptrs, out_ptrs, stream=None,
+                      check: bool = True):
+        """n consecutive layers in one step: x_ptrs / w_ptrs / out_ptrs lists of
+        n device addresses ([T, H], [T, k], [T, H]); ids HOST int32 [n, T, k]
+        global expert ids. Returns (status, stats); raises on error if check."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        n, T, k = ids.shape
+        xs = (C.c_void_p * n)(*[_ptr(p) for p in x_ptrs])
+        ws = (C.c_void_p * n)(*[_ptr(p) for p in w_ptrs])
+        os_ = (C.c_void_p * n)(*[_ptr(p) for p in out_ptrs])
+        rc = self.arena._lib.gx_ep_stack_forward(self.h, first_layer, n, C.byref(self.arena.desc), xs, ids.ctypes.data,
+                                                 ws, k, T, os_, _stream(stream), C.byref(self.st))
+        if check:
+            L.check(rc, "gx_ep_stack_forward")
+        return rc, self.st
 
     def close(self):
         if getattr(self, "h", None):

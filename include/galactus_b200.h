@@ -256,7 +256,11 @@ int gx_expf(const float * x, float * y, int64_t n, void * stream);
  *   remap (policy + miss copies) -> gate/up mul_mat_id + activation
  *   -> down mul_mat_id -> weighted combine in slot order.
  * x: device f32 [H, T]; ids: HOST i32 [k, T] (contiguous); w: device f32 [k, T];
- * out: device f32 [H, T]. Record layout down | gate | up (offsets below). */
+ * out: device f32 [H, T]. Record layout down | gate | up (offsets below).
+ * A micro-batch whose distinct experts exceed the policy's batch bound
+ * min(quota, probation) (the reference's micro-batch rule,
+ * src/h4/h4-expert-cache.cpp:105-124) runs in expert-major waves of at most
+ * that many experts; the output bits do not depend on the wave schedule. */
 typedef struct gx_layer_desc {
     int32_t type_gate;
     int32_t type_up;
@@ -273,6 +277,25 @@ typedef struct gx_layer_desc {
 int gx_moe_layer_forward(gx_arena * arena, uint32_t layer, const gx_layer_desc * desc,
                          const float * x, const int32_t * ids, const float * w, int64_t k, int64_t T,
                          float * out, void * stream, gx_serve_stats * stats);
+
+/* The shared expert of a layer (DeepSeek-style MoE: one dense FFN every token
+ * runs with weight 1 beside the routed experts): one record in the routed
+ * layout (down | gate | up at desc's offsets), resident in device memory and
+ * owned by the caller. */
+typedef struct gx_shared_expert {
+    const void * record;      /* device address of the record */
+    gx_layer_desc desc;       /* its types (e.g. Q4_K), hidden = the layer's H, intermediate, offsets */
+} gx_shared_expert;
+
+/* gx_moe_layer_forward plus the shared expert: out = moe_out + shexp(x), the
+ * ggml_add(moe_out, ffn_shexp) that follows build_moe_ffn in upstream
+ * llama.cpp (the tail the routed output feeds, diff:2153-2191); shexp is
+ * silu(x W_gate) * (x W_up) W_down with ggml's mul_mat order per row.
+ * The shared intermediate may not exceed k * the routed intermediate. */
+int gx_moe_layer_forward_shared(gx_arena * arena, uint32_t layer, const gx_layer_desc * desc,
+                                const float * x, const int32_t * ids, const float * w, int64_t k, int64_t T,
+                                const gx_shared_expert * shared, float * out, void * stream,
+                                gx_serve_stats * stats);
 
 /* A stack of consecutive MoE layers for one micro-batch whose routes are all
  * known (the reference's "token" serving regime, src/h4/h4-expert-store.hpp:
@@ -475,8 +498,9 @@ int gx_ep_init(gx_arena * local_arena, void * nccl_comm, int32_t rank, int32_t w
                int32_t placement, gx_ep ** ep);
 int gx_ep_destroy(gx_ep * ep);
 /* dispatch: x device f32 [T, H]; ids HOST i32 [T, k] of global expert ids.
- * Synchronizes the stream once (the peers' pair counts and expert ids are
- * needed on the host for the slot policy). */
+ * Synchronizes the stream twice: the ranks' shapes and statuses (a call one
+ * rank rejects fails on every rank), then the peers' pair counts and expert
+ * ids (needed on the host for the slot policy). */
 int gx_ep_dispatch(gx_ep * ep, uint32_t layer, const float * x, const int32_t * ids, int64_t k, int64_t T, int64_t H,
                    void * stream);
 /* compute: the pairs received by the last dispatch, on the local arena */
@@ -486,6 +510,17 @@ int gx_ep_combine(gx_ep * ep, const float * w, float * out, void * stream);
 /* the three in sequence */
 int gx_ep_layer_forward(gx_ep * ep, uint32_t layer, const gx_layer_desc * desc, const float * x, const int32_t * ids,
                         const float * w, int64_t k, int64_t T, float * out, void * stream, gx_serve_stats * stats);
+/* n_layers consecutive layers whose routes are all known (the stack regime of
+ * gx_moe_stack_forward) in one step: x, w, out arrays of n_layers device
+ * pointers ([T, H], [T, k], [T, H]); ids HOST i32 [n_layers, T, k] of global
+ * expert ids. Two host synchronizations per step (the shape and id headers,
+ * whatever n_layers), one row exchange and one result exchange for all
+ * layers; the owners compute layer by layer without synchronizing. Every rank
+ * must pass the same first_layer, n_layers, k and H; T may differ. A call one
+ * rank rejects fails on every rank before any row moves. */
+int gx_ep_stack_forward(gx_ep * ep, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * desc,
+                        const float * const * x, const int32_t * ids, const float * const * w, int64_t k, int64_t T,
+                        float * const * out, void * stream, gx_serve_stats * stats);
 
 /* ------------------------------------------------------------- synthetic
  * Seeded synthetic data written straight into device memory (test and bench

@@ -523,10 +523,17 @@ void orc_expf_many(const float * x, float * y, int64_t n) {
 
 // ------------------------------------------------------------ activations
 
+// The exp inside the activations: this library's orc_expf (the default, the
+// one the device shares) or the host C library's expf (orc_act_exp_libm(1)),
+// for measuring how far layer outputs move when the exp is swapped.
+static std::atomic<int> g_act_exp_libm{0};
+void orc_act_exp_libm(int on) { g_act_exp_libm.store(on ? 1 : 0); }
+static inline float act_exp(float x) { return g_act_exp_libm.load(std::memory_order_relaxed) ? std::exp(x) : orc_expf(x); }
+
 // SwiGLU as ggml's scalar CPU form: silu(g) * u with silu(g) = g / (1 + exp(-g))
 void orc_swiglu(const float * g, const float * u, float * out, int64_t n) {
     for (int64_t i = 0; i < n; ++i) {
-        const float s = g[i] / (1.0f + orc_expf(-g[i]));
+        const float s = g[i] / (1.0f + act_exp(-g[i]));
         out[i] = s * u[i];
     }
 }
@@ -538,7 +545,7 @@ void orc_swiglu_oai(const float * g, const float * u, float * out, int64_t n, fl
     for (int64_t i = 0; i < n; ++i) {
         const float x = limit < g[i] ? limit : g[i];
         const float y = u[i] < -limit ? -limit : (limit < u[i] ? limit : u[i]);
-        const float glu = x / (1.0f + orc_expf(alpha * (-x)));
+        const float glu = x / (1.0f + act_exp(alpha * (-x)));
         out[i] = glu * (y + 1.0f);
     }
 }

@@ -135,6 +135,12 @@ def expf(x: np.ndarray) -> np.ndarray:
     return y
 
 
+def act_exp_libm(on: bool) -> None:
+    """Swap the exp inside the oracle's activations for the C library's expf
+    (True) or back to the shared one (False)."""
+    lib().orc_act_exp_libm(1 if on else 0)
+
+
 def swiglu(g, u):
     g = np.ascontiguousarray(g, dtype=np.float32); u = np.ascontiguousarray(u, dtype=np.float32)
     out = np.empty_like(g)

@@ -201,8 +201,10 @@ def _nccl_rank(rank, world, port, name, placement, T, result_q):
         owned = [e for e in range(m.experts) if (e % world if placement == 0 else e // ((m.experts + world - 1) // world)) == rank]
         # the local arena: this rank's experts only, every one resident
         lm = ModelShape(**{**m.__dict__, "experts": len(owned), "used": min(m.used, len(owned))})
-        arena = gx.Arena(lm, capacity_bytes=len(owned) * m.record * m.layers, policy=gx.POLICY_AUTO,
-                         max_tokens=world * T * m.used, device=rank)
+        # the local arena: this rank's experts, a cache of 4 slots per layer
+        # (the owners run the received pairs in waves when they do not fit)
+        arena = gx.Arena(lm, capacity_bytes=4 * m.record * m.layers, policy=gx.POLICY_AUTO,
+                         max_tokens=world * (T + 2 * world) * m.used, device=rank)
         for L in range(m.layers):
             for li, e in enumerate(owned):
                 arena.load_record(L, li, orc.synth_record(m, m.seed, L, e))
@@ -222,6 +224,26 @@ def _nccl_rank(rank, world, port, name, placement, T, result_q):
                 got = out.cpu().numpy()
                 want = orc.moe_layer(m, recs[L], x, ids, w)
                 good = good and bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+        # both layers in one step, each rank with its own token count
+        Tr = T + 1 + 2 * rank
+        xs, ids_s, ws = zip(*[_rank_inputs(m, rank, Tr, seed=900 + L) for L in range(m.layers)])
+        xd = [torch.from_numpy(v).to(dev) for v in xs]
+        wd = [torch.from_numpy(v).to(dev) for v in ws]
+        outs = [torch.full((Tr, m.hidden), float("nan"), device=dev) for _ in range(m.layers)]
+        ep.stack_forward(0, xd, np.stack(ids_s), wd, outs, stream)
+        for L in range(m.layers):
+            want = orc.moe_layer(m, recs[L], xs[L], ids_s[L], ws[L])
+            good = good and bool(np.array_equal(outs[L].cpu().numpy().view(np.uint32), want.view(np.uint32)))
+        # a call that rank 1 rejects (an expert id out of range) fails on every
+        # rank with the same status, and the next step runs normally
+        bad = np.stack(ids_s).copy()
+        if rank == 1:
+            bad[0, 0, 0] = m.experts + 5
+        rc, _ = ep.stack_forward(0, xd, bad, wd, outs, stream, check=False)
+        good = good and rc == gx.GX_ERR_DOMAIN
+        ep.stack_forward(0, xd, np.stack(ids_s), wd, outs, stream)
+        want = orc.moe_layer(m, recs[1], xs[1], ids_s[1], ws[1])
+        good = good and bool(np.array_equal(outs[1].cpu().numpy().view(np.uint32), want.view(np.uint32)))
         from galactus_b200.moe import device_error
         good = good and device_error() == 0
         ep.close()
@@ -235,9 +257,12 @@ def _nccl_rank(rank, world, port, name, placement, T, result_q):
 @pytest.mark.gpu
 @pytest.mark.parametrize("name,placement", [("qwen3-30b", 0), ("qwen3-235b", 1)])
 def test_ep_nccl_two_gpus(gxlib, name, placement):
-    """gx_ep_layer_forward over two GPUs (NCCL send/recv on torch's
-    communicator): every rank's outputs are the one-process oracle layer's
-    bits, for two layers, three steps, with pairs local and remote."""
+    """gx_ep_layer_forward and gx_ep_stack_forward over two GPUs (NCCL
+    send/recv on torch's communicator): every rank's outputs are the
+    one-process oracle layer's bits, for two layers, three steps, pairs local
+    and remote, owners running waves through a 4-slot cache, ranks with
+    different token counts; a call one rank rejects fails on both ranks with
+    the same status and the next step runs."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -253,3 +278,52 @@ def test_ep_nccl_two_gpus(gxlib, name, placement):
     for p in procs:
         p.join(timeout=120)
     assert all(ok for _, ok in res), res
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["qwen3-235b", "deepseek-v3"])
+def test_ep_one_rank_stack_step(gxlib, orc, dev, name):
+    """The expert-parallel step on one GPU (no communicator: the exchanges are
+    local copies): gx_ep_stack_forward over three layers through a small slot
+    cache (waves) equals the oracle layers bit for bit, and a rejected call
+    returns its status and leaves the next step intact."""
+    import torch
+    from galactus_b200.models import ModelShape
+    from galactus_b200.moe import ExpertParallel, device_error
+    base = gxlib.MODELS[name]
+    m = ModelShape(**{**base.__dict__, "experts": 16, "layers": 3})
+    T, k = 4, m.used
+    arena = gxlib.Arena(m, capacity_bytes=(k + 2) * m.record * m.layers, policy=gxlib.POLICY_AUTO,
+                        max_tokens=T * k)
+    try:
+        recs = [np.stack([orc.synth_record(m, m.seed, L, e) for e in range(m.experts)]) for L in range(m.layers)]
+        for L in range(m.layers):
+            for e in range(m.experts):
+                arena.load_record(L, e, recs[L][e])
+        ep = ExpertParallel(arena, 0, 0, 1, m.experts, 0)
+        stream = torch.cuda.current_stream()
+        rng = np.random.default_rng(11)
+        for step in range(3):
+            ids = np.stack([np.stack([rng.choice(m.experts, k, replace=False) for _ in range(T)])
+                            for _ in range(m.layers)]).astype(np.int32)
+            w = rng.random((m.layers, T, k)).astype(np.float32)
+            x = rng.standard_normal((m.layers, T, m.hidden)).astype(np.float32)
+            xd, wd = torch.from_numpy(x).to(dev), torch.from_numpy(w).to(dev)
+            out = torch.full((m.layers, T, m.hidden), float("nan"), device=dev)
+            ep.stack_forward(0, [xd[L] for L in range(m.layers)], ids, [wd[L] for L in range(m.layers)],
+                             [out[L] for L in range(m.layers)], stream)
+            got = out.cpu().numpy()
+            for L in range(m.layers):
+                want = orc.moe_layer(m, recs[L], x[L], ids[L], w[L])
+                np.testing.assert_array_equal(got[L].view(np.uint32), want.view(np.uint32), err_msg=f"step {step} L {L}")
+            if step == 1:
+                bad = ids.copy()
+                bad[2, 1, 0] = -3
+                rc, _ = ep.stack_forward(0, [xd[L] for L in range(m.layers)], bad, [wd[L] for L in range(m.layers)],
+                                         [out[L] for L in range(m.layers)], stream, check=False)
+                assert rc == gxlib.GX_ERR_DOMAIN
+        assert arena.stats()["misses"] > 0
+        assert device_error() == 0
+        ep.close()
+    finally:
+        arena.close()
