@@ -2,6 +2,7 @@
 // tier, the remap node, the expert kernels and the MoE layer entry point.
 // No C++ exception crosses this boundary; every entry point returns GX_*.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cstdio>
@@ -184,6 +185,10 @@ struct gx_arena {
     float * d_wfull = nullptr;          // [pairs, H] the same in (token, slot) order
     float * d_ones = nullptr;           // [pairs] 1.0f
     float * d_shy = nullptr;            // [max_tokens, H] shared-expert output
+    // tensor-core prefill: masked B tiles and block scales of every pair chunk
+    uint8_t * d_mmab = nullptr;
+    float * d_mmady = nullptr;
+    size_t mmab_cap = 0;                // chunk-blocks the buffers hold
     int32_t * d_widx = nullptr;         // [2, pairs] token of each wave-order pair | its pair index
     int32_t * h_widx = nullptr;         // pinned staging of d_widx
     cudaEvent_t ev_widx = nullptr;
@@ -329,6 +334,8 @@ int gx_arena_destroy(gx_arena * a) {
     if (a->d_wy) cudaFree(a->d_wy);
     if (a->d_wfull) cudaFree(a->d_wfull);
     if (a->d_shy) cudaFree(a->d_shy);
+    if (a->d_mmab) cudaFree(a->d_mmab);
+    if (a->d_mmady) cudaFree(a->d_mmady);
     if (a->d_ones) cudaFree(a->d_ones);
     if (a->d_widx) cudaFree(a->d_widx);
     if (a->h_widx) cudaFreeHost(a->h_widx);
@@ -948,6 +955,51 @@ void enqueue_layer(const LayerPlan & lp, const float * x, const float * w, float
 // every expert's rows are read once per layer instead of once per pair.
 constexpr int64_t kGroupedPairs = 128;
 
+// cuTensorMapEncodeTiled from the driver, resolved once through the runtime
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void * f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// Weight rows of every slot of a layer as a 3-D tensor of 16-bit words
+// (x: word of a row, y: row, z: slot), boxes of 136 words (8 Q8_0 blocks)
+// by box_rows rows.
+bool encode_rows_map(CUtensorMap * map, const void * base, int64_t nb01, int64_t rows, int64_t slots, int64_t nb02,
+                     uint32_t box_rows) {
+    const auto enc = tensor_map_encoder();
+    if (enc == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u) != 0 || nb01 % 16 != 0 || nb02 % 16 != 0) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)(nb01 / 2), (cuuint64_t)rows, (cuuint64_t)slots};
+    const cuuint64_t strides[2] = {(cuuint64_t)nb01, (cuuint64_t)nb02};
+    const cuuint32_t box[3] = {136u, box_rows, 1u};
+    const cuuint32_t elem[3] = {1u, 1u, 1u};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void *>(base), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The tensor-core prefill replaces the CUDA-core grouped kernels when the
+// weights are Q8_0 and the micro-batch has at least this many pairs per
+// touched expert on average (below it most of an MMA's 16-pair columns
+// would be padding).
+constexpr int64_t kMmaPairsPerExpert = 4;
+
+bool use_mma(const LayerPlan & lp, int64_t pairs, int64_t experts_touched) {
+    if (const char * env = std::getenv("GX_PREFILL_MMA")) {
+        if (env[0] == '0') return false;
+    }
+    // the up rows must follow the gate rows in the record (one tensor for both)
+    return gx::prefill_mma_supported(lp.type_gate, lp.type_down, lp.H, lp.I) &&
+           lp.g.w1 == lp.g.w0 + lp.I * lp.g.nb01 && tensor_map_encoder() != nullptr &&
+           pairs >= kMmaPairsPerExpert * std::max<int64_t>(1, experts_touched);
+}
+
 bool use_grouped(const LayerPlan & lp, int64_t pairs) {
     if (const char * env = std::getenv("GX_GROUPED")) {
         if (env[0] == '0') return false;
@@ -966,7 +1018,8 @@ void prefill_layer(gx_arena * a, const LayerPlan & lp, const float * x, const in
     // grouping: counting sort of the pairs by slot
     const int64_t slots_used = std::min<int64_t>(P, n_as);
     const int64_t units_max = slots_used * (I / 8 + H / 16);
-    const size_t need = (size_t)(n_as + 1) + 3 * (size_t)P + 4 * (size_t)units_max;
+    const int64_t chunks_max = P / gx::kMmaTok + slots_used;
+    const size_t need = (size_t)(n_as + 1) + 3 * (size_t)P + 4 * (size_t)units_max + 3 * (size_t)chunks_max;
     if (need > a->grp_cap) {
         if (a->h_grp) {
             ck(cudaEventSynchronize(a->ev_grp));
@@ -1002,8 +1055,21 @@ void prefill_layer(gx_arena * a, const LayerPlan & lp, const float * x, const in
         src_pair[j] = (int32_t)i;
         dst[j] = (int32_t)i;
     }
-    int32_t ng = 0, nd = 0;
+    int32_t * c_slot = u_row_d + units_max;
+    int32_t * c_first = c_slot + chunks_max;
+    int32_t * c_count = c_first + chunks_max;
+    int32_t nchunks = 0, touched = 0;
     for (int32_t e = 0; e < n_as; ++e) {
+        if (seg[e + 1] > seg[e]) ++touched;
+        for (int32_t f = seg[e]; f < seg[e + 1]; f += gx::kMmaTok) {
+            c_slot[nchunks] = e;
+            c_first[nchunks] = f;
+            c_count[nchunks++] = std::min<int32_t>(gx::kMmaTok, seg[e + 1] - f);
+        }
+    }
+    const bool mma = use_mma(lp, P, touched);
+    int32_t ng = 0, nd = 0;
+    for (int32_t e = 0; e < n_as && !mma; ++e) {
         if (seg[e + 1] == seg[e]) continue;
         for (int64_t r = 0; r < I; r += 8) {
             u_slot_g[ng] = e;
@@ -1024,8 +1090,74 @@ void prefill_layer(gx_arena * a, const LayerPlan & lp, const float * x, const in
     const int32_t * durg = dusg + units_max;
     const int32_t * dusd = durg + units_max;
     const int32_t * durd = dusd + units_max;
+    const int32_t * dcs = durd + units_max;
+    const int32_t * dcf = dcs + chunks_max;
+    const int32_t * dcc = dcf + chunks_max;
 
     ck(gx::launch_quant_split(gx::GX_T_Q8_0, x, (int)H, T, H * 4, a->d_xq, s, false));
+    if (mma) {
+        // tensor cores: masked B tiles of the layer input per chunk, gate/up
+        // units (64 gate + 64 up rows x 16 pairs), the activation quantized,
+        // masked B tiles of it, down units (128 rows x 16 pairs), combine
+        const int64_t nbh = H / 32, nbi = I / 32, nbmax = std::max(nbh, nbi);
+        const size_t want = (size_t)chunks_max * (size_t)nbmax;
+        if (want > a->mmab_cap) {
+            if (a->d_mmab) cudaFree(a->d_mmab);
+            if (a->d_mmady) cudaFree(a->d_mmady);
+            a->d_mmab = nullptr;
+            a->d_mmady = nullptr;
+            a->mmab_cap = 0;
+            ck(cudaMalloc(&a->d_mmab, want * (size_t)(gx::kMmaN * 32)));
+            ck(cudaMalloc(&a->d_mmady, want * (size_t)gx::kMmaTok * sizeof(float)));
+            a->mmab_cap = want;
+        }
+        gx::MmaPrepParams bp{};
+        bp.chunk_first = dcf;
+        bp.chunk_count = dcc;
+        bp.pair_src = dtok;
+        bp.aq = a->d_xq;
+        bp.al = lp.g.al;
+        bp.nblk = (int32_t)nbh;
+        bp.btiles = a->d_mmab;
+        bp.dyt = a->d_mmady;
+        ck(gx::launch_mma_bprep(bp, nchunks, s));
+        gx::MmaParams mp{};
+        if (!encode_rows_map(&mp.tmap, lp.g.w0, lp.g.nb01, 2 * I, n_as, lp.g.nb02, 64u))
+            throw PolicyError(GX_ERR_ALIGN, "gate/up tensor map");
+        mp.up_row0 = (int32_t)I;
+        mp.nb01 = lp.g.nb01;
+        mp.nblk = (int32_t)nbh;
+        mp.n_rt = (int32_t)(I / 64);
+        mp.chunk_slot = dcs;
+        mp.chunk_first = dcf;
+        mp.chunk_count = dcc;
+        mp.pair_dst = ddst;
+        mp.btiles = a->d_mmab;
+        mp.dyt = a->d_mmady;
+        mp.out = a->d_act;
+        mp.out_ld = I;
+        mp.act = lp.g.act;
+        mp.alpha = lp.g.alpha;
+        mp.limit = lp.g.limit;
+        ck(gx::launch_prefill_mma(0, mp, nchunks * mp.n_rt, s));
+        ck(gx::launch_quant_split(gx::GX_T_Q8_0, a->d_act, (int)I, P, I * 4, a->d_actq, s, false));
+        bp.pair_src = dpair;
+        bp.aq = a->d_actq;
+        bp.al = lp.dn.al;
+        bp.nblk = (int32_t)nbi;
+        ck(gx::launch_mma_bprep(bp, nchunks, s));
+        if (!encode_rows_map(&mp.tmap, lp.dn.w0, lp.dn.nb01, H, n_as, lp.dn.nb02, (uint32_t)gx::kMmaRows))
+            throw PolicyError(GX_ERR_ALIGN, "down tensor map");
+        mp.up_row0 = 0;
+        mp.nb01 = lp.dn.nb01;
+        mp.nblk = (int32_t)nbi;
+        mp.n_rt = (int32_t)(H / gx::kMmaRows);
+        mp.out = a->d_y;
+        mp.out_ld = H;
+        ck(gx::launch_prefill_mma(1, mp, nchunks * mp.n_rt, s));
+        ck(gx::launch_combine(a->d_y, w, out, H, (int)k, T, s));
+        return;
+    }
     gx::PrefillParams g{};
     g.w0 = lp.g.w0;
     g.w1 = lp.g.w1;

@@ -24,6 +24,7 @@
 #include "gx_stack.cuh"
 #include "gx_prefill.cuh"
 #include "gx_router.cuh"
+#include "gx_mma.cuh"
 
 namespace gx {
 
@@ -908,6 +909,35 @@ static cudaError_t launch_prefill_t(const PrefillParams & p, uint32_t smem, cuda
     if (p.n_units <= 0) return cudaSuccess;
     k_prefill<MODE><<<p.n_units, 32 * kPrefillWarps, smem, stream>>>(p);
     return cudaGetLastError();
+}
+
+cudaError_t launch_mma_bprep(const MmaPrepParams & p, int n_chunks, cudaStream_t stream) {
+    if (n_chunks <= 0) return cudaSuccess;
+    k_mma_bprep<<<dim3((unsigned)p.nblk, (unsigned)n_chunks), kMmaN, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <int MODE>
+static cudaError_t launch_prefill_mma_t(const MmaParams & p, int n_units, cudaStream_t stream) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(k_prefill_mma<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)MmaSmem::total);
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    k_prefill_mma<MODE><<<(unsigned)n_units, kMmaThreads, MmaSmem::total, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_mma(int mode, const MmaParams & p, int n_units, cudaStream_t stream) {
+    if (n_units <= 0) return cudaSuccess;
+    return mode == 0 ? launch_prefill_mma_t<0>(p, n_units, stream) : launch_prefill_mma_t<1>(p, n_units, stream);
+}
+
+bool prefill_mma_supported(int type_gate, int type_down, int64_t H, int64_t I) {
+    return type_gate == GX_T_Q8_0 && type_down == GX_T_Q8_0 && H % 256 == 0 && I % 256 == 0 && H <= 32 * kMmaMaxBlocks &&
+           I <= 32 * kMmaMaxBlocks && I % 64 == 0 && H % kMmaRows == 0;
 }
 
 cudaError_t launch_prefill(int mode, const PrefillParams & p, uint32_t smem, cudaStream_t stream) {

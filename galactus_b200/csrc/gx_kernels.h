@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "gx_formats.h"
@@ -179,6 +180,47 @@ struct PrefillParams {
 
 uint32_t prefill_layout(PrefillParams & p);
 cudaError_t launch_prefill(int mode, const PrefillParams & p, uint32_t smem, cudaStream_t stream);
+
+// Tensor-core prefill (gx_mma.cuh): pair chunks of <= 16 pairs of one expert.
+constexpr int kMmaRows = 128;          // weight rows per unit (MMA M)
+constexpr int kMmaTok = 16;            // (token, slot) pairs per chunk
+constexpr int kMmaN = 4 * kMmaTok;     // MMA N: four lane copies per pair
+constexpr int kMmaMaxBlocks = 64;      // Q8_0 blocks per row at most (K <= 2048)
+struct MmaPrepParams {
+    const int32_t * chunk_first;   // [chunks] first sorted-pair index
+    const int32_t * chunk_count;   // [chunks] pairs in the chunk (<= 16)
+    const int32_t * pair_src;      // [P] activation row of each sorted pair
+    const uint8_t * aq;            // activation rows (Q8_0 split layout)
+    ActLayout al;
+    int32_t nblk;                  // Q8_0 blocks per activation row
+    uint8_t * btiles;              // [chunks][nblk][64 x 32] masked B tiles
+    float * dyt;                   // [chunks][nblk][16] block scales
+};
+struct MmaParams {
+    // weight rows of every slot as a 3-D tensor of 16-bit words: x = word in
+    // the row (nb01 / 2), y = row (MODE 0: the I gate rows then the I up rows,
+    // contiguous in the record; MODE 1: the H down rows), z = slot; boxes of
+    // 136 words (8 Q8_0 blocks) x 64 (MODE 0) or 128 (MODE 1) rows
+    CUtensorMap tmap;
+    int32_t up_row0;               // MODE 0: row of up row 0 in the tensor (I)
+    int64_t nb01;                  // row bytes
+    int32_t nblk;                  // Q8_0 blocks per weight row (a multiple of 8, at most 64)
+    int32_t n_rt;                  // row tiles per chunk (units = chunks * n_rt)
+    const int32_t * chunk_slot;    // [chunks]
+    const int32_t * chunk_first;   // [chunks]
+    const int32_t * chunk_count;   // [chunks]
+    const int32_t * pair_dst;      // [P] output row of each sorted pair
+    const uint8_t * btiles;
+    const float * dyt;
+    float * out;                   // MODE 0: act [P, I]; MODE 1: y [P, H]
+    int64_t out_ld;
+    int32_t act;
+    float alpha, limit;
+};
+cudaError_t launch_mma_bprep(const MmaPrepParams & p, int n_chunks, cudaStream_t stream);
+cudaError_t launch_prefill_mma(int mode, const MmaParams & p, int n_units, cudaStream_t stream);
+// the tensor-core prefill's constraints: Q8_0 weights and activations, K a multiple of 256 (8 blocks) up to 2048
+bool prefill_mma_supported(int type_gate, int type_down, int64_t H, int64_t I);
 
 uint32_t stack_layout(StackParams & p, int & threads);
 bool stack_types_supported(int type_gate, int type_down);

@@ -1,0 +1,482 @@
+// Expert-grouped prefill on the 5th-generation tensor cores (sm_100a):
+// tcgen05.mma kind::i8 with operands staged in shared memory by bulk copies,
+// int32 accumulators in tensor memory, and the reference's float tail on the
+// CUDA cores.
+//
+// Q8_0 x Q8_0 (ggml_vec_dot_q8_0_q8_0, NEON order, diff:1049-1054,
+// 1074-1163): per 32-element block b the four integer partials
+//   p_l = sum_m x[4l+m] y[4l+m] + x[16+4l+m] y[16+4l+m]      (l = 0..3)
+// each enter their own float chain acc_l = fma((float)p_l, dx*dy, acc_l),
+// one set of chains for even blocks and one for odd blocks, and the row's
+// dot is ((e0+e1)+(e2+e3)) + ((o0+o1)+(o2+o3)). The tensor core computes the
+// partials exactly: the B operand holds, for each token n, four copies of
+// its activation block, copy l keeping only the eight bytes of lane l (the
+// others zero), so one M=128 x N=64 x K=32 MMA per block writes p_l(m, n) to
+// TMEM column 4n + l of row m. Each block's tile accumulates onto the
+// integer 0x4B400000 (1.5 * 2^23 as f32), so the epilogue reads the partials
+// as floats offset by 12582912 and one exact subtract recovers them; eight
+// tiles of 64 columns rotate through the 512 TMEM columns while the epilogue
+// warps read them (tcgen05.ld 32x32b), store the constant back (tcgen05.st)
+// and run the chains in block order (packed f32x2 subtract and fma).
+//
+// A unit is (chunk of <= 16 (token, slot) pairs of one expert, tile of 128
+// weight rows): gate/up units take gate rows r0..r0+63 and up rows
+// r0..r0+63 of the expert (the SwiGLU pairs gate row i with up row i);
+// down units take 128 rows of the down matrix. One CTA per unit, 12 warps:
+//   warp 0        producer: per chunk of 8 blocks, the unit's weight rows
+//                 as TMA tensor tiles (box 136 16-bit words x 64 or 128
+//                 rows of a 3-D map over the slots) into a raw stage, and the
+//                 chunk's 8 prepared B tiles (one bulk copy)
+//   warp 1        TMEM allocation; lane 0 issues the MMAs and commits
+//   warps 2-3     repack: thread q moves rows q and q+64's eight Q8_0 blocks
+//                 from the raw stage into the UMMA K-major layout (core
+//                 matrices of 8 rows x 16 bytes) and keeps each block's scale dx
+//   warps 4-11    epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows),
+//                 columns of tokens 0-7 (warps 4-7) or 8-15 (warps 8-11)
+// Every wait is bounded and gives up (recording GX_DEVERR_TIMEOUT) once any
+// CTA has recorded an error; TMEM is freed after the MMAs in flight land.
+#pragma once
+
+#include <cstdint>
+
+#include "gx_device.cuh"
+#include "gx_kernels.h"
+
+namespace gx {
+
+// ------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ void tmem_alloc(uint32_t * dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// D[tmem] = A x B^T (int8 x int8 -> int32), both K-major, one thread
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+        : "memory");
+}
+// the mbarrier arrives once every MMA this thread issued before has completed
+__device__ __forceinline__ void mma_commit(uint64_t * bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// A 3-D tile of the tensor map into shared memory (no multicast: the
+// weights are this GPU's own memory)
+__device__ __forceinline__ void tma_load_3d(void * dst, const CUtensorMap * map, int x, int y, int z, uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand without swizzling:
+// core matrices of 8 rows x 16 bytes stored as 128 contiguous bytes, the
+// two 16-byte halves of a 32-byte K step lbo bytes apart, consecutive
+// 8-row groups sbo bytes apart (version 1, base offset 0, layout type 0).
+__device__ __forceinline__ uint64_t umma_desc(const void * smem, uint32_t lbo, uint32_t sbo) {
+    const uint32_t a = smem_u32(smem);
+    return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// instruction descriptor: s32 accumulator, signed int8 A and B, both K-major
+__host__ __device__ constexpr uint32_t umma_idesc_i8(uint32_t M, uint32_t N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane (no wait)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 consecutive columns of this thread's TMEM lane set to v
+__device__ __forceinline__ void tmem_st32_const(uint32_t taddr, uint32_t v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+        "r"(v)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// The accumulators start at the integer 0x4B400000, the bits of 1.5 * 2^23:
+// a partial |p| < 2^22 added to it (exactly, in int32) lands in the mantissa,
+// so the tile read as f32 is 12582912 + p and one exact float subtract gives
+// (float)p (no conversion instruction)
+constexpr uint32_t kMagicBits = 0x4B400000u;
+constexpr float kMagic = 12582912.0f;
+
+// two IEEE operations in one instruction (f32x2, round to nearest, no flush)
+__device__ __forceinline__ void sub2(float & d0, float & d1, float a0, float a1, float b) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+        "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b));
+}
+__device__ __forceinline__ void fma2(float & c0, float & c1, float a0, float a1, float b) {
+    asm("{\n\t.reg .b64 ra, rb, rc;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\tmov.b64 rc, {%0, %1};\n\t"
+        "fma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
+        : "+f"(c0), "+f"(c1)
+        : "f"(a0), "f"(a1), "f"(b));
+}
+
+__device__ __forceinline__ bool mma_wait(uint64_t * bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 20); ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 500u)) return true;
+        if ((i & 63u) == 63u && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) return false;
+    }
+    return false;
+}
+
+// ---------------------------------------------------------------- layout
+
+constexpr int kMmaKb = 8;              // Q8_0 blocks per stage
+constexpr int kMmaBufs = 8;            // TMEM tiles of kMmaN columns
+constexpr int kMmaRawPitch = 272;      // bytes per weight row in the raw stage (one box row)
+constexpr int kMmaThreads = 12 * 32;   // 3 warps per SM sub-partition: up to 168 registers a thread
+
+struct MmaSmem {
+    static constexpr uint32_t raw = 0;                                              // [2][128][272]
+    static constexpr uint32_t atile = raw + 2 * kMmaRows * kMmaRawPitch;            // [2][8][128 x 32]
+    static constexpr uint32_t btile = atile + 2 * kMmaKb * kMmaRows * 32;           // [2][8][64 x 32]
+    static constexpr uint32_t dx = btile + 2 * kMmaKb * kMmaN * 32;                 // [64][128] f32
+    static constexpr uint32_t dy = dx + kMmaMaxBlocks * kMmaRows * 4;               // [64][16] f32
+    static constexpr uint32_t xch = dy + kMmaMaxBlocks * kMmaTok * 4;               // [16][64] f32 up dots
+    static constexpr uint32_t bars = xch + kMmaTok * 64 * 4;                        // mbarriers
+    static constexpr uint32_t nbars = 2 + 2 + 2 + 2 * kMmaBufs + kMmaMaxBlocks / kMmaKb + 1;
+    static constexpr uint32_t tmem_slot = bars + nbars * 8;
+    static constexpr uint32_t total = tmem_slot + 16;
+};
+static_assert(MmaSmem::total <= kMaxSmem, "prefill MMA shared memory");
+
+// offset of row r, K-half c of a K-major tile in core-matrix order
+__device__ __forceinline__ uint32_t core_off(int r, int c) { return (uint32_t)((r >> 3) * 256 + c * 128 + (r & 7) * 16); }
+
+// ------------------------------------------------------ B operand prep
+// For chunk c and block b: 64 rows (pair n = row / 4, lane l = row % 4) of
+// 32 bytes, row (n, l) = the pair's activation block with every byte outside
+// lane l's eight (4l..4l+3, 16+4l..16+4l+3) zeroed, in core-matrix order;
+// and the pair's block scale as f32. Pairs past the chunk's count are zero.
+__global__ void k_mma_bprep(MmaPrepParams p) {
+    const int c = blockIdx.y;
+    const int b = blockIdx.x;
+    const int row = threadIdx.x;   // 0..63
+    const int n = row >> 2, l = row & 3;
+    const int cnt = p.chunk_count[c];
+    uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+    float d = 0.0f;
+    if (n < cnt) {
+        const int src = p.pair_src[p.chunk_first[c] + n];
+        const uint8_t * q = p.aq + (int64_t)src * p.al.pitch;
+        const uint32_t wlo = *reinterpret_cast<const uint32_t *>(q + 32 * b + 4 * l);
+        const uint32_t whi = *reinterpret_cast<const uint32_t *>(q + 32 * b + 16 + 4 * l);
+        uint32_t * plo = reinterpret_cast<uint32_t *>(&lo);
+        uint32_t * phi = reinterpret_cast<uint32_t *>(&hi);
+        plo[l] = wlo;
+        phi[l] = whi;
+        d = h2f(*reinterpret_cast<const uint16_t *>(q + p.al.d_off + 2 * b));
+    }
+    uint8_t * t = p.btiles + ((int64_t)c * p.nblk + b) * (kMmaN * 32);
+    *reinterpret_cast<uint4 *>(t + core_off(row, 0)) = lo;
+    *reinterpret_cast<uint4 *>(t + core_off(row, 1)) = hi;
+    if (l == 0) p.dyt[((int64_t)c * p.nblk + b) * kMmaTok + n] = d;
+}
+
+// ---------------------------------------------------------------- kernel
+
+template <int MODE>
+__global__ void __launch_bounds__(kMmaThreads, 1) k_prefill_mma(const __grid_constant__ MmaParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t * bars = reinterpret_cast<uint64_t *>(smem + MmaSmem::bars);
+    uint64_t * raw_full = bars;                  // [2] producer -> repack, MMA
+    uint64_t * a_ready = bars + 2;               // [2] repack -> MMA (128 arrivals)
+    uint64_t * slot_free = bars + 4;             // [2] MMA commit -> producer
+    uint64_t * tm_full = bars + 6;               // [8] MMA commit -> epilogue
+    uint64_t * tm_empty = tm_full + kMmaBufs;    // [8] epilogue (8 warps) -> MMA
+    uint64_t * dx_full = tm_empty + kMmaBufs;    // [chunks] repack (128) -> epilogue
+    uint64_t * dy_full = dx_full + kMmaMaxBlocks / kMmaKb;
+    uint32_t * tslot = reinterpret_cast<uint32_t *>(smem + MmaSmem::tmem_slot);
+    float * dx = reinterpret_cast<float *>(smem + MmaSmem::dx);
+    float * dy = reinterpret_cast<float *>(smem + MmaSmem::dy);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int unit = blockIdx.x;
+    const int c = unit / p.n_rt, rt = unit - c * p.n_rt;
+    const int nblk = p.nblk, nch = nblk / kMmaKb;
+    const int slot = p.chunk_slot[c];
+    const int first = p.chunk_first[c], cnt = p.chunk_count[c];
+    const int r0 = rt * (MODE == 0 ? 64 : kMmaRows);
+
+    if (tid == 0) {
+        mbar_init(raw_full + 0, 1);
+        mbar_init(raw_full + 1, 1);
+        mbar_init(a_ready + 0, 64);
+        mbar_init(a_ready + 1, 64);
+        mbar_init(slot_free + 0, 1);
+        mbar_init(slot_free + 1, 1);
+        for (int i = 0; i < kMmaBufs; ++i) {
+            mbar_init(tm_full + i, 1);
+            mbar_init(tm_empty + i, 8);
+        }
+        for (int i = 0; i < nch; ++i) mbar_init(dx_full + i, 64);
+        mbar_init(dy_full, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tslot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------- producer
+        if (lane == 0) {
+            tma_expect(dy_full, (uint32_t)(nblk * kMmaTok * 4));
+            tma_load(dy, p.dyt + (int64_t)c * nblk * kMmaTok, (uint32_t)(nblk * kMmaTok * 4), dy_full);
+        }
+        for (int j = 0; j < nch; ++j) {
+            const int s = j & 1;
+            int ok = 1;
+            if (j >= 2 && lane == 0) ok = mma_wait(slot_free + s, (uint32_t)(((j >> 1) - 1) & 1)) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) record_error(GX_DEVERR_TIMEOUT);
+                break;
+            }
+            uint8_t * rawp = smem + MmaSmem::raw + s * kMmaRows * kMmaRawPitch;
+            const uint32_t chunk_bytes = (uint32_t)(kMmaKb * 34);   // 272 = 136 16-bit words
+            if (lane == 0) {
+                tma_expect(raw_full + s, (uint32_t)kMmaRows * chunk_bytes + (uint32_t)(kMmaKb * kMmaN * 32));
+                const int x = j * (int)(chunk_bytes / 2);
+                if (MODE == 0) {
+                    tma_load_3d(rawp, &p.tmap, x, r0, slot, raw_full + s);                                  // gate rows
+                    tma_load_3d(rawp + 64 * kMmaRawPitch, &p.tmap, x, p.up_row0 + r0, slot, raw_full + s);   // up rows
+                } else {
+                    tma_load_3d(rawp, &p.tmap, x, r0, slot, raw_full + s);
+                }
+                tma_load(smem + MmaSmem::btile + s * (kMmaKb * kMmaN * 32),
+                         p.btiles + ((int64_t)c * nblk + (int64_t)j * kMmaKb) * (kMmaN * 32), (uint32_t)(kMmaKb * kMmaN * 32),
+                         raw_full + s);
+            }
+        }
+        // the last two stages' copies land before the CTA can exit
+        if (lane == 0)
+            for (int j = nch - 2 < 0 ? 0 : nch - 2; j < nch; ++j) mma_wait(raw_full + (j & 1), (uint32_t)((j >> 1) & 1));
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_i8(kMmaRows, kMmaN);
+            bool ok = true;
+            int issued = 0;
+            for (int j = 0; j < nch && ok; ++j) {
+                const int s = j & 1;
+                ok = mma_wait(raw_full + s, (uint32_t)((j >> 1) & 1)) && mma_wait(a_ready + s, (uint32_t)((j >> 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                const uint8_t * at = smem + MmaSmem::atile + s * (kMmaKb * kMmaRows * 32);
+                const uint8_t * bt = smem + MmaSmem::btile + s * (kMmaKb * kMmaN * 32);
+                for (int i = 0; i < kMmaKb; ++i) {
+                    const int bidx = j * kMmaKb + i, buf = bidx % kMmaBufs;
+                    // the buffer holds the magic constant again (epilogue)
+                    ok = mma_wait(tm_empty + buf, (uint32_t)((bidx / kMmaBufs) & 1));
+                    if (!ok) break;
+                    tc_fence_after();
+                    mma_i8(tbase + (uint32_t)(buf * kMmaN), umma_desc(at + i * kMmaRows * 32, 128, 256),
+                           umma_desc(bt + i * kMmaN * 32, 128, 256), idesc, 1u);
+                    mma_commit(tm_full + buf);
+                    ++issued;
+                }
+                mma_commit(slot_free + s);   // the chunk's operands are no longer read
+            }
+            if (!ok) record_error(GX_DEVERR_TIMEOUT);
+            // every MMA issued has landed before TMEM is freed
+            if (issued > 0) {
+                const int last = issued - 1;
+                mma_wait(tm_full + last % kMmaBufs, (uint32_t)((last / kMmaBufs) & 1));
+            }
+        }
+    } else if (warp < 4) {
+        // ------------------------------------------------------ repack
+        // thread q (0..63) takes weight rows q and q + 64
+        for (int j = 0; j < nch; ++j) {
+            const int s = j & 1;
+            if (!mma_wait(raw_full + s, (uint32_t)((j >> 1) & 1))) {
+                record_error(GX_DEVERR_TIMEOUT);
+                break;
+            }
+            uint8_t * at = smem + MmaSmem::atile + s * (kMmaKb * kMmaRows * 32);
+            for (int m = tid - 64; m < kMmaRows; m += 64) {
+            const uint8_t * rr = smem + MmaSmem::raw + s * kMmaRows * kMmaRawPitch + m * kMmaRawPitch;
+#pragma unroll
+            for (int i = 0; i < kMmaKb; ++i) {
+                // block i: fp16 d at 34i, quants at 34i+2 (34i is 0 or 2 mod 4)
+                const uint8_t * bp = rr + ((34 * i) & ~3);
+                uint32_t W[9];
+#pragma unroll
+                for (int k = 0; k < 9; ++k) W[k] = lds32(bp + 4 * k);
+                uint32_t q[8];
+                uint16_t d;
+                if ((i & 1) == 0) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) q[k] = __funnelshift_r(W[k], W[k + 1], 16);
+                    d = (uint16_t)(W[0] & 0xffffu);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) q[k] = W[k + 1];
+                    d = (uint16_t)(W[0] >> 16);
+                }
+                uint8_t * t = at + i * kMmaRows * 32;
+                *reinterpret_cast<uint4 *>(t + core_off(m, 0)) = make_uint4(q[0], q[1], q[2], q[3]);
+                *reinterpret_cast<uint4 *>(t + core_off(m, 1)) = make_uint4(q[4], q[5], q[6], q[7]);
+                dx[(j * kMmaKb + i) * kMmaRows + m] = h2f(d);
+            }
+            }
+            fence_async_smem();   // generic writes -> tensor-core reads
+            mbar_arrive(a_ready + s);
+            mbar_arrive(dx_full + j);
+            // the slot's next fill waits for the MMAs, which wait for a_ready
+        }
+    } else {
+        // ---------------------------------------------------- epilogue
+        const int lg = warp & 3;                 // TMEM lane group: rows 32*lg..
+        const int half = (warp - 4) >> 2;        // tokens 8*half..8*half+7
+        const int m = 32 * lg + lane;
+        float acc[2][8][4];
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+#pragma unroll
+                for (int l = 0; l < 4; ++l) acc[a][t][l] = 0.0f;
+        // every buffer starts at the magic constant (its first phase of "empty")
+        const uint32_t tl = tbase + ((uint32_t)(32 * lg) << 16) + (uint32_t)(32 * half);
+        for (int buf = 0; buf < kMmaBufs; ++buf) tmem_st32_const(tl + (uint32_t)(buf * kMmaN), kMagicBits);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+            for (int buf = 0; buf < kMmaBufs; ++buf) mbar_arrive(tm_empty + buf);
+        // the chains of 4 tokens of one block from their 16 partials
+        auto chains4 = [&](float dxm, const float4 & dq, const uint32_t (&v)[16], float (&ac)[8][4], int t0) {
+            const float dyv[4] = {dq.x, dq.y, dq.z, dq.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float sc = __fmul_rn(dxm, dyv[t]);
+                float p0, p1, p2, p3;
+                sub2(p0, p1, __uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]), kMagic);
+                sub2(p2, p3, __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]), kMagic);
+                fma2(ac[t0 + t][0], ac[t0 + t][1], p0, p1, sc);
+                fma2(ac[t0 + t][2], ac[t0 + t][3], p2, p3, sc);
+            }
+        };
+        // one block: read its tile, restore the constant (the store overlaps
+        // the chains), run its chains, free the buffer
+        auto block = [&](int b, float (&ac)[8][4]) -> bool {
+            const int u = b % kMmaBufs;
+            if (!mma_wait(tm_full + u, (uint32_t)((b / kMmaBufs) & 1))) return false;
+            tc_fence_after();
+            uint32_t a0[16], a1[16];
+            tmem_ld16(tl + (uint32_t)(u * kMmaN), a0);
+            tmem_ld16(tl + (uint32_t)(u * kMmaN + 16), a1);
+            tmem_wait_ld();
+            tmem_st32_const(tl + (uint32_t)(u * kMmaN), kMagicBits);
+            const float * dyb = dy + b * kMmaTok + 8 * half;
+            const float dxm = dx[b * kMmaRows + m];
+            chains4(dxm, *reinterpret_cast<const float4 *>(dyb), a0, ac, 0);
+            chains4(dxm, *reinterpret_cast<const float4 *>(dyb + 4), a1, ac, 4);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tm_empty + u);
+            return true;
+        };
+        bool ok = mma_wait(dy_full, 0);
+        for (int j = 0; j < nch && ok; ++j) {
+            ok = mma_wait(dx_full + j, 0);
+            // blocks in (even, odd) pairs: the chunk size is even
+            for (int i = 0; i < kMmaKb && ok; i += 2) {
+                ok = block(j * kMmaKb + i, acc[0]);
+                if (ok) ok = block(j * kMmaKb + i + 1, acc[1]);
+            }
+        }
+        if (!ok) record_error(GX_DEVERR_TIMEOUT);
+        float dot[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const float se = __fadd_rn(__fadd_rn(acc[0][t][0], acc[0][t][1]), __fadd_rn(acc[0][t][2], acc[0][t][3]));
+            const float so = __fadd_rn(__fadd_rn(acc[1][t][0], acc[1][t][1]), __fadd_rn(acc[1][t][2], acc[1][t][3]));
+            dot[t] = __fadd_rn(se, so);
+        }
+        if constexpr (MODE == 0) {
+            // rows 64..127 are the up rows: hand them to the gate rows
+            float * xch = reinterpret_cast<float *>(smem + MmaSmem::xch);
+            if (m >= 64)
+#pragma unroll
+                for (int t = 0; t < 8; ++t) xch[(8 * half + t) * 64 + (m - 64)] = dot[t];
+            named_barrier(1, 256);
+            if (m < 64 && ok) {
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const int n = 8 * half + t;
+                    if (n < cnt) {
+                        const float up = xch[n * 64 + m];
+                        const float a = p.act == 1 ? act_swiglu_oai(dot[t], up, p.alpha, p.limit) : act_swiglu(dot[t], up);
+                        p.out[(int64_t)p.pair_dst[first + n] * p.out_ld + r0 + m] = a;
+                    }
+                }
+            }
+        } else {
+            if (ok)
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const int n = 8 * half + t;
+                    if (n < cnt) p.out[(int64_t)p.pair_dst[first + n] * p.out_ld + r0 + m] = dot[t];
+                }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+}  // namespace gx

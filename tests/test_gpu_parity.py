@@ -269,12 +269,14 @@ def test_layer_forward_bitwise_with_churn(gxlib, orc, dev, name):
     arena.close()
 
 
-@pytest.mark.parametrize("T", [16, 64, 257])
+@pytest.mark.parametrize("T", [16, 64, 257, 512])
 def test_grouped_prefill_matches_oracle(gxlib, orc, dev, T):
     """Micro-batches of >= 128 (token, slot) pairs take the expert-grouped
-    kernels (each expert's rows read once, its tokens streamed in chunks of
-    16, four per warp); the bits equal the oracle and the per-pair decode path
-    (GX_GROUPED=0), including experts with one token and with 17 chunks."""
+    path: by default the tensor-core kernels (tcgen05 int8 MMA, 16 pairs of
+    one expert x 128 weight rows per unit), with GX_PREFILL_MMA=0 the
+    CUDA-core grouped kernels, with GX_GROUPED=0 the per-pair decode kernels;
+    all three give the oracle's bits, including experts with one token, with
+    a partial last chunk and with many chunks."""
     import os
     m = _small_model(gxlib, "qwen3-30b", experts=12, layers=1)
     k = m.used
@@ -289,16 +291,19 @@ def test_grouped_prefill_matches_oracle(gxlib, orc, dev, T):
     out = torch.full((T, m.hidden), float("nan"), dtype=torch.float32, device=dev)
     arena.layer_forward(0, D(x), ids, D(w), out, stream=stream)
     got = H(out)
-    os.environ["GX_GROUPED"] = "0"
-    try:
-        out2 = torch.full((T, m.hidden), float("nan"), dtype=torch.float32, device=dev)
-        arena.layer_forward(0, D(x), ids, D(w), out2, stream=stream)
-        per_pair = H(out2)
-    finally:
-        del os.environ["GX_GROUPED"]
+    variants = {}
+    for env in ("GX_PREFILL_MMA", "GX_GROUPED"):
+        os.environ[env] = "0"
+        try:
+            out2 = torch.full((T, m.hidden), float("nan"), dtype=torch.float32, device=dev)
+            arena.layer_forward(0, D(x), ids, D(w), out2, stream=stream)
+            variants[env] = H(out2)
+        finally:
+            del os.environ[env]
     want = orc.moe_layer(m, recs, x, ids, w)
-    np.testing.assert_array_equal(bits(got), bits(want), err_msg=f"grouped T={T}")
-    np.testing.assert_array_equal(bits(per_pair), bits(want), err_msg=f"per-pair T={T}")
+    np.testing.assert_array_equal(bits(got), bits(want), err_msg=f"tensor-core T={T}")
+    np.testing.assert_array_equal(bits(variants["GX_PREFILL_MMA"]), bits(want), err_msg=f"CUDA-core grouped T={T}")
+    np.testing.assert_array_equal(bits(variants["GX_GROUPED"]), bits(want), err_msg=f"per-pair T={T}")
     no_device_error(gxlib)
     arena.close()
 
