@@ -22,7 +22,7 @@
 // A unit is (chunk of <= 16 (token, slot) pairs of one expert, tile of 128
 // weight rows): gate/up units take gate rows r0..r0+63 and up rows
 // r0..r0+63 of the expert (the SwiGLU pairs gate row i with up row i);
-// down units take 128 rows of the down matrix. One CTA per unit, 12 warps:
+// down units take 128 rows of the down matrix. One CTA per unit, 20 warps:
 //   warp 0        producer: per chunk of 8 blocks, the unit's weight rows
 //                 as TMA tensor tiles (box 136 16-bit words x 64 or 128
 //                 rows of a 3-D map over the slots) into a raw stage, and the
@@ -31,8 +31,8 @@
 //   warps 2-3     repack: thread q moves rows q and q+64's eight Q8_0 blocks
 //                 from the raw stage into the UMMA K-major layout (core
 //                 matrices of 8 rows x 16 bytes) and keeps each block's scale dx
-//   warps 4-11    epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows),
-//                 columns of tokens 0-7 (warps 4-7) or 8-15 (warps 8-11)
+//   warps 4-19    epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows)
+//                 and the 16 columns of tokens 4q..4q+3, q = (w-4)/4
 // Every wait is bounded and gives up (recording GX_DEVERR_TIMEOUT) once any
 // CTA has recorded an error; TMEM is freed after the MMAs in flight land.
 #pragma once
@@ -134,6 +134,13 @@ __device__ __forceinline__ void tmem_st32_const(uint32_t taddr, uint32_t v) {
         "r"(v)
         : "memory");
 }
+__device__ __forceinline__ void tmem_st16_const(uint32_t taddr, uint32_t v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1};" ::"r"(taddr),
+        "r"(v)
+        : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // The accumulators start at the integer 0x4B400000, the bits of 1.5 * 2^23:
@@ -143,18 +150,30 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;
 
-// two IEEE operations in one instruction (f32x2, round to nearest, no flush)
-__device__ __forceinline__ void sub2(float & d0, float & d1, float a0, float a1, float b) {
-    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
-        "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b));
+// f32 pairs in 64-bit registers: two IEEE operations per instruction
+// (f32x2, round to nearest, no flush)
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
 }
-__device__ __forceinline__ void fma2(float & c0, float & c1, float a0, float a1, float b) {
-    asm("{\n\t.reg .b64 ra, rb, rc;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\tmov.b64 rc, {%0, %1};\n\t"
-        "fma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
-        : "+f"(c0), "+f"(c1)
-        : "f"(a0), "f"(a1), "f"(b));
+__device__ __forceinline__ uint64_t u2pack(uint32_t a, uint32_t b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float & a, float & b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t sub_x2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma_x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
 }
 
 __device__ __forceinline__ bool mma_wait(uint64_t * bar, uint32_t parity) {
@@ -170,7 +189,8 @@ __device__ __forceinline__ bool mma_wait(uint64_t * bar, uint32_t parity) {
 constexpr int kMmaKb = 8;              // Q8_0 blocks per stage
 constexpr int kMmaBufs = 8;            // TMEM tiles of kMmaN columns
 constexpr int kMmaRawPitch = 272;      // bytes per weight row in the raw stage (one box row)
-constexpr int kMmaThreads = 12 * 32;   // 3 warps per SM sub-partition: up to 168 registers a thread
+constexpr int kMmaThreads = 20 * 32;   // 5 warps per SM sub-partition: up to 96 registers a thread
+constexpr int kMmaEpiWarps = 16;       // 4 TMEM lane groups x 4 token quarters
 
 struct MmaSmem {
     static constexpr uint32_t raw = 0;                                              // [2][128][272]
@@ -252,7 +272,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_prefill_mma(const __grid_con
         mbar_init(slot_free + 1, 1);
         for (int i = 0; i < kMmaBufs; ++i) {
             mbar_init(tm_full + i, 1);
-            mbar_init(tm_empty + i, 8);
+            mbar_init(tm_empty + i, kMmaEpiWarps);
         }
         for (int i = 0; i < nch; ++i) mbar_init(dx_full + i, 64);
         mbar_init(dy_full, 1);
@@ -378,51 +398,43 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_prefill_mma(const __grid_con
     } else {
         // ---------------------------------------------------- epilogue
         const int lg = warp & 3;                 // TMEM lane group: rows 32*lg..
-        const int half = (warp - 4) >> 2;        // tokens 8*half..8*half+7
+        const int qt = (warp - 4) >> 2;          // token quarter: tokens 4*qt..4*qt+3
         const int m = 32 * lg + lane;
-        float acc[2][8][4];
+        // chains of 4 tokens: acc2[parity][t] = pairs (l0, l1), (l2, l3)
+        uint64_t acc2[2][4][2];
 #pragma unroll
         for (int a = 0; a < 2; ++a)
 #pragma unroll
-            for (int t = 0; t < 8; ++t)
-#pragma unroll
-                for (int l = 0; l < 4; ++l) acc[a][t][l] = 0.0f;
+            for (int t = 0; t < 4; ++t) acc2[a][t][0] = acc2[a][t][1] = 0ull;
+        const uint64_t magic2 = f2pack(kMagic, kMagic);
+        const uint32_t tl = tbase + ((uint32_t)(32 * lg) << 16) + (uint32_t)(16 * qt);
         // every buffer starts at the magic constant (its first phase of "empty")
-        const uint32_t tl = tbase + ((uint32_t)(32 * lg) << 16) + (uint32_t)(32 * half);
-        for (int buf = 0; buf < kMmaBufs; ++buf) tmem_st32_const(tl + (uint32_t)(buf * kMmaN), kMagicBits);
+        for (int buf = 0; buf < kMmaBufs; ++buf) tmem_st16_const(tl + (uint32_t)(buf * kMmaN), kMagicBits);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0)
             for (int buf = 0; buf < kMmaBufs; ++buf) mbar_arrive(tm_empty + buf);
-        // the chains of 4 tokens of one block from their 16 partials
-        auto chains4 = [&](float dxm, const float4 & dq, const uint32_t (&v)[16], float (&ac)[8][4], int t0) {
+        // one block: read its 16 columns, restore the constant (the store
+        // overlaps the chains), run the chains, free the buffer
+        auto block = [&](int b, uint64_t (&ac)[4][2]) -> bool {
+            const int u = b % kMmaBufs;
+            if (!mma_wait(tm_full + u, (uint32_t)((b / kMmaBufs) & 1))) return false;
+            tc_fence_after();
+            uint32_t v[16];
+            tmem_ld16(tl + (uint32_t)(u * kMmaN), v);
+            tmem_wait_ld();
+            tmem_st16_const(tl + (uint32_t)(u * kMmaN), kMagicBits);
+            const float dxm = dx[b * kMmaRows + m];
+            const float4 dq = *reinterpret_cast<const float4 *>(dy + b * kMmaTok + 4 * qt);
             const float dyv[4] = {dq.x, dq.y, dq.z, dq.w};
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
                 const float sc = __fmul_rn(dxm, dyv[t]);
-                float p0, p1, p2, p3;
-                sub2(p0, p1, __uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]), kMagic);
-                sub2(p2, p3, __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]), kMagic);
-                fma2(ac[t0 + t][0], ac[t0 + t][1], p0, p1, sc);
-                fma2(ac[t0 + t][2], ac[t0 + t][3], p2, p3, sc);
+                const uint64_t sc2 = f2pack(sc, sc);
+                ac[t][0] = fma_x2(sub_x2(u2pack(v[4 * t], v[4 * t + 1]), magic2), sc2, ac[t][0]);
+                ac[t][1] = fma_x2(sub_x2(u2pack(v[4 * t + 2], v[4 * t + 3]), magic2), sc2, ac[t][1]);
             }
-        };
-        // one block: read its tile, restore the constant (the store overlaps
-        // the chains), run its chains, free the buffer
-        auto block = [&](int b, float (&ac)[8][4]) -> bool {
-            const int u = b % kMmaBufs;
-            if (!mma_wait(tm_full + u, (uint32_t)((b / kMmaBufs) & 1))) return false;
-            tc_fence_after();
-            uint32_t a0[16], a1[16];
-            tmem_ld16(tl + (uint32_t)(u * kMmaN), a0);
-            tmem_ld16(tl + (uint32_t)(u * kMmaN + 16), a1);
-            tmem_wait_ld();
-            tmem_st32_const(tl + (uint32_t)(u * kMmaN), kMagicBits);
-            const float * dyb = dy + b * kMmaTok + 8 * half;
-            const float dxm = dx[b * kMmaRows + m];
-            chains4(dxm, *reinterpret_cast<const float4 *>(dyb), a0, ac, 0);
-            chains4(dxm, *reinterpret_cast<const float4 *>(dyb + 4), a1, ac, 4);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -434,16 +446,21 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_prefill_mma(const __grid_con
             ok = mma_wait(dx_full + j, 0);
             // blocks in (even, odd) pairs: the chunk size is even
             for (int i = 0; i < kMmaKb && ok; i += 2) {
-                ok = block(j * kMmaKb + i, acc[0]);
-                if (ok) ok = block(j * kMmaKb + i + 1, acc[1]);
+                ok = block(j * kMmaKb + i, acc2[0]);
+                if (ok) ok = block(j * kMmaKb + i + 1, acc2[1]);
             }
         }
         if (!ok) record_error(GX_DEVERR_TIMEOUT);
-        float dot[8];
+        float dot[4];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const float se = __fadd_rn(__fadd_rn(acc[0][t][0], acc[0][t][1]), __fadd_rn(acc[0][t][2], acc[0][t][3]));
-            const float so = __fadd_rn(__fadd_rn(acc[1][t][0], acc[1][t][1]), __fadd_rn(acc[1][t][2], acc[1][t][3]));
+        for (int t = 0; t < 4; ++t) {
+            float e0, e1, e2, e3, o0, o1, o2, o3;
+            f2unpack(acc2[0][t][0], e0, e1);
+            f2unpack(acc2[0][t][1], e2, e3);
+            f2unpack(acc2[1][t][0], o0, o1);
+            f2unpack(acc2[1][t][1], o2, o3);
+            const float se = __fadd_rn(__fadd_rn(e0, e1), __fadd_rn(e2, e3));
+            const float so = __fadd_rn(__fadd_rn(o0, o1), __fadd_rn(o2, o3));
             dot[t] = __fadd_rn(se, so);
         }
         if constexpr (MODE == 0) {
@@ -451,12 +468,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_prefill_mma(const __grid_con
             float * xch = reinterpret_cast<float *>(smem + MmaSmem::xch);
             if (m >= 64)
 #pragma unroll
-                for (int t = 0; t < 8; ++t) xch[(8 * half + t) * 64 + (m - 64)] = dot[t];
-            named_barrier(1, 256);
+                for (int t = 0; t < 4; ++t) xch[(4 * qt + t) * 64 + (m - 64)] = dot[t];
+            named_barrier(1, 32 * kMmaEpiWarps);
             if (m < 64 && ok) {
 #pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const int n = 8 * half + t;
+                for (int t = 0; t < 4; ++t) {
+                    const int n = 4 * qt + t;
                     if (n < cnt) {
                         const float up = xch[n * 64 + m];
                         const float a = p.act == 1 ? act_swiglu_oai(dot[t], up, p.alpha, p.limit) : act_swiglu(dot[t], up);
@@ -467,8 +484,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) k_prefill_mma(const __grid_con
         } else {
             if (ok)
 #pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const int n = 8 * half + t;
+                for (int t = 0; t < 4; ++t) {
+                    const int n = 4 * qt + t;
                     if (n < cnt) p.out[(int64_t)p.pair_dst[first + n] * p.out_ld + r0 + m] = dot[t];
                 }
         }

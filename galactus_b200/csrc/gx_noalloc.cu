@@ -17,9 +17,11 @@
 // caller. Each call clears the counters it needs before its kernels run; the
 // other regions are fully rewritten by each call.
 //
-// The first call on a device resolves the array's device address with
-// cudaGetSymbolAddress (with that device current) and caches it; make that
-// first call before any stream capture.
+// Each call outside a stream capture resolves the array's device address with
+// cudaGetSymbolAddress (with its device current) and caches it; a call during
+// a capture uses the cached address, so make one call on the device before
+// capturing (a context reset between them needs another call outside a
+// capture).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -41,18 +43,26 @@ std::mutex g_addr_mu;
 uint8_t * g_addr[kMaxDevices] = {nullptr};
 
 // device address of the scratch array on the current device (host code only
-// sees a host-side stand-in under the array's name)
-cudaError_t scratch_address(uint8_t ** out) {
+// sees a host-side stand-in under the array's name). Outside a stream capture
+// the address is looked up on every call, so a context that was reset and
+// reloaded the module is picked up; during a capture the address cached by
+// the last call outside one is used (a capture cannot look it up).
+cudaError_t scratch_address(cudaStream_t stream, uint8_t ** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(g_addr_mu);
-    if (g_addr[dev] == nullptr) {
+    if (cap == cudaStreamCaptureStatusNone) {
         void * p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return e;
         g_addr[dev] = static_cast<uint8_t *>(p);
+    } else if (g_addr[dev] == nullptr) {
+        return cudaErrorStreamCaptureUnsupported;
     }
     *out = g_addr[dev];
     return cudaSuccess;
@@ -87,7 +97,7 @@ extern "C" int gx_moe_ffn_noalloc(const gx_layer_desc * d, const void * slot0_re
         if (slots[j] < 0 || (uint32_t)slots[j] >= n_slots) return GX_ERR_DOMAIN;
 
     uint8_t * base = nullptr;
-    if (scratch_address(&base) != cudaSuccess) return GX_ERR_CUDA;
+    if (scratch_address(reinterpret_cast<cudaStream_t>(stream), &base) != cudaSuccess) return GX_ERR_CUDA;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int vdt_g = gx::vec_dot_type(d->type_gate), vdt_d = gx::vec_dot_type(d->type_down);
     const gx::ActLayout al_x = gx::act_layout(vdt_g, (int)H), al_a = gx::act_layout(vdt_d, (int)I);

@@ -360,8 +360,10 @@ int gx_stack_plan_destroy(gx_stack_plan * plan);
  * the library, held by every GPU that loads it until exit; k*T, H and I above
  * the GX_NOALLOC_MAX_* limits are rejected with GX_ERR_INVALID. Every call on
  * a device shares the array: calls that overlap on the GPU race and must be
- * serialized by the caller. The first call on a device looks up the array's
- * address (make it before any stream capture).
+ * serialized by the caller. Each call outside a stream capture looks up the
+ * array's address on its device; a call inside a capture uses the address of
+ * the last call outside one (make one first; after a reset of the device's
+ * context, make another before capturing again).
  * No counterpart in the reference. */
 #define GX_NOALLOC_MAX_PAIRS 64
 #define GX_NOALLOC_MAX_HIDDEN 8192
