@@ -72,7 +72,7 @@ class gx_router_desc(C.Structure):
 class gx_stack_plan_info(C.Structure):
     _fields_ = [("stack_kernel", C.c_int32), ("grid", C.c_int32), ("threads", C.c_int32),
                 ("ctas_per_sm", C.c_int32), ("stages", C.c_int32), ("rows_gate_up", C.c_int32),
-                ("rows_down", C.c_int32), ("smem_bytes", C.c_uint32)]
+                ("rows_down", C.c_int32), ("smem_bytes", C.c_uint32), ("tensor_cores", C.c_int32)]
 
 
 class gx_arena_config(C.Structure):

@@ -1428,6 +1428,42 @@ bool choose_stack_tiles(gx::StackParams & sp, int & threads, uint32_t & smem) {
     return false;
 }
 
+// MXFP4 jobs on the tensor cores (row mode 4): 16 + 16 gate/up rows, 8 rows
+// of each of k = 4 experts per down job, the 12 role warps of the tensor-core
+// jobs, three ring stages, the activations as e4m3 digit rows (per 32-element
+// block: 2 K halves x k rows x 2 digits x 16 bytes, then the fp16 scales;
+// the down inputs of a token's k slots interleaved in one row). On with
+// GX_STACK_MMA=1 (opt-in: measured slower than the CUDA-core MXFP4 jobs,
+// whose default it is not); on any shape it does not cover the CUDA-core
+// MXFP4 jobs run.
+bool choose_stack_tiles_tc(gx::StackParams & sp, int & threads, uint32_t & smem) {
+    const char * env = std::getenv("GX_STACK_MMA");
+    if (env == nullptr || std::strcmp(env, "1") != 0) return false;
+    if (sp.k != 4 || sp.H % 64 != 0 || sp.I % 64 != 0) return false;
+    const gx::StackParams keep = sp;
+    const int nbh = sp.H / 32, nbi = sp.I / 32;
+    sp.row_mode = 4;
+    sp.Rg = 16;
+    sp.Rd = 8;
+    sp.W = 12;
+    sp.alx.d_off = 64 * nbh;
+    sp.alx.bs_off = sp.alx.d_off;
+    // the N = 16 B tiles of the last block read up to 224 bytes past the digits
+    sp.alx.pitch = gx::align16i((int64_t)sp.alx.d_off + std::max(2 * nbh, 256));
+    const int64_t tok = 64ll * sp.k * nbi + std::max(2ll * sp.k * nbi, 256ll);   // a token's k digit rows and scales
+    const int64_t tok_al = (tok + 16 * sp.k - 1) / (16 * sp.k) * (16 * sp.k);
+    sp.ald.d_off = 64 * sp.k * nbi;
+    sp.ald.bs_off = sp.ald.d_off;
+    sp.ald.pitch = (int32_t)(tok_al / sp.k);
+    for (int C = 3; C >= 2; --C) {
+        sp.C = C;
+        smem = gx::stack_layout(sp, threads);
+        if (smem != 0) return true;
+    }
+    sp = keep;
+    return false;
+}
+
 // Device buffers and the layer table of the stack kernel.
 int setup_stack(gx_stack_plan * p, const float * const * x, const float * const * w, float * const * out) {
     gx_arena * a = p->a;
@@ -1458,7 +1494,8 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     sp.need_grid = (l0.type_gate == gx::GX_T_IQ1_S || l0.type_down == gx::GX_T_IQ1_S) ? 1 : 0;
     int threads = 0;
     uint32_t smem = 0;
-    if (!choose_stack_tiles(sp, threads, smem)) return GX_ERR_ALIGN;
+    if (!(sp.row_mode == 3 && choose_stack_tiles_tc(sp, threads, smem)) && !choose_stack_tiles(sp, threads, smem))
+        return GX_ERR_ALIGN;
     sp.split = sp.row_mode == 3 ? 4 : (sp.row_mode == 1 || (sp.row_mode == 2 && sp.k * sp.Rd == 32)) ? 2 : 1;
     sp.n_gu = (int32_t)(p->T * p->k * (l0.I / sp.Rg));
     sp.n_d = (int32_t)(p->T * (l0.H / sp.Rd));
@@ -1761,6 +1798,7 @@ int gx_stack_plan_info_get(const gx_stack_plan * p, gx_stack_plan_info * info) {
         info->rows_gate_up = p->sp.Rg;
         info->rows_down = p->sp.Rd;
         info->smem_bytes = p->smem;
+        info->tensor_cores = p->sp.row_mode == 4 ? 1 : 0;
     }
     return GX_OK;
 }

@@ -776,11 +776,15 @@ static bool stack_copy_mode(int64_t nb01, int R, int32_t & row_copy, int32_t & p
 // gate/up tiles and rows of K % 256 == 0), 1 octet rows (any whole number
 // of their type's 64- or 256-element units, checked per layer; 2 gate/up copies).
 uint32_t stack_layout(StackParams & p, int & threads) {
-    if (!(p.Rg == 8 || (p.Rg == 16 && p.row_mode == 3)) || p.Rd < 1 ||
-        (p.k * p.Rd != 32 && !(p.row_mode == 2 && p.k * p.Rd == 16)))
+    const bool mx = p.row_mode == 3 || p.row_mode == 4;
+    if (!(p.Rg == 8 || (p.Rg == 16 && mx)) || p.Rd < 1 || (p.k * p.Rd != 32 && !(p.row_mode == 2 && p.k * p.Rd == 16)))
         return 0;
-    const bool tiles8 = p.row_mode == 1 || p.row_mode == 3;   // gate/up as 2 copies of 8 rows
-    if (p.row_mode < 0 || p.row_mode > 3 || p.gu_copies != (tiles8 ? 2 : 4)) return 0;
+    // tensor-core MXFP4 jobs: 16 + 16 gate/up rows, 8 rows of each of 4 experts,
+    // the 12 role warps of gx_stack_tc.cuh, rows of at most kTcMaxBlocks blocks
+    if (p.row_mode == 4 && (p.Rg != 16 || p.k != 4 || p.W != 12 || p.H / 32 > kTcMaxBlocks || p.I / 32 > kTcMaxBlocks))
+        return 0;
+    const bool tiles8 = p.row_mode == 1 || mx;   // gate/up as 2 copies of Rg rows
+    if (p.row_mode < 0 || p.row_mode > 4 || p.gu_copies != (tiles8 ? 2 : 4)) return 0;
     const int ra = tiles8 ? 64 : 256;
     if (p.H % ra || p.I % ra || p.I % p.Rg || p.qblk % p.Rg || p.H % p.Rd) return 0;
     if (p.C < 1 || p.C > kStackMaxConsumers || p.NL < 1 || p.NL > kStackMaxLayers) return 0;
@@ -790,10 +794,17 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     // it and the parity wait is unambiguous. With C not a multiple of P two
     // producers would share a stage and one could wait on a barrier two phases
     // behind, read the older phase as complete and refill a stage in use.
-    if (p.C % kStackProducers != 0) return 0;
+    if (p.C % (p.row_mode == 4 ? 1 : kStackProducers) != 0) return 0;
     if (p.W < 1 || p.W > stack_max_warps(p.row_mode)) return 0;
     if (p.row_mode == 1 && (p.Rd & 1)) return 0;   // octet row pairs stay inside one expert
     threads = 32 * (kStackProducers + 2) + 32 * p.W;
+    // the digit rows of row mode 4 (per block: 2 K halves x k rows x 2 digits x 16 bytes, then fp16 scales)
+    // (and room for the MMA's N = 16 B tiles of the last block, which read up to 256 bytes past the digits)
+    if (p.row_mode == 4 && (p.alx.d_off != 64 * (p.H / 32) || p.ald.d_off != 64 * p.k * (p.I / 32) ||
+                            p.alx.pitch < p.alx.d_off + 256 || p.alx.pitch < p.alx.d_off + 2 * (p.H / 32) ||
+                            (int64_t)p.k * p.ald.pitch < p.ald.d_off + 256 ||
+                            (int64_t)p.k * p.ald.pitch < p.ald.d_off + 2 * p.k * (p.I / 32)))
+        return 0;
     if (!stack_copy_mode(p.nb01_d, p.Rd, p.row_copy_d, p.pitch_d)) return 0;
     uint64_t gw;
     if (p.gu_copies == 4) {
@@ -829,20 +840,41 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     p.meta_off = (uint32_t)align_up(8ull * (3 * kStackMaxConsumers + 2 * kStackBufs), 128);
     // fill words, buffer counters, release counter per stage, next task, finished parts per stage
     p.stage_off = p.meta_off + (uint32_t)align_up(4ull * (3 * kStackMaxConsumers + 2 * kStackBufs + 1), 128);
-    p.xbuf_off = p.stage_off + (uint32_t)p.C * (uint32_t)p.stage_bytes;
+    // row mode 4: the A tiles, scales, pair terms, dots and barriers of the roles
+    p.tc_off = p.stage_off + (uint32_t)p.C * (uint32_t)p.stage_bytes;
+    const int nbmax = (p.H > p.I ? p.H : p.I) / 32;
+    p.tc_na = kTcAmax;
+    p.xbuf_off = p.tc_off + (p.row_mode == 4 ? (uint32_t)align_up(tc_bytes(nbmax, p.tc_na), 128) : 0u);
     p.dbuf_off = p.xbuf_off + align_up((uint64_t)kStackBufs * p.alx.pitch, 128);
-    p.wt_off = p.dbuf_off + align_up((uint64_t)kStackBufs * p.k * p.ald.pitch, 128);
+    p.nbuf_d = p.row_mode == 4 ? 1 : kStackBufs;
+    p.wt_off = p.dbuf_off + align_up((uint64_t)p.nbuf_d * p.k * p.ald.pitch, 128);
     p.dots_off = p.wt_off + (uint32_t)p.NL * 32u;    // per-layer weight bases
     p.slots_off = p.dots_off + (uint32_t)p.C * 32u * 4u;   // 32 down-row dots per stage
     p.grid_off = p.slots_off + (uint32_t)align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
-    const uint32_t total = p.grid_off + (p.need_grid ? 2048u * 8u : 0u);
+    // row mode 4: the B tiles of the last MMA steps read up to 2 KB past the input rows
+    const uint32_t total = p.grid_off + (p.need_grid ? 2048u * 8u : 0u) + (p.row_mode == 4 ? 2048u : 0u);
+    if (p.row_mode == 4 && total > kMaxSmem) {
+        // fewer A slots (MMA steps in flight), down to kTcAmin
+        const uint32_t over = total - kMaxSmem;
+        const int drop = (int)((over + 4095) / 4096);
+        if (p.tc_na - drop < kTcAmin) return 0;
+        p.tc_na -= drop;
+        const uint32_t shift = (uint32_t)align_up(tc_bytes(nbmax, kTcAmax), 128) - (uint32_t)align_up(tc_bytes(nbmax, p.tc_na), 128);
+        p.xbuf_off -= shift;
+        p.dbuf_off -= shift;
+        p.wt_off -= shift;
+        p.dots_off -= shift;
+        p.slots_off -= shift;
+        p.grid_off -= shift;
+        return total - shift <= kMaxSmem ? total - shift : 0;
+    }
     return total <= kMaxSmem ? total : 0;
 }
 
-template <int TG, int TD>
+template <int TG, int TD, bool TC = false>
 static cudaError_t stack_dispatch(const StackParams * p, int grid, int threads, uint32_t smem, cudaStream_t stream,
                                   int * per_sm) {
-    if (per_sm) return resident_per_sm(k_stack<TG, TD>, threads, smem, *per_sm);
+    if (per_sm) return resident_per_sm(k_stack<TG, TD, TC>, threads, smem, *per_sm);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3((unsigned)threads);
@@ -854,7 +886,7 @@ static cudaError_t stack_dispatch(const StackParams * p, int grid, int threads, 
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_stack<TG, TD>, *p);
+    return cudaLaunchKernelEx(&cfg, k_stack<TG, TD, TC>, *p);
 }
 
 static cudaError_t stack_switch(int tg, int td, const StackParams * p, int grid, int threads, uint32_t smem,
@@ -862,7 +894,8 @@ static cudaError_t stack_switch(int tg, int td, const StackParams * p, int grid,
     if (tg == GX_T_Q8_0 && td == GX_T_Q8_0) return stack_dispatch<GX_T_Q8_0, GX_T_Q8_0>(p, grid, threads, smem, stream, per_sm);
     if (tg == GX_T_Q4_K && td == GX_T_Q6_K) return stack_dispatch<GX_T_Q4_K, GX_T_Q6_K>(p, grid, threads, smem, stream, per_sm);
     if (tg == GX_T_MXFP4 && td == GX_T_MXFP4)
-        return stack_dispatch<GX_T_MXFP4, GX_T_MXFP4>(p, grid, threads, smem, stream, per_sm);
+        return p->row_mode == 4 ? stack_dispatch<GX_T_MXFP4, GX_T_MXFP4, true>(p, grid, threads, smem, stream, per_sm)
+                                : stack_dispatch<GX_T_MXFP4, GX_T_MXFP4>(p, grid, threads, smem, stream, per_sm);
     if (tg == GX_T_IQ1_S && td == GX_T_IQ1_S)
         return stack_dispatch<GX_T_IQ1_S, GX_T_IQ1_S>(p, grid, threads, smem, stream, per_sm);
     return cudaErrorInvalidValue;

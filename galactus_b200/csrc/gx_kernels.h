@@ -136,7 +136,8 @@ struct StackParams {
     int32_t W;                 // consumer warps (may exceed C)
     int32_t skew;              // down jobs of layer L follow the gate/up jobs of layer L+skew
     int32_t row_copy_d, pitch_d;
-    int32_t row_mode;          // 0: two-lane Q8_0 rows, 1: octet rows, 2: two-lane Q4_K/Q6_K rows, 3: two-lane MXFP4 rows
+    int32_t row_mode;          // 0: two-lane Q8_0 rows, 1: octet rows, 2: two-lane Q4_K/Q6_K rows, 3: MXFP4 rows on
+                               // the CUDA cores, 4: MXFP4 rows on the tensor cores (activations as e4m3 digit rows)
     int32_t gu_copies;         // 4 (modes 0, 2): gate/up job in 4 tiles of 4 rows (gate 0-3, 4-7, up 0-3,
                                //    4-7) at gu_tile[0..3], staggered so quarter-warp loads hit distinct
                                //    bank groups; 2 (mode 1): gate rows 0-7 at gu_tile[0], up rows at gu_tile[1]
@@ -152,6 +153,9 @@ struct StackParams {
     int32_t split;             // warps per job: 4 for MXFP4 jobs, 2 for octet jobs and 32-row two-lane K-quant
                                // down jobs, else 1
     uint32_t grid_off;
+    uint32_t tc_off;           // row mode 4: A tiles, block scales, pair terms, mbarriers and the TMEM address
+    int32_t nbuf_d;            // down-input buffers (kStackBufs, or 1 in row mode 4)
+    int32_t tc_na;             // row mode 4: A-tile slots (MMA steps in flight)
     StackLayer layers[kStackMaxLayers];
 };
 

@@ -739,7 +739,7 @@ __device__ __forceinline__ void stack_d_oct(const StackParams & p, const uint8_t
 
 // Input producer of one kind (0: gate/up inputs x_L, 1: down inputs).
 // The input rows of key K = L*T + t (a layer's token) go to buffer
-// K % kStackBufs. Walking the CTA's jobs of its kind in order (their keys
+// K % (kStackBufs, or nbuf_d for down inputs). Walking the CTA's jobs of its kind in order (their keys
 // never decrease), the producer counts the jobs of each buffer; at each new
 // key it waits until every job of the buffer's previous key is done, waits
 // for the rows to exist (x_L quantized, or every Q8 block of the token's
@@ -753,6 +753,7 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
                                                      uint8_t * buf, int buf_bytes) {
     const StackGeom g = stack_geom(p);
     const int blocks_per_token = p.k * (p.I / p.qblk);   // quantized down-input blocks of a token
+    const int nb = kind == 1 ? p.nbuf_d : kStackBufs;       // buffers of this kind
     int iss[kStackBufs], fills[kStackBufs];
 #pragma unroll
     for (int i = 0; i < kStackBufs; ++i) {
@@ -767,7 +768,7 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
         walk.kind(g, jL, jgu);
         if (jgu != (kind == 0 ? 1 : 0)) continue;
         const StackJob J = walk.job(g);
-        const int K = J.L * p.T + J.t, bi = K % kStackBufs;
+        const int K = J.L * p.T + J.t, bi = K % nb;
         if (K != cur) {
             // every job that used the buffer before is done with it
             bool ok = false;
@@ -805,14 +806,26 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
         if (fills[i] > 0) stack_mbar_wait(bbar + i, (uint32_t)((fills[i] - 1) & 1));
 }
 
-template <int TG, int TD>
-__global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_warps(TG == GX_T_MXFP4 ? 3 : 0), 1)
+}  // namespace gx
+
+#include "gx_stack_tc.cuh"
+
+namespace gx {
+
+// TC: MXFP4 jobs on the tensor cores (row mode 4, one weight producer, the
+// roles of gx_stack_tc.cuh on warps 1 and 4-15)
+template <int TG, int TD, bool TC = false>
+__global__ void __launch_bounds__(TC ? kTcThreads : 32 * (kStackProducers + 2) + 32 * stack_max_warps(TG == GX_T_MXFP4 ? 3 : 0), 1)
     k_stack(const __grid_constant__ StackParams p) {
-    // row mode: 0 two-lane Q8_0 rows, 2 two-lane Q4_K gate/up + Q6_K down rows, 1 octet rows
-    constexpr int kMode = (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0
+    // row mode: 0 two-lane Q8_0 rows, 2 two-lane Q4_K gate/up + Q6_K down rows, 1 octet rows,
+    // 3 MXFP4 rows on the CUDA cores, 4 MXFP4 rows on the tensor cores
+    constexpr int kMode = TC ? 4
+                          : (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0
                           : (TG == GX_T_Q4_K && TD == GX_T_Q6_K) ? 2
                           : (TG == GX_T_MXFP4 && TD == GX_T_MXFP4) ? 3
                                                                   : 1;
+    static_assert(!TC || (TG == GX_T_MXFP4 && TD == GX_T_MXFP4), "tensor-core stack jobs are MXFP4 rows");
+    constexpr int P = TC ? 1 : kStackProducers;   // weight producer warps
     constexpr int VG = Oct<TG>::VDT, VD = Oct<TD>::VDT;       // activation types of gate/up and down
     // warps per job (p.split): octet jobs are compute-bound and two warps
     // share each (passes split between them); so do the 32-row down jobs of
@@ -867,11 +880,18 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_wa
     }
     if (tid == 0) {
         for (int s = 0; s < 2 * C + 2 * kStackBufs; ++s) mbar_init(wfull + s, 1);
+        if constexpr (TC) tc_init_bars(tc_team(smem, p.tc_off, (p.H > p.I ? p.H : p.I) / 32, p.tc_na));
         mbar_fence_init();
     }
     __syncthreads();
 
-    if (warp < kStackProducers) {
+    if (TC && warp > 0 && warp < kStackProducers) {
+        // one weight producer; warp 1 issues the MMAs
+        stack_tc(p, smem, warp, lane, b, G, mine, wfull, empty, xbar, dbar, fillw, bufdone, rel, smem + p.stage_off,
+                 smem + p.xbuf_off, smem + p.dbuf_off);
+        return;
+    }
+    if (warp < P) {
         // ------------------------------------------------ weight producers
         // producer warp w issues the jobs jl = w, w + P, ... (P producers)
         const StackGeom g = stack_geom(p);
@@ -884,14 +904,14 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_wa
         q.k = p.k;
         q.Rg = p.Rg;
         q.Rd = p.Rd;
-        q.gu_copies = (kMode == 1 || kMode == 3) ? 2 : 4;
+        q.gu_copies = (kMode == 1 || kMode >= 3) ? 2 : 4;
         for (int t = 0; t < 4; ++t) q.tile[t] = p.gu_tile[t];
         const int stage_bytes = p.stage_bytes;
         StackWalk walk{0, 0};
         walk.advance(g, b + warp * G);
         int last = -1;   // the last job this warp issued
         bool aborted = false;
-        for (int jl = warp; jl < mine; jl += kStackProducers) {
+        for (int jl = warp; jl < mine; jl += P) {
             const int s = jl % C, n = jl / C;
             int okw = 1;
             if (n > 0) {
@@ -905,14 +925,14 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_wa
             }
             stack_issue_weights(q, walk.job(g), slots, wt, stages + s * stage_bytes, wfull + s, lane);
             last = jl;
-            walk.advance(g, kStackProducers * G);
+            walk.advance(g, P * G);
         }
         // Let the copies of this warp that no later job consumed land before
         // the CTA can exit: a stage's final job (jl + C >= mine); a job with a
         // successor on its stage was consumed before the successor was issued.
         // After an abort, every recent copy (bounded waits).
         if (lane == 0)
-            for (int jl = last; jl >= 0 && jl > last - C; jl -= kStackProducers)
+            for (int jl = last; jl >= 0 && jl > last - C; jl -= P)
                 if (aborted || jl + C >= mine) stack_mbar_wait(wfull + jl % C, (uint32_t)((jl / C) & 1));
         return;
     }
@@ -925,6 +945,11 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_wa
         return;
     }
 
+    if constexpr (TC) {
+        // ------------------------------------------ tensor-core roles
+        stack_tc(p, smem, warp, lane, b, G, mine, wfull, empty, xbar, dbar, fillw, bufdone, rel, stages, xbuf, dbuf);
+        return;
+    }
     // ------------------------------------------------------------ consumers
     // W consumer warps take the CTA's jobs dynamically (a shared counter), so
     // a warp busy with an epilogue never leaves a loaded stage idle; job jl
@@ -946,7 +971,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_wa
             const StackLayer & ly = p.layers[L];
             for (int wi = c; wi < p.T * nblk; wi += W) {
                 const int t = wi / nblk, ib = wi - t * nblk;
-                quant_block_split<VG, false, kMode == 3>(ly.x + (int64_t)t * p.H, ly.xq + (int64_t)t * p.alx.pitch, p.alx,
+                quant_block_split<VG, false, kMode >= 3>(ly.x + (int64_t)t * p.H, ly.xq + (int64_t)t * p.alx.pitch, p.alx,
                                                          ib, lane);
             }
             any = true;
@@ -1018,7 +1043,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_wa
         int * done = bufdone + (J.gu ? 0 : kStackBufs) + bi;
         if (J.gu) {
             const uint8_t * xa = xbuf + bi * xbytes;
-            if constexpr (kMode == 3) {
+            if constexpr (kMode >= 3) {
                 // 16 gate rows (tile 0) + 16 up rows (tile 1): lane r takes row r;
                 // part `sub` computes pairs sub, sub + split, ... and parks their terms
                 const uint8_t * row = st + p.gu_tile[lane >> 4] + (lane & 15) * (int)p.nb01_g;
@@ -1127,7 +1152,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_wa
                 // this job finished the Q8 block last: quantize it and count the
                 // block into its token (the down inputs wait for k*I/qblk blocks)
                 fence_acq_rel_gpu();
-                quant_block_split<VD, true, kMode == 3>(ly.act + (int64_t)J.pair * p.I,
+                quant_block_split<VD, true, kMode >= 3>(ly.act + (int64_t)J.pair * p.I,
                                                          ly.actq + (int64_t)J.pair * p.ald.pitch, p.ald, blk, lane);
                 fence_proxy_async_global();
                 __syncwarp();
@@ -1165,7 +1190,7 @@ __global__ void __launch_bounds__(32 * (kStackProducers + 2) + 32 * stack_max_wa
                 }
             }
             __syncwarp();
-        } else if constexpr (kMode == 3) {
+        } else if constexpr (kMode >= 3) {
             // k*Rd = 32 weight rows (row r: row r % Rd of expert r / Rd): lane r
             // takes row r against its expert's activation row
             const uint8_t * da = dbuf + bi * dbytes;

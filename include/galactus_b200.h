@@ -337,6 +337,8 @@ typedef struct gx_stack_plan_info {
     int32_t rows_gate_up;     /* gate (and up) rows per gate/up unit */
     int32_t rows_down;        /* down rows per expert per down unit */
     uint32_t smem_bytes;      /* dynamic shared memory per CTA */
+    int32_t tensor_cores;     /* 1: the block dots of the stack's jobs run on the tensor cores (MXFP4 rows,
+                                 tcgen05 kind::f8f6f4; opt-in with GX_STACK_MMA=1) */
 } gx_stack_plan_info;
 int gx_stack_plan_create(gx_arena * arena, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * desc,
                          const float * const * x, const float * const * w, float * const * out, int64_t k, int64_t T,

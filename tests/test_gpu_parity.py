@@ -2,6 +2,8 @@
 bit-identical outputs on the same seeded inputs, for every weight format of
 the benchmark models, token counts 1..512, both src1 shapes (ne11 = 1 and
 ne11 = k), strided id views, slot churn, and the error paths."""
+import os
+
 import numpy as np
 import pytest
 
@@ -410,8 +412,11 @@ def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name, T, layers, layer
     expect = not layerwise and (m.type_gate, m.type_down) in stack_types
     assert info["stack_kernel"] == (1 if expect else 0), info
     if expect:
-        # each ring stage belongs to one of the two weight-producer warps
-        assert info["stages"] % 2 == 0, info
+        # each ring stage belongs to one of the two weight-producer warps; the
+        # tensor-core MXFP4 jobs (k = 4) have one producer and three stages
+        mx_tc = m.type_gate == gxlib.TYPE_MXFP4 and k == 4 and os.environ.get("GX_STACK_MMA") == "1"
+        assert info["tensor_cores"] == (1 if mx_tc else 0), info
+        assert info["stages"] % (1 if mx_tc else 2) == 0, info
     call = StackCall(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, T)
     rng = np.random.default_rng(5 + T)
     stream = torch.cuda.current_stream()
@@ -432,6 +437,49 @@ def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name, T, layers, layer
     if T == 1:
         assert arena.stats()["misses"] > 0
     no_device_error(gxlib)
+    plan.close()
+    arena.close()
+
+
+@pytest.mark.parametrize("tc", ["1", "0"])
+@pytest.mark.parametrize("T,layers,experts", [(1, 4, 16), (2, 3, 12), (8, 2, 16)])
+def test_stack_plan_mxfp4_tensor_and_cuda_cores(gxlib, orc, dev, monkeypatch, tc, T, layers, experts):
+    """gpt-oss-shaped MXFP4 stacks (hidden 2880, top-4) with the block dots on
+    the tensor cores (tcgen05 kind::f8f6f4, e4m3 activation digits) and on
+    the CUDA cores (the default, GX_STACK_MMA=0): both give the oracle's bits, through the
+    captured plan and after slot churn."""
+    from galactus_b200.moe import StackPlan
+    monkeypatch.setenv("GX_STACK_MMA", tc)
+    m = _small_model(gxlib, "gpt-oss-120b", experts=experts, layers=layers)
+    k = m.used
+    slots = k + 3 if T == 1 else m.experts   # churn at one token; every expert resident at more
+    arena = gxlib.Arena(m, capacity_bytes=slots * m.record * m.layers, policy=gxlib.POLICY_AUTO, max_tokens=T)
+    recs = [np.stack([orc.synth_record(m, m.seed, L, e) for e in range(m.experts)]) for L in range(m.layers)]
+    for L in range(m.layers):
+        for e in range(m.experts):
+            arena.load_record(L, e, recs[L][e])
+    x = torch.zeros((m.layers, T, m.hidden), dtype=torch.float32, device=dev)
+    w = torch.zeros((m.layers, T, k), dtype=torch.float32, device=dev)
+    out = torch.zeros((m.layers, T, m.hidden), dtype=torch.float32, device=dev)
+    ptr = lambda t: [t[L].data_ptr() for L in range(m.layers)]
+    plan = StackPlan(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, T)
+    info = plan.info()
+    assert info["stack_kernel"] == 1 and info["tensor_cores"] == (1 if tc == "1" else 0), info
+    rng = np.random.default_rng(90 + T)
+    stream = torch.cuda.current_stream()
+    for step in range(3):
+        xs = (rng.standard_normal((m.layers, T, m.hidden)) * (1.0 + 3.0 * step)).astype(np.float32)
+        ids = np.stack([_zipf_routes(rng, T, m.experts, k)[0] for _ in range(m.layers)]).astype(np.int32)
+        ws = rng.random((m.layers, T, k)).astype(np.float32)
+        x.copy_(torch.from_numpy(xs))
+        w.copy_(torch.from_numpy(ws))
+        out.fill_(float("nan"))
+        plan(np.ascontiguousarray(ids), stream)
+        got = H(out)
+        no_device_error(gxlib)
+        for L in range(m.layers):
+            want = orc.moe_layer(m, recs[L], xs[L], ids[L], ws[L])
+            np.testing.assert_array_equal(bits(got[L]), bits(want), err_msg=f"tc={tc} T={T} step {step} layer {L}")
     plan.close()
     arena.close()
 
