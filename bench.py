@@ -524,10 +524,13 @@ def stack_line(args, gx, torch, name, dev, local, stream, extras):
     arena, res = headline(args, gx, torch, sg, dev, local)
     peak, peak_kind = measured_peaks()
     dbytes, achieved = roofline_of(gx, model, 1, res["stack_ms"])
+    # DRAM traffic of one launch: the per-layer figure of an ncu capture of the
+    # same kernel and row types, times the layers streamed
     traffic = None
     tp = ROOT / "profiles" / "traffic.json"
     if tp.exists():
-        traffic = json.loads(tp.read_text()).get(model.name, {}).get("k_stack")
+        per_layer = json.loads(tp.read_text()).get(model.name, {}).get("k_stack_per_layer")
+        traffic = per_layer * model.layers if per_layer else None
     metric, config, dtype = single_config(gx, model)
     line = {
         "metric": metric, "value": args.steps / (res["ms"] / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
