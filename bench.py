@@ -840,6 +840,20 @@ def cpu_baseline_leg(args, gx, model, traces, cfg1_ids):
     return out
 
 
+def cached_record(cache, limit, key, make):
+    """The record of key from a bounded LRU cache (an OrderedDict, least
+    recently used first), made and inserted on a miss. The record is returned
+    before any later insertion can evict it."""
+    r = cache.get(key)
+    if r is None:
+        while len(cache) >= limit:
+            cache.popitem(last=False)
+        r = cache[key] = make()
+    else:
+        cache.move_to_end(key)
+    return r
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -855,19 +869,16 @@ def run_reference(args):
     # each step: one decode token through every layer of the stack; the
     # records are generated once (a bounded cache; the routes' locality makes
     # most of them repeat) and only the layer arithmetic is timed
-    cache: dict = {}
+    from collections import OrderedDict
+    cache: OrderedDict = OrderedDict()          # least recently used first
     limit = max(64, int(8e9 // model.record))
     times = []
     for t in range(args.warmup + args.steps):
         tt = 0.0
         for L in range(NL):
             ex = sorted(set(ids_all[t, L].tolist()))
-            for e in ex:
-                if (L, e) not in cache:
-                    if len(cache) >= limit:
-                        cache.pop(next(iter(cache)))
-                    cache[(L, e)] = orc.synth_record(model, model.seed, L, e)
-            recs = np.stack([cache[(L, e)] for e in ex])
+            recs = np.stack([cached_record(cache, limit, (L, e), lambda L=L, e=e: orc.synth_record(model, model.seed, L, e))
+                             for e in ex])
             remap = {e: i for i, e in enumerate(ex)}
             cid = np.array([[remap[e] for e in ids_all[t, L]]], np.int32)
             t0 = time.perf_counter()
