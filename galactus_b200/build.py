@@ -20,7 +20,7 @@ GEN = CSRC / "_gen"
 LIB = PKG / "libgalactus_b200.so"
 
 SOURCES = ["gx_kernels.cu", "gx_capi.cpp", "gx_policy.cpp", "gx_noalloc.cu", "gx_ep.cpp", "gx_plan.cpp", "gx_observer.cpp", "gx_gguf.cpp"]
-HEADERS = ["gx_device.cuh", "gx_moe.cuh", "gx_stack.cuh", "gx_prefill.cuh", "gx_mma.cuh", "gx_tc.cuh", "gx_stack_tc.cuh", "gx_router.cuh", "gx_formats.h", "gx_kernels.h", "gx_policy.hpp", "gx_observer.hpp"]
+HEADERS = ["gx_device.cuh", "gx_moe.cuh", "gx_stack.cuh", "gx_prefill.cuh", "gx_mma.cuh", "gx_tc.cuh", "gx_stack_tc.cuh", "gx_stack_tma.cuh", "gx_router.cuh", "gx_formats.h", "gx_kernels.h", "gx_policy.hpp", "gx_observer.hpp"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -160,6 +160,7 @@ struct gx_arena {
     int device = 0;
     std::vector<uint64_t> record, record_raw;
     std::vector<uint64_t> slab_base;    // device offset of each layer's slab
+    std::vector<std::vector<uint32_t>> slot_gen;   // per layer and slot: fills so far (copies of a plan's slot mirror follow it)
     std::vector<uint64_t> host_base;    // host-tier offset of each layer's records
     uint8_t * d_arena = nullptr;
     uint64_t arena_bytes = 0;
@@ -372,6 +373,7 @@ int gx_arena_create(const gx_arena_config * c, gx_arena ** out) {
         uint64_t off = 0, hoff = 0;
         for (uint32_t i = 0; i < n; ++i) {
             a->slab_base.push_back(off);
+            a->slot_gen.emplace_back(P.quota_of(P.first_layer() + i), 0u);
             off += a->record[i] * P.quota_of(P.first_layer() + i);
             a->host_base.push_back(hoff);
             hoff += a->record[i] * P.experts();
@@ -530,6 +532,7 @@ int arena_serve_impl(gx_arena * a, uint32_t layer, const int32_t * experts, uint
             const uint8_t * src = a->h_tier + a->host_base[i] + (uint64_t)m.first * a->record[i];
             if (cudaMemcpyAsync(dst, src, a->record_raw[i], cudaMemcpyHostToDevice, a->copy_stream) != cudaSuccess)
                 return GX_ERR_COPY;
+            ++a->slot_gen[i][(size_t)m.second];
             st.bytes_copied += a->record_raw[i];
         }
         ck(cudaEventRecord(a->ev_copy[i], a->copy_stream));
@@ -1386,6 +1389,12 @@ struct gx_stack_plan {
     std::vector<const float *> wp;      // the plan's router weight pointers
     int32_t * d_table = nullptr;        // [n, experts] slot of every expert, built once the layers are pinned
     int32_t * d_ids = nullptr;          // [n, T, k] router ids when the caller keeps none
+    // row mode 5: the layers' slots in the tensor-core record layout, kept in
+    // step with the arena's fills, and the TMA maps over their codes
+    uint8_t * d_shadow = nullptr;
+    std::vector<uint64_t> shadow_base;             // per layer: offset of its slots in d_shadow
+    std::vector<std::vector<uint32_t>> shadow_gen; // per layer and slot: the arena fill the copy follows
+    CUtensorMap * d_maps = nullptr;                // [n][3]
     std::vector<int32_t> h_ids;         // ids read back for the route trace
 };
 
@@ -1464,6 +1473,140 @@ bool choose_stack_tiles_tc(gx::StackParams & sp, int & threads, uint32_t & smem)
     return false;
 }
 
+// MXFP4 jobs on the tensor cores fed by TMA (row mode 5, gx_stack_tma.cuh):
+// 64 + 64 gate/up rows, 32 rows of each of k = 4 experts per down job, read
+// from a copy of the slots in the tensor-core record layout. Opt-in with
+// GX_STACK_MMA=2.
+bool choose_stack_tiles_t5(gx::StackParams & sp, int & threads, uint32_t & smem) {
+    const char * env = std::getenv("GX_STACK_MMA");
+    if (env == nullptr || std::strcmp(env, "2") != 0) return false;
+    if (sp.k != 4 || sp.H % 64 != 0 || sp.I % 64 != 0 || tensor_map_encoder() == nullptr) return false;
+    const gx::StackParams keep = sp;
+    const int nbh = sp.H / 32, nbi = sp.I / 32;
+    sp.row_mode = 5;
+    sp.Rg = 64;
+    sp.Rd = 32;
+    sp.W = 10;   // warps 4-13: epilogue, tails, two more MMA issuers and producers
+    sp.C = 1;
+    sp.alx.d_off = 64 * nbh;
+    sp.alx.bs_off = sp.alx.d_off;
+    sp.alx.pitch = gx::align16i((int64_t)sp.alx.d_off + std::max(2 * nbh, 256));
+    const int64_t tok = 64ll * sp.k * nbi + std::max(2ll * sp.k * nbi, 256ll);
+    const int64_t tok_al = (tok + 16 * sp.k - 1) / (16 * sp.k) * (16 * sp.k);
+    sp.ald.d_off = 64 * sp.k * nbi;
+    sp.ald.bs_off = sp.ald.d_off;
+    sp.ald.pitch = (int32_t)(tok_al / sp.k);
+    smem = gx::stack_layout(sp, threads);
+    if (smem != 0) return true;
+    sp = keep;
+    return false;
+}
+
+// The MXFP4 matrices of a layer's record: down (H rows of I), gate and up (I
+// rows of H), and their places in the tensor-core record (32-byte aligned).
+gx::Mxfp4TcMats mxfp4_mats(const LayerPlan & lp, int64_t * tc_record = nullptr) {
+    const uint8_t * base = lp.dn.w0;
+    gx::Mxfp4TcMats m{};
+    m.off[0] = 0;
+    m.off[1] = lp.g.w0 - base;
+    m.off[2] = lp.g.w1 - base;
+    m.rows[0] = (int32_t)lp.H;
+    m.rows[1] = m.rows[2] = (int32_t)lp.I;
+    m.nb[0] = (int32_t)(lp.I / 32);
+    m.nb[1] = m.nb[2] = (int32_t)(lp.H / 32);
+    m.trows[0] = 32;                 // down jobs: 32 rows of each expert
+    m.trows[1] = m.trows[2] = 64;    // gate/up jobs: 64 gate + 64 up rows
+    int64_t at = 0;
+    for (int q = 0; q < 3; ++q) {
+        m.doff[q] = at;
+        at += ((int64_t)m.rows[q] * (gx::mxfp4_tc_cstride(m.nb[q]) + m.nb[q]) + 31) / 32 * 32;
+    }
+    if (tc_record) *tc_record = at;
+    return m;
+}
+
+// The codes of one matrix of every slot of a layer in TMA-box order as a 5-D
+// tensor of 4-bit values (x: 128 elements = 4 blocks of a row, y: row of a
+// tile, z: chunk, w: tile, v: slot), unpacked by TMA into 16-byte groups of
+// 16 with the 128-byte swizzle; a box (128 elements x trows rows) is one
+// contiguous run.
+bool encode_codes_map(CUtensorMap * map, const void * base, int64_t nch, int64_t trows, int64_t tiles, int64_t slots,
+                      int64_t record) {
+    const auto enc = tensor_map_encoder();
+    if (enc == nullptr || (reinterpret_cast<uintptr_t>(base) & 31u) != 0 || record % 32 != 0) return false;
+    // row length a multiple of 128 elements, strides of 32 bytes (16U4_ALIGN16B)
+    const cuuint64_t dims[5] = {128u, (cuuint64_t)trows, (cuuint64_t)nch, (cuuint64_t)tiles, (cuuint64_t)slots};
+    const cuuint64_t strides[4] = {64u, (cuuint64_t)(64 * trows), (cuuint64_t)(64 * trows * nch), (cuuint64_t)record};
+    const cuuint32_t box[5] = {128u, (cuuint32_t)trows, 1u, 1u, 1u};
+    const cuuint32_t elem[5] = {1u, 1u, 1u, 1u, 1u};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 5, const_cast<void *>(base), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Slot `slot` of plan layer i into the tensor-core layout copy, on stream s,
+// when the arena has filled it since the copy was made.
+void t5_follow_slot(gx_stack_plan * p, uint32_t i, int32_t slot, cudaStream_t s) {
+    gx_arena * a = p->a;
+    const uint32_t li = p->lps[i].li;
+    uint32_t & gen = p->shadow_gen[i][(size_t)slot];
+    if (gen == a->slot_gen[li][(size_t)slot]) return;
+    int64_t trec = 0;
+    const gx::Mxfp4TcMats m = mxfp4_mats(p->lps[i], &trec);
+    ck(gx::launch_mxfp4_tc_layout(a->d_arena + a->slab_base[li] + (uint64_t)slot * a->record[li],
+                                  p->d_shadow + p->shadow_base[i] + (uint64_t)slot * (uint64_t)trec, m, s));
+    gen = a->slot_gen[li][(size_t)slot];
+}
+
+// Row mode 5: the slot copies in the tensor-core layout (every slot now),
+// their tensor maps, and the layer table pointed at the copies.
+int setup_t5(gx_stack_plan * p) {
+    gx_arena * a = p->a;
+    gx::StackParams & sp = p->sp;
+    uint64_t total = 0;
+    p->shadow_base.assign(p->n, 0);
+    p->shadow_gen.assign(p->n, {});
+    for (uint32_t i = 0; i < p->n; ++i) {
+        int64_t trec = 0;
+        mxfp4_mats(p->lps[i], &trec);
+        p->shadow_base[i] = total;
+        total += (uint64_t)trec * (uint64_t)p->lps[i].g.n_as;
+        p->shadow_gen[i].assign((size_t)p->lps[i].g.n_as, ~0u);
+    }
+    ck(cudaMalloc(&p->d_shadow, (size_t)total));
+    ck(cudaMemset(p->d_shadow, 0, (size_t)total));   // row padding reads as zero codes
+    std::vector<CUtensorMap> maps((size_t)p->n * 3);
+    for (uint32_t i = 0; i < p->n; ++i) {
+        const LayerPlan & lp = p->lps[i];
+        int64_t trec = 0;
+        const gx::Mxfp4TcMats m = mxfp4_mats(lp, &trec);
+        uint8_t * lb = p->d_shadow + p->shadow_base[i];
+        bool okm = true;
+        for (int q = 0; q < 3 && okm; ++q) {
+            const int idx = q == 0 ? 2 : q - 1;   // maps: gate, up, down
+            okm = m.rows[q] % m.trows[q] == 0 &&
+                  encode_codes_map(&maps[3 * i + idx], lb + m.doff[q], gx::mxfp4_tc_cstride(m.nb[q]) / 64, m.trows[q],
+                                   m.rows[q] / m.trows[q], lp.g.n_as, trec);
+        }
+        if (!okm) return GX_ERR_ALIGN;
+        gx::StackLayer & L = sp.layers[i];
+        L.wg = lb + m.doff[1];
+        L.wu = lb + m.doff[2];
+        L.wd = lb + m.doff[0];
+        L.nb02 = trec;
+    }
+    ck(cudaMalloc(&p->d_maps, maps.size() * sizeof(CUtensorMap)));
+    ck(cudaMemcpy(p->d_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
+    sp.t5_maps = p->d_maps;
+    // every slot now (a copy of what it holds, once its fills have landed),
+    // then in step with the arena's fills
+    ck(cudaStreamSynchronize(a->copy_stream));
+    for (uint32_t i = 0; i < p->n; ++i)
+        for (int32_t slot = 0; slot < p->lps[i].g.n_as; ++slot) t5_follow_slot(p, i, slot, nullptr);
+    ck(cudaDeviceSynchronize());
+    return GX_OK;
+}
+
 // Device buffers and the layer table of the stack kernel.
 int setup_stack(gx_stack_plan * p, const float * const * x, const float * const * w, float * const * out) {
     gx_arena * a = p->a;
@@ -1494,7 +1637,8 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     sp.need_grid = (l0.type_gate == gx::GX_T_IQ1_S || l0.type_down == gx::GX_T_IQ1_S) ? 1 : 0;
     int threads = 0;
     uint32_t smem = 0;
-    if (!(sp.row_mode == 3 && choose_stack_tiles_tc(sp, threads, smem)) && !choose_stack_tiles(sp, threads, smem))
+    if (!(sp.row_mode == 3 && (choose_stack_tiles_t5(sp, threads, smem) || choose_stack_tiles_tc(sp, threads, smem))) &&
+        !choose_stack_tiles(sp, threads, smem))
         return GX_ERR_ALIGN;
     sp.split = sp.row_mode == 3 ? 4 : (sp.row_mode == 1 || (sp.row_mode == 2 && sp.k * sp.Rd == 32)) ? 2 : 1;
     sp.n_gu = (int32_t)(p->T * p->k * (l0.I / sp.Rg));
@@ -1530,6 +1674,10 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     }
     sp.q_done = p->d_cnt;
     sp.gu_done = p->d_cnt + n;
+    if (sp.row_mode == 5) {
+        const int rc = setup_t5(p);
+        if (rc != GX_OK) return rc;
+    }
     p->threads = threads;
     p->smem = smem;
     p->per_sm = per_sm;
@@ -1639,6 +1787,8 @@ int gx_stack_plan_destroy(gx_stack_plan * p) {
     if (p->d_xq) cudaFree(p->d_xq);
     if (p->d_act) cudaFree(p->d_act);
     if (p->d_actq) cudaFree(p->d_actq);
+    if (p->d_shadow) cudaFree(p->d_shadow);
+    if (p->d_maps) cudaFree(p->d_maps);
     if (p->d_table) cudaFree(p->d_table);
     if (p->d_ids) cudaFree(p->d_ids);
     delete p;
@@ -1745,6 +1895,8 @@ int gx_stack_plan_run(gx_stack_plan * p, const int32_t * ids, void * stream, gx_
             const int rc = arena_serve(a, p->first + i, ids + (size_t)i * per, (uint32_t)per, h + (size_t)i * per,
                                        a->last_ev[li], s, &st, (uint32_t)p->T, (uint32_t)p->k);
             if (rc != GX_OK) return rc;
+            if (p->d_shadow)   // slots filled by this serve: their tensor-core copies, after the fill on s
+                for (int64_t j = 0; j < per; ++j) t5_follow_slot(p, i, h[(size_t)i * per + j], s);
             sum.hits += st.hits;
             sum.misses += st.misses;
             sum.evictions += st.evictions;
@@ -1798,7 +1950,7 @@ int gx_stack_plan_info_get(const gx_stack_plan * p, gx_stack_plan_info * info) {
         info->rows_gate_up = p->sp.Rg;
         info->rows_down = p->sp.Rd;
         info->smem_bytes = p->smem;
-        info->tensor_cores = p->sp.row_mode == 4 ? 1 : 0;
+        info->tensor_cores = p->sp.row_mode == 4 ? 1 : p->sp.row_mode == 5 ? 2 : 0;
     }
     return GX_OK;
 }

@@ -526,6 +526,40 @@ cudaError_t launch_add_inplace(float * out, const float * b, int64_t n, cudaStre
     return cudaGetLastError();
 }
 
+// MXFP4 matrices of one record into the tensor-core record layout
+// (Mxfp4TcMats). One thread per (row, block): byte reads of the 17-byte
+// block, one 16-byte store of its codes, one byte store of its scale.
+__global__ void k_mxfp4_tc_layout(const uint8_t * src, uint8_t * dst, Mxfp4TcMats m) {
+    int64_t n[3], tot = 0;
+    for (int q = 0; q < 3; ++q) {
+        n[q] = (int64_t)m.rows[q] * m.nb[q];
+        tot += n[q];
+    }
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < tot; i += (int64_t)gridDim.x * blockDim.x) {
+        int q = 0;
+        int64_t j = i;
+        while (j >= n[q]) j -= n[q++];
+        const int nb = m.nb[q];
+        const int64_t r = j / nb, bb = j - r * nb;
+        const uint8_t * blk = src + m.off[q] + r * (int64_t)(17 * nb) + 17 * bb;
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            w[k] = (uint32_t)blk[1 + 4 * k] | ((uint32_t)blk[2 + 4 * k] << 8) | ((uint32_t)blk[3 + 4 * k] << 16) |
+                   ((uint32_t)blk[4 + 4 * k] << 24);
+        const int64_t cs = mxfp4_tc_cstride(nb), nch = cs / 64, tr = m.trows[q];
+        const int64_t tile = r / tr, ri = r - tile * tr, c = bb / 4;
+        uint8_t * d = dst + m.doff[q];
+        *reinterpret_cast<uint4 *>(d + ((tile * nch + c) * tr + ri) * 64 + 16 * (bb - 4 * c)) = make_uint4(w[0], w[1], w[2], w[3]);
+        d[(int64_t)m.rows[q] * cs + r * nb + bb] = blk[0];
+    }
+}
+
+cudaError_t launch_mxfp4_tc_layout(const uint8_t * src, uint8_t * dst, const Mxfp4TcMats & m, cudaStream_t stream) {
+    k_mxfp4_tc_layout<<<1184, 256, 0, stream>>>(src, dst, m);   // 8 CTAs per SM of a B200, grid-stride
+    return cudaGetLastError();
+}
+
 cudaError_t launch_fill(float * dst, int64_t n, float v, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     k_fill<<<grid_1d(n, 256), 256, 0, stream>>>(dst, n, v);
@@ -775,7 +809,44 @@ static bool stack_copy_mode(int64_t nb01, int R, int32_t & row_copy, int32_t & p
 // Q8_0 rows, 2 two-lane Q4_K gate/up and Q6_K down rows (both in 4 staggered
 // gate/up tiles and rows of K % 256 == 0), 1 octet rows (any whole number
 // of their type's 64- or 256-element units, checked per layer; 2 gate/up copies).
+// Row mode 5 (gx_stack_tma.cuh): 64 + 64 gate/up rows, 32 rows of each of 4
+// experts per down job, 4 epilogue warps, no weight stage of the generic
+// layout (its ring is the region at tc_off: as many 16 KB chunk stages as fit).
+static uint32_t stack_layout_t5(StackParams & p, int & threads) {
+    if (p.Rg != 64 || p.Rd != 32 || p.k != 4 || p.W != 10 || p.C != 1) return 0;
+    if (p.H % 64 || p.I % 64 || p.H / 32 > kTcMaxBlocks || p.I / 32 > kTcMaxBlocks) return 0;
+    if (p.NL < 1 || p.NL > kStackMaxLayers) return 0;
+    if (p.alx.d_off != 64 * (p.H / 32) || p.ald.d_off != 64 * p.k * (p.I / 32) || p.alx.pitch < p.alx.d_off + 256 ||
+        p.alx.pitch < p.alx.d_off + 2 * (p.H / 32) || (int64_t)p.k * p.ald.pitch < p.ald.d_off + 256 ||
+        (int64_t)p.k * p.ald.pitch < p.ald.d_off + 2 * p.k * (p.I / 32))
+        return 0;
+    threads = 32 * (kStackProducers + 2) + 32 * p.W;
+    p.stage_bytes = 0;
+    p.row_copy_d = 0;
+    p.pitch_d = (int32_t)p.nb01_d;
+    p.bar_off = 0;
+    p.meta_off = (uint32_t)align_up(8ull * (3 * kStackMaxConsumers + 2 * kStackBufs), 128);
+    p.stage_off = p.meta_off + (uint32_t)align_up(4ull * (3 * kStackMaxConsumers + 2 * kStackBufs + 1), 128);
+    p.tc_off = p.stage_off;
+    p.nbuf_d = 1;
+    const int nbmax = (p.H > p.I ? p.H : p.I) / 32;
+    const uint64_t rest = align_up((uint64_t)kStackBufs * p.alx.pitch, 128) + align_up((uint64_t)p.k * p.ald.pitch, 128) +
+                          (uint64_t)p.NL * 32u + (uint64_t)p.C * 32u * 4u + align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
+    int stages = kT5StagesMax;
+    while (stages >= kT5StagesMin && p.tc_off + align_up(t5_bytes(nbmax, stages), 128) + rest > kMaxSmem) --stages;
+    if (stages < kT5StagesMin) return 0;
+    p.tc_na = stages;
+    p.xbuf_off = p.tc_off + (uint32_t)align_up(t5_bytes(nbmax, stages), 128);
+    p.dbuf_off = p.xbuf_off + (uint32_t)align_up((uint64_t)kStackBufs * p.alx.pitch, 128);
+    p.wt_off = p.dbuf_off + (uint32_t)align_up((uint64_t)p.k * p.ald.pitch, 128);
+    p.dots_off = p.wt_off + (uint32_t)p.NL * 32u;
+    p.slots_off = p.dots_off + (uint32_t)p.C * 32u * 4u;
+    p.grid_off = p.slots_off + (uint32_t)align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
+    return p.grid_off <= kMaxSmem ? p.grid_off : 0;
+}
+
 uint32_t stack_layout(StackParams & p, int & threads) {
+    if (p.row_mode == 5) return stack_layout_t5(p, threads);
     const bool mx = p.row_mode == 3 || p.row_mode == 4;
     if (!(p.Rg == 8 || (p.Rg == 16 && mx)) || p.Rd < 1 || (p.k * p.Rd != 32 && !(p.row_mode == 2 && p.k * p.Rd == 16)))
         return 0;
@@ -871,7 +942,7 @@ uint32_t stack_layout(StackParams & p, int & threads) {
     return total <= kMaxSmem ? total : 0;
 }
 
-template <int TG, int TD, bool TC = false>
+template <int TG, int TD, int TC = 0>
 static cudaError_t stack_dispatch(const StackParams * p, int grid, int threads, uint32_t smem, cudaStream_t stream,
                                   int * per_sm) {
     if (per_sm) return resident_per_sm(k_stack<TG, TD, TC>, threads, smem, *per_sm);
@@ -894,8 +965,9 @@ static cudaError_t stack_switch(int tg, int td, const StackParams * p, int grid,
     if (tg == GX_T_Q8_0 && td == GX_T_Q8_0) return stack_dispatch<GX_T_Q8_0, GX_T_Q8_0>(p, grid, threads, smem, stream, per_sm);
     if (tg == GX_T_Q4_K && td == GX_T_Q6_K) return stack_dispatch<GX_T_Q4_K, GX_T_Q6_K>(p, grid, threads, smem, stream, per_sm);
     if (tg == GX_T_MXFP4 && td == GX_T_MXFP4)
-        return p->row_mode == 4 ? stack_dispatch<GX_T_MXFP4, GX_T_MXFP4, true>(p, grid, threads, smem, stream, per_sm)
-                                : stack_dispatch<GX_T_MXFP4, GX_T_MXFP4>(p, grid, threads, smem, stream, per_sm);
+        return p->row_mode == 4   ? stack_dispatch<GX_T_MXFP4, GX_T_MXFP4, 4>(p, grid, threads, smem, stream, per_sm)
+               : p->row_mode == 5 ? stack_dispatch<GX_T_MXFP4, GX_T_MXFP4, 5>(p, grid, threads, smem, stream, per_sm)
+                                  : stack_dispatch<GX_T_MXFP4, GX_T_MXFP4>(p, grid, threads, smem, stream, per_sm);
     if (tg == GX_T_IQ1_S && td == GX_T_IQ1_S)
         return stack_dispatch<GX_T_IQ1_S, GX_T_IQ1_S>(p, grid, threads, smem, stream, per_sm);
     return cudaErrorInvalidValue;

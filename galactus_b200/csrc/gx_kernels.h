@@ -126,7 +126,7 @@ constexpr int kStackMaxLayers = 128;   // the layer table travels in the kernel 
 constexpr int kStackBufs = 2;          // activation buffers per kind (gate/up inputs, down inputs)
 
 struct StackParams {
-    int32_t * q_done;          // [NL]   1 once x_L is quantized
+    int32_t * q_done;          // [NL]   1 once x_L is quantized (row mode 5: its blocks quantized, T*H/32 when done)
     int32_t * gu_done;         // [NL*T] quantized down-input blocks per token (k*I/qblk when complete)
     int32_t NL, k, T, H, I;
     int64_t nb01_g, nb01_d;    // gate/up and down row bytes
@@ -153,9 +153,10 @@ struct StackParams {
     int32_t split;             // warps per job: 4 for MXFP4 jobs, 2 for octet jobs and 32-row two-lane K-quant
                                // down jobs, else 1
     uint32_t grid_off;
-    uint32_t tc_off;           // row mode 4: A tiles, block scales, pair terms, mbarriers and the TMEM address
+    uint32_t tc_off;           // row modes 4, 5: their shared-memory region
     int32_t nbuf_d;            // down-input buffers (kStackBufs, or 1 in row mode 4)
-    int32_t tc_na;             // row mode 4: A-tile slots (MMA steps in flight)
+    int32_t tc_na;             // row mode 4: A-tile slots (MMA steps in flight); row mode 5: ring stages
+    const CUtensorMap * t5_maps;   // row mode 5: [NL][3] codes of gate (64-row boxes), up (64), down (32)
     StackLayer layers[kStackMaxLayers];
 };
 
@@ -256,6 +257,21 @@ cudaError_t launch_fill(float * dst, int64_t n, float v, cudaStream_t stream);
 cudaError_t launch_gather_ptrs(const float * const * ptrs, const int32_t * layers, const int32_t * rows, int64_t n,
                                int64_t H, float * dst, cudaStream_t stream);
 // out[i] = out[i] + b[i] (one rounding per element)
+// One record's MXFP4 matrices (down, gate, up) for the tensor-core layout:
+// per matrix the codes in TMA-box order [tile of trows rows][chunk of 4
+// blocks][row of the tile][64 bytes: the 16 code bytes of each of the 4
+// blocks] (each box one contiguous run; rows padded to whole chunks), then
+// the block scales [rows][nb].
+struct Mxfp4TcMats {
+    int64_t off[3];    // matrix offsets in the source (GGUF) record
+    int64_t doff[3];   // matrix offsets in the tensor-core record
+    int32_t rows[3];
+    int32_t nb[3];     // 32-element blocks per row
+    int32_t trows[3];  // rows per tile (TMA box rows)
+};
+// code bytes per row of nb blocks in the tensor-core layout (whole chunks)
+GX_HD constexpr int32_t mxfp4_tc_cstride(int32_t nb) { return ((nb + 3) / 4) * 64; }
+cudaError_t launch_mxfp4_tc_layout(const uint8_t * src, uint8_t * dst, const Mxfp4TcMats & m, cudaStream_t stream);
 cudaError_t launch_add_inplace(float * out, const float * b, int64_t n, cudaStream_t stream);
 // router: logits [rows, ld] -> ids/w [rows, k] (+ slots through table); rows = n_layers * T
 constexpr int kRouterWarps = 4;

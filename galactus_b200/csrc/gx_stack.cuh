@@ -742,15 +742,15 @@ __device__ __forceinline__ void stack_d_oct(const StackParams & p, const uint8_t
 // K % (kStackBufs, or nbuf_d for down inputs). Walking the CTA's jobs of its kind in order (their keys
 // never decrease), the producer counts the jobs of each buffer; at each new
 // key it waits until every job of the buffer's previous key is done, waits
-// for the rows to exist (x_L quantized, or every Q8 block of the token's
-// activations), copies them in and publishes the fill word (K << 1 | phase
+// for the rows to exist (x_L quantized: q_done[L] reaches q_target, or every
+// Q8 block of the token's activations), copies them in and publishes the fill word (K << 1 | phase
 // parity). A consumer spins until its buffer's fill word names its key, then
 // waits on the buffer barrier with that parity: the fill of K is issued only
 // after every job of the buffer's previous key has finished, so the barrier
 // is never two phases behind a waiting consumer and its parity is unambiguous.
 __device__ __forceinline__ void stack_input_producer(const StackParams & p, int kind, int mine, int b, int G,
                                                      uint64_t * bbar, volatile int * fillw, volatile int * bufdone,
-                                                     uint8_t * buf, int buf_bytes) {
+                                                     uint8_t * buf, int buf_bytes, int q_target) {
     const StackGeom g = stack_geom(p);
     const int blocks_per_token = p.k * (p.I / p.qblk);   // quantized down-input blocks of a token
     const int nb = kind == 1 ? p.nbuf_d : kStackBufs;       // buffers of this kind
@@ -777,7 +777,7 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
                 if (!ok && (i & 63u) == 63u && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) break;
                 if (!ok && i >= 16) __nanosleep(64);
             }
-            if (ok) ok = kind == 0 ? stack_wait(p.q_done + J.L, 1) : stack_wait(p.gu_done + K, blocks_per_token);
+            if (ok) ok = kind == 0 ? stack_wait(p.q_done + J.L, q_target) : stack_wait(p.gu_done + K, blocks_per_token);
             if (!ok) {
                 record_error(GX_DEVERR_TIMEOUT);
                 break;
@@ -809,17 +809,21 @@ __device__ __forceinline__ void stack_input_producer(const StackParams & p, int 
 }  // namespace gx
 
 #include "gx_stack_tc.cuh"
+#include "gx_stack_tma.cuh"
 
 namespace gx {
 
-// TC: MXFP4 jobs on the tensor cores (row mode 4, one weight producer, the
-// roles of gx_stack_tc.cuh on warps 1 and 4-15)
-template <int TG, int TD, bool TC = false>
-__global__ void __launch_bounds__(TC ? kTcThreads : 32 * (kStackProducers + 2) + 32 * stack_max_warps(TG == GX_T_MXFP4 ? 3 : 0), 1)
+// TCM: MXFP4 jobs on the tensor cores, row mode 4 (one weight producer, the
+// roles of gx_stack_tc.cuh on warps 1 and 4-15) or row mode 5 (the roles of
+// gx_stack_tma.cuh on warps 0, 1 and 4-13); 0 for the CUDA-core row modes
+template <int TG, int TD, int TCM = 0>
+__global__ void __launch_bounds__(TCM == 4 ? kTcThreads : TCM == 5 ? kT5Threads
+                                  : 32 * (kStackProducers + 2) + 32 * stack_max_warps(TG == GX_T_MXFP4 ? 3 : 0), 1)
     k_stack(const __grid_constant__ StackParams p) {
     // row mode: 0 two-lane Q8_0 rows, 2 two-lane Q4_K gate/up + Q6_K down rows, 1 octet rows,
     // 3 MXFP4 rows on the CUDA cores, 4 MXFP4 rows on the tensor cores
-    constexpr int kMode = TC ? 4
+    constexpr bool TC = TCM != 0;
+    constexpr int kMode = TC ? TCM
                           : (TG == GX_T_Q8_0 && TD == GX_T_Q8_0) ? 0
                           : (TG == GX_T_Q4_K && TD == GX_T_Q6_K) ? 2
                           : (TG == GX_T_MXFP4 && TD == GX_T_MXFP4) ? 3
@@ -880,12 +884,21 @@ __global__ void __launch_bounds__(TC ? kTcThreads : 32 * (kStackProducers + 2) +
     }
     if (tid == 0) {
         for (int s = 0; s < 2 * C + 2 * kStackBufs; ++s) mbar_init(wfull + s, 1);
-        if constexpr (TC) tc_init_bars(tc_team(smem, p.tc_off, (p.H > p.I ? p.H : p.I) / 32, p.tc_na));
+        if constexpr (TCM == 4) tc_init_bars(tc_team(smem, p.tc_off, (p.H > p.I ? p.H : p.I) / 32, p.tc_na));
+        if constexpr (TCM == 5) t5_init_bars(t5_team(smem, p.tc_off, (p.H > p.I ? p.H : p.I) / 32, p.tc_na));
         mbar_fence_init();
     }
     __syncthreads();
 
-    if (TC && warp > 0 && warp < kStackProducers) {
+    if constexpr (TCM == 5) {
+        // row mode 5: the TMA producer (warp 0) and the MMA issuer (warp 1)
+        if (warp < kStackProducers) {
+            stack_t5(p, smem, warp, lane, b, G, mine, slots, wt, xbar, dbar, fillw, bufdone, smem + p.xbuf_off,
+                     smem + p.dbuf_off);
+            return;
+        }
+    }
+    if (TCM == 4 && warp > 0 && warp < kStackProducers) {
         // one weight producer; warp 1 issues the MMAs
         stack_tc(p, smem, warp, lane, b, G, mine, wfull, empty, xbar, dbar, fillw, bufdone, rel, smem + p.stage_off,
                  smem + p.xbuf_off, smem + p.dbuf_off);
@@ -940,14 +953,23 @@ __global__ void __launch_bounds__(TC ? kTcThreads : 32 * (kStackProducers + 2) +
         // -------------------------------------------------- input producers
         if (lane != 0) return;
         const int kind = warp - kStackProducers;
+        // row mode 5 counts x blocks quantized anywhere in the grid; the
+        // others flag a layer once its owner CTA quantized all of it
+        const int q_target = TCM == 5 ? p.T * (p.H / 32) : 1;
         stack_input_producer(p, kind, mine, b, G, kind == 0 ? xbar : dbar, fillw + kind * kStackBufs,
-                             bufdone + kind * kStackBufs, kind == 0 ? xbuf : dbuf, kind == 0 ? xbytes : dbytes);
+                             bufdone + kind * kStackBufs, kind == 0 ? xbuf : dbuf, kind == 0 ? xbytes : dbytes,
+                             q_target);
         return;
     }
 
-    if constexpr (TC) {
+    if constexpr (TCM == 4) {
         // ------------------------------------------ tensor-core roles
         stack_tc(p, smem, warp, lane, b, G, mine, wfull, empty, xbar, dbar, fillw, bufdone, rel, stages, xbuf, dbuf);
+        return;
+    }
+    if constexpr (TCM == 5) {
+        // ------------------------------------------ epilogue warps of row mode 5
+        stack_t5(p, smem, warp, lane, b, G, mine, slots, wt, xbar, dbar, fillw, bufdone, xbuf, dbuf);
         return;
     }
     // ------------------------------------------------------------ consumers

@@ -64,6 +64,17 @@ __device__ __forceinline__ void tma_load_3d(void * dst, const CUtensorMap * map,
         : "memory");
 }
 
+// A 5-D tile of the tensor map into shared memory (no multicast: the
+// weights are this GPU's own memory)
+__device__ __forceinline__ void tma_load_5d(void * dst, const CUtensorMap * map, int x0, int x1, int x2, int x3, int x4,
+                                            uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x0), "r"(x1), "r"(x2), "r"(x3), "r"(x4), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // 32 consecutive 32-bit columns of this thread's TMEM lane
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
@@ -86,6 +97,17 @@ __device__ __forceinline__ uint64_t umma_desc(const void * smem, uint32_t lbo, u
     const uint32_t a = smem_u32(smem);
     return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// Shared-memory matrix descriptor of a K-major operand in the 128-byte
+// swizzled layout that TMA writes with CU_TENSOR_MAP_SWIZZLE_128B: rows of
+// 128 bytes, the 16-byte chunks of row r XOR-ed with r % 8, 8-row atoms of
+// 1024 bytes sbo apart (atoms 1024-byte aligned, base offset 0); a K step
+// inside the row advances the start address (version 1, layout type 2).
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void * smem, uint32_t sbo) {
+    const uint32_t a = smem_u32(smem);
+    return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) |
+           (1ull << 46) | (2ull << 61);
 }
 
 // instruction descriptor: s32 accumulator, signed int8 A and B, both K-major

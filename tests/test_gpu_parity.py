@@ -441,13 +441,15 @@ def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name, T, layers, layer
     arena.close()
 
 
-@pytest.mark.parametrize("tc", ["1", "0"])
+@pytest.mark.parametrize("tc", ["2", "1", "0"])
 @pytest.mark.parametrize("T,layers,experts", [(1, 4, 16), (2, 3, 12), (8, 2, 16)])
 def test_stack_plan_mxfp4_tensor_and_cuda_cores(gxlib, orc, dev, monkeypatch, tc, T, layers, experts):
     """gpt-oss-shaped MXFP4 stacks (hidden 2880, top-4) with the block dots on
-    the tensor cores (tcgen05 kind::f8f6f4, e4m3 activation digits) and on
-    the CUDA cores (the default, GX_STACK_MMA=0): both give the oracle's bits, through the
-    captured plan and after slot churn."""
+    the tensor cores (tcgen05 kind::f8f6f4, e4m3 activation digits) fed by TMA
+    from the slots' tensor-core copies (GX_STACK_MMA=2) or repacked by the CUDA
+    cores (1), and on the CUDA cores (the default, 0): all give the oracle's
+    bits, through the captured plan and after slot churn (the copies follow
+    the arena's fills)."""
     from galactus_b200.moe import StackPlan
     monkeypatch.setenv("GX_STACK_MMA", tc)
     m = _small_model(gxlib, "gpt-oss-120b", experts=experts, layers=layers)
@@ -464,7 +466,7 @@ def test_stack_plan_mxfp4_tensor_and_cuda_cores(gxlib, orc, dev, monkeypatch, tc
     ptr = lambda t: [t[L].data_ptr() for L in range(m.layers)]
     plan = StackPlan(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, T)
     info = plan.info()
-    assert info["stack_kernel"] == 1 and info["tensor_cores"] == (1 if tc == "1" else 0), info
+    assert info["stack_kernel"] == 1 and info["tensor_cores"] == int(tc), info
     rng = np.random.default_rng(90 + T)
     stream = torch.cuda.current_stream()
     for step in range(3):
