@@ -1486,7 +1486,7 @@ bool choose_stack_tiles_t5(gx::StackParams & sp, int & threads, uint32_t & smem)
     sp.row_mode = 5;
     sp.Rg = 64;
     sp.Rd = 32;
-    sp.W = 10;   // warps 4-13: epilogue, tails, two more MMA issuers and producers
+    sp.W = gx::kT5Warps - 4;   // warps 4..: epilogue, tails, more MMA issuers and producers
     sp.C = 1;
     sp.alx.d_off = 64 * nbh;
     sp.alx.bs_off = sp.alx.d_off;

@@ -813,7 +813,7 @@ static bool stack_copy_mode(int64_t nb01, int R, int32_t & row_copy, int32_t & p
 // experts per down job, 4 epilogue warps, no weight stage of the generic
 // layout (its ring is the region at tc_off: as many 16 KB chunk stages as fit).
 static uint32_t stack_layout_t5(StackParams & p, int & threads) {
-    if (p.Rg != 64 || p.Rd != 32 || p.k != 4 || p.W != 10 || p.C != 1) return 0;
+    if (p.Rg != 64 || p.Rd != 32 || p.k != 4 || p.W != kT5Warps - 4 || p.C != 1) return 0;
     if (p.H % 64 || p.I % 64 || p.H / 32 > kTcMaxBlocks || p.I / 32 > kTcMaxBlocks) return 0;
     if (p.NL < 1 || p.NL > kStackMaxLayers) return 0;
     if (p.alx.d_off != 64 * (p.H / 32) || p.ald.d_off != 64 * p.k * (p.I / 32) || p.alx.pitch < p.alx.d_off + 256 ||
@@ -828,17 +828,29 @@ static uint32_t stack_layout_t5(StackParams & p, int & threads) {
     p.meta_off = (uint32_t)align_up(8ull * (3 * kStackMaxConsumers + 2 * kStackBufs), 128);
     p.stage_off = p.meta_off + (uint32_t)align_up(4ull * (3 * kStackMaxConsumers + 2 * kStackBufs + 1), 128);
     p.tc_off = p.stage_off;
-    p.nbuf_d = 1;
     const int nbmax = (p.H > p.I ? p.H : p.I) / 32;
-    const uint64_t rest = align_up((uint64_t)kStackBufs * p.alx.pitch, 128) + align_up((uint64_t)p.k * p.ald.pitch, 128) +
-                          (uint64_t)p.NL * 32u + (uint64_t)p.C * 32u * 4u + align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
-    int stages = kT5StagesMax;
-    while (stages >= kT5StagesMin && p.tc_off + align_up(t5_bytes(nbmax, stages), 128) + rest > kMaxSmem) --stages;
-    if (stages < kT5StagesMin) return 0;
+    // the most stages that fit, a multiple of kT5StageStep (gx_stack_tma.cuh),
+    // with two down-input buffers where they fit (a down job's inputs then
+    // load during the job before), else one
+    const auto rest = [&](int nbd) {
+        return align_up((uint64_t)kStackBufs * p.alx.pitch, 128) + align_up((uint64_t)nbd * p.k * p.ald.pitch, 128) +
+               (uint64_t)p.NL * 32u + (uint64_t)p.C * 32u * 4u + align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
+    };
+    int stages = kT5StagesMax / kT5StageStep * kT5StageStep, nbd = 2;
+    while (stages >= kT5StagesMin && p.tc_off + align_up(t5_bytes(nbmax, stages), 128) + rest(nbd) > kMaxSmem) {
+        if (nbd == 2) {
+            nbd = 1;
+        } else {
+            nbd = 2;
+            stages -= kT5StageStep;
+        }
+    }
+    if (stages < kT5StagesMin || stages % kT5StageStep != 0) return 0;
     p.tc_na = stages;
+    p.nbuf_d = nbd;
     p.xbuf_off = p.tc_off + (uint32_t)align_up(t5_bytes(nbmax, stages), 128);
     p.dbuf_off = p.xbuf_off + (uint32_t)align_up((uint64_t)kStackBufs * p.alx.pitch, 128);
-    p.wt_off = p.dbuf_off + (uint32_t)align_up((uint64_t)p.k * p.ald.pitch, 128);
+    p.wt_off = p.dbuf_off + (uint32_t)align_up((uint64_t)nbd * p.k * p.ald.pitch, 128);
     p.dots_off = p.wt_off + (uint32_t)p.NL * 32u;
     p.slots_off = p.dots_off + (uint32_t)p.C * 32u * 4u;
     p.grid_off = p.slots_off + (uint32_t)align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);

@@ -256,7 +256,12 @@ cudaError_t launch_fill(float * dst, int64_t n, float v, cudaStream_t stream);
 // dst[j] = row rows[j] of the [*, H] matrix at ptrs[layers[j]] (gather over a pointer table)
 cudaError_t launch_gather_ptrs(const float * const * ptrs, const int32_t * layers, const int32_t * rows, int64_t n,
                                int64_t H, float * dst, cudaStream_t stream);
-// out[i] = out[i] + b[i] (one rounding per element)
+// Row mode 5 (TMA-fed tensor-core MXFP4 stack jobs): MMA issuer warps (1,
+// 10, 11, then 14, ...) and the CTA's warps (2 chunk producers, a scale
+// producer, 2 input producers, 4 epilogue and 2 tail warps besides the issuers)
+constexpr int kT5Issuers = 4;
+constexpr int kT5Warps = 11 + kT5Issuers;
+
 // One record's MXFP4 matrices (down, gate, up) for the tensor-core layout:
 // per matrix the codes in TMA-box order [tile of trows rows][chunk of 4
 // blocks][row of the tile][64 bytes: the 16 code bytes of each of the 4
@@ -272,6 +277,7 @@ struct Mxfp4TcMats {
 // code bytes per row of nb blocks in the tensor-core layout (whole chunks)
 GX_HD constexpr int32_t mxfp4_tc_cstride(int32_t nb) { return ((nb + 3) / 4) * 64; }
 cudaError_t launch_mxfp4_tc_layout(const uint8_t * src, uint8_t * dst, const Mxfp4TcMats & m, cudaStream_t stream);
+// out[i] = out[i] + b[i] (one rounding per element)
 cudaError_t launch_add_inplace(float * out, const float * b, int64_t n, cudaStream_t stream);
 // router: logits [rows, ld] -> ids/w [rows, k] (+ slots through table); rows = n_layers * T
 constexpr int kRouterWarps = 4;

@@ -2,16 +2,17 @@
 //
 // The rows come from a copy of the layer's slots in the tensor-core record
 // layout (Mxfp4TcMats): per matrix, the 16 code bytes of every block of a row
-// side by side in TMA-box order (tile, chunk of 4 blocks, row: each box one
-// contiguous 4 KB run), then the block scale bytes ([rows][nb]). TMA loads the codes with data type 16U4_ALIGN16B, which
+// side by side in TMA-box order (tile, group of 4 blocks, row: each box one
+// contiguous run of 64 bytes per row), then the block scale bytes
+// ([rows][nb]). TMA loads the codes with data type 16U4_ALIGN16B, which
 // writes each 16 codes (8 bytes) into 16 bytes of shared memory, the
 // unpacked e2m1 operand of tcgen05.mma kind::f8f6f4, and with the 128-byte
 // swizzle the UMMA descriptor reads: no CUDA core touches a weight byte. A
 // job is 128 rows (64 gate + 64 up rows of one (token, slot) pair, or 32
 // rows of each of the k = 4 experts of a token's down projection); a chunk
-// is 4 blocks (128 K elements, a 16 KB tile), and each block is one
-// M=128 x N=16 x K=32 MMA against the activation's e4m3 digit columns (hi,
-// lo; q = 16*hi + lo, exact) in TMEM columns of its own.
+// is 4 blocks (128 K elements, a 16 KB tile), and each
+// block is one M=128 x N=16 x K=32 MMA against the activation's e4m3 digit
+// columns (hi, lo; q = 16*hi + lo, exact) in TMEM columns of its own.
 //
 // The arithmetic is that of ggml_vec_dot_mxfp4_q8_0 (diff:1209-1240): the
 // block's integer dot sumi = 2*(16*D_hi + D_lo) (exact: every partial is a
@@ -19,17 +20,17 @@
 // t = fma(sc_e, sumi_e, sc_o*sumi_o) and the chain sumf += t in pair order,
 // each row in its own lane from the first chunk to the last.
 //
-// Warps (448 threads):
+// Warps (kT5Warps, 32 * (11 + kT5Issuers) threads):
 //   0, 13   chunk producers (lane 0): producer i takes the chunks gc = i
 //           (mod 2), the TMA tiles (2 boxes of 64 rows, or 4 of 32 rows, one
 //           per expert slot) into the ring;
 //   12      scale producer (lane 0): per job the scale bytes of its rows (one
 //           bulk copy per 64 or 32 rows), a job ahead of the epilogue;
-//   1, 10, 11  MMA issuers: issuer i takes the chunks gc = i (mod 3) of the
-//           CTA's chunk sequence, so that one chunk's waits and commits overlap
-//           the next chunk's MMAs; the whole warp walks the chunks (its
-//           descriptors stay warp-uniform), lane 0 issues per chunk 4 MMAs and
-//           2 commits (TMEM slot full, ring stage empty);
+//   1, 10, 11, 14..  MMA issuers: issuer i takes the chunks gc = i (mod
+//           kT5Issuers) of the CTA's chunk sequence, so that one chunk's waits
+//           and commits overlap other chunks' MMAs; the whole warp walks the
+//           chunks (its descriptors stay warp-uniform), lane 0 issues per
+//           chunk 4 MMAs and 2 commits (TMEM slot full, ring stage empty);
 //   2, 3    input producers (the digit rows of x and of the down inputs);
 //   4-7     epilogue warp s, TMEM lanes 32s..32s+31 = rows 32s..32s+31 of the
 //           job: the pair terms and the chain of its rows (the next chunk's
@@ -53,14 +54,32 @@
 namespace gx {
 
 constexpr int kT5Chunk = 4;                    // MXFP4 blocks per chunk (128 K elements)
-constexpr uint32_t kT5Tile = 128u * 128u;      // 128 rows x 128 swizzled bytes
-constexpr int kT5StagesMin = 4, kT5StagesMax = 12;
+constexpr int kT5Sub = 4;                      // blocks per TMA box (one 128-byte swizzled row of 128 codes)
+constexpr int kT5Subs = kT5Chunk / kT5Sub;     // sub-tiles per chunk
+constexpr uint32_t kT5SubTile = 128u * 128u;   // 128 rows x 128 swizzled bytes: 4 blocks of the job's rows
+constexpr uint32_t kT5Tile = kT5Subs * kT5SubTile;
+constexpr int kT5StagesMin = 4, kT5StagesMax = 12;   // (a multiple of kT5StageStep, below)
 constexpr int kT5TSlots = 8;                   // TMEM slots (chunks)
 constexpr int kT5N = 16;                       // MMA N (digit columns: 2 per activation row, k = 4 rows)
 constexpr int kT5Cols = kT5TSlots * kT5Chunk * kT5N;   // 512
-constexpr int kT5Threads = 448;
-constexpr int kT5Issuers = 3;                  // warps 1, 10, 11
 constexpr int kT5Producers = 2;                // warps 0, 13
+constexpr int kT5Threads = 32 * kT5Warps;
+// Every wait names the barrier's phase by its parity, which is unambiguous
+// only while the waiter is at most one phase ahead of the barrier. A role
+// that takes every n-th chunk could otherwise run a whole ring ahead of
+// another role's chunk on the same stage and read an older, still incomplete
+// phase as complete. So the ring's stage count is a multiple of both the
+// issuer and the producer counts, and the TMEM slot count a multiple of the
+// issuer count: the previous use of every stage and slot a role waits on was
+// that role's own chunk, which it has already waited for.
+constexpr int t5_gcd(int a, int b) { return b == 0 ? a : t5_gcd(b, a % b); }
+constexpr int kT5StageStep = kT5Issuers / t5_gcd(kT5Issuers, kT5Producers) * kT5Producers;
+static_assert(kT5TSlots % kT5Issuers == 0, "TMEM slots: a multiple of the issuer count");
+
+// issuer index of warp w (-1: not an issuer)
+__host__ __device__ constexpr int t5_issuer_index(int w) {
+    return w == 1 ? 0 : (w == 10 || w == 11) ? w - 9 : (w >= 14 && w < kT5Warps) ? w - 11 : -1;
+}
 constexpr uint32_t kT5Bars = 2 * kT5StagesMax + 2 * kT5TSlots + 8 + 1;
 // full[S], empty[S], tfull[8], tempty[8], sfull[2], sfree[2], xfull[2], xfree[2], fin
 
@@ -189,6 +208,7 @@ __device__ __forceinline__ void t5_producer(const StackParams & p, const T5Team 
         const StackJob J = stack_job(g, b + jl * G);
         const int32_t * sl = slots + J.L * p.T * p.k + J.pair;
         const int NB = (J.gu ? p.H : p.I) / 32, nch = (NB + kT5Chunk - 1) / kT5Chunk;
+        const int nsub_all = (NB + kT5Sub - 1) / kT5Sub;   // boxes along the row
         const CUtensorMap * mp = p.t5_maps + 3 * J.L;
         const int tile_y = J.gu ? J.r0 / 64 : J.r0 / 32;
         int sk[4];
@@ -201,17 +221,21 @@ __device__ __forceinline__ void t5_producer(const StackParams & p, const T5Team 
                     break;
                 }
                 uint8_t * tile = tm.ring + st * kT5Tile;
+                const int nsub = min(kT5Subs, nsub_all - kT5Subs * c);
                 // the transaction bytes of 16U4_ALIGN16B boxes count the packed 4-bit
-                // values (half the 16 KB the tile fills in shared memory)
-                tma_expect(tm.full + st, kT5Tile / 2);
-                // box (chunk c, tile of the job's rows, slot): one contiguous 4 KB run
-                if (J.gu) {
-                    tma_load_5d(tile, mp + 0, 0, 0, c, tile_y, sk[0], tm.full + st);
-                    tma_load_5d(tile + kT5Tile / 2, mp + 1, 0, 0, c, tile_y, sk[0], tm.full + st);
-                } else {
+                // values (half the 16 KB each sub-tile fills in shared memory)
+                tma_expect(tm.full + st, (uint32_t)nsub * (kT5SubTile / 2));
+                // box (4-block group kT5Subs*c + u, tile of the job's rows, slot): one contiguous run
+                for (int u = 0; u < nsub; ++u) {
+                    uint8_t * sub = tile + u * kT5SubTile;
+                    if (J.gu) {
+                        tma_load_5d(sub, mp + 0, 0, 0, kT5Subs * c + u, tile_y, sk[0], tm.full + st);
+                        tma_load_5d(sub + kT5SubTile / 2, mp + 1, 0, 0, kT5Subs * c + u, tile_y, sk[0], tm.full + st);
+                    } else {
 #pragma unroll
-                    for (int m = 0; m < 4; ++m)
-                        tma_load_5d(tile + (kT5Tile / 4) * m, mp + 2, 0, 0, c, tile_y, sk[m], tm.full + st);
+                        for (int m = 0; m < 4; ++m)
+                            tma_load_5d(sub + (kT5SubTile / 4) * m, mp + 2, 0, 0, kT5Subs * c + u, tile_y, sk[m], tm.full + st);
+                    }
                 }
             }
             if (++st == S) {
@@ -302,7 +326,9 @@ __device__ __forceinline__ void t5_issuer(const StackParams & p, const T5Team & 
 #pragma unroll
                     for (int j = 1; j < kT5Chunk; ++j)
                         if (j < nbc)
-                            mma_f8f6f4(dt + (uint32_t)(kT5N * j), ad + (uint64_t)(2 * j), bd + bstep * (uint64_t)j, idesc, 0u);
+                            mma_f8f6f4(dt + (uint32_t)(kT5N * j),
+                                       ad + (uint64_t)((j / kT5Sub) * (kT5SubTile >> 4) + 2 * (j % kT5Sub)),
+                                       bd + bstep * (uint64_t)j, idesc, 0u);
                     mma_commit(tm.tfull + ts);
                     mma_commit(tm.empty + st);
                 }
@@ -325,7 +351,7 @@ __device__ __forceinline__ void t5_issuer(const StackParams & p, const T5Team & 
     tc_warp_wait(tm.fin, 0u, lane);
 }
 
-// the float block scales of blocks c0..c0+3 of one row (zero past nb)
+// the raw block scales of blocks c0..c0+3 of one row (the last block's past nb)
 __device__ __forceinline__ void t5_scales(const uint8_t * sb, const uint8_t * dyp, int c0, int nb, uint16_t (&dy)[kT5Chunk],
                                           uint8_t (&e)[kT5Chunk]) {
 #pragma unroll
@@ -499,7 +525,7 @@ __device__ __forceinline__ void stack_t5(const StackParams & p, uint8_t * smem, 
         return;
     }
     // warps 1 and 4-11 from here on
-    constexpr int kBar = 7 * 32;   // warps 1, 4-7, 10 and 11 (the TMEM users)
+    constexpr int kBar = 32 * (4 + kT5Issuers);   // the epilogue warps 4-7 and the issuers (the TMEM users)
     if (warp == 4) {
         tmem_alloc(tm.tslot, kT5Cols);
         tmem_relinquish();
@@ -534,8 +560,8 @@ __device__ __forceinline__ void stack_t5(const StackParams & p, uint8_t * smem, 
     named_barrier(3, kBar);
     tc_fence_after();
     const uint32_t tbase = *reinterpret_cast<volatile uint32_t *>(tm.tslot);
-    if (warp == 1 || warp == 10 || warp == 11)
-        t5_issuer(p, tm, tbase, b, G, mine, xbar, dbar, fillw, xbuf, dbuf, lane, warp == 1 ? 0 : warp - 9);
+    if (t5_issuer_index(warp) >= 0)
+        t5_issuer(p, tm, tbase, b, G, mine, xbar, dbar, fillw, xbuf, dbuf, lane, t5_issuer_index(warp));
     else
         t5_epilogue(p, tm, tbase, warp - 4, lane, b, G, mine, fillw, xbar, dbar, xbuf, dbuf);
     tc_fence_before();

@@ -207,12 +207,13 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t * bar, uint32_t parity) 
 
 // Bounded wait on an mbarrier phase for the hand-offs between warps of one
 // pipeline: a first non-blocking test, then try_wait polls that suspend the
-// thread (it issues nothing while suspended) until the phase completes or
-// 1 us passes; gives up after 2^20 polls or once any CTA has recorded an error.
+// thread (it issues nothing while suspended) until the phase completes or a
+// system-dependent time limit passes; gives up after 2^20 polls or once any
+// CTA has recorded an error.
 __device__ __forceinline__ bool mbar_spin(uint64_t * bar, uint32_t parity) {
     if (mbar_test_wait(bar, parity)) return true;
     for (uint32_t i = 0; i < (1u << 20); ++i) {
-        if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+        if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 63u && *reinterpret_cast<volatile int *>(&g_dev_error) != 0) return false;
     }
     return false;
