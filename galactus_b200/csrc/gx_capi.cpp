@@ -1475,11 +1475,12 @@ bool choose_stack_tiles_tc(gx::StackParams & sp, int & threads, uint32_t & smem)
 
 // MXFP4 jobs on the tensor cores fed by TMA (row mode 5, gx_stack_tma.cuh):
 // 64 + 64 gate/up rows, 32 rows of each of k = 4 experts per down job, read
-// from a copy of the slots in the tensor-core record layout. Opt-in with
-// GX_STACK_MMA=2.
+// from a copy of the slots in the tensor-core record layout. The default for
+// such stacks; GX_STACK_MMA=0 keeps them on the CUDA cores (row mode 3) and
+// GX_STACK_MMA=1 selects row mode 4.
 bool choose_stack_tiles_t5(gx::StackParams & sp, int & threads, uint32_t & smem) {
     const char * env = std::getenv("GX_STACK_MMA");
-    if (env == nullptr || std::strcmp(env, "2") != 0) return false;
+    if (env != nullptr && std::strcmp(env, "2") != 0) return false;
     if (sp.k != 4 || sp.H % 64 != 0 || sp.I % 64 != 0 || tensor_map_encoder() == nullptr) return false;
     const gx::StackParams keep = sp;
     const int nbh = sp.H / 32, nbi = sp.I / 32;
@@ -1637,7 +1638,21 @@ int setup_stack(gx_stack_plan * p, const float * const * x, const float * const 
     sp.need_grid = (l0.type_gate == gx::GX_T_IQ1_S || l0.type_down == gx::GX_T_IQ1_S) ? 1 : 0;
     int threads = 0;
     uint32_t smem = 0;
-    if (!(sp.row_mode == 3 && (choose_stack_tiles_t5(sp, threads, smem) || choose_stack_tiles_tc(sp, threads, smem))) &&
+    // row mode 5 where its copies of the slots fit in free device memory with
+    // 1 GiB to spare (else the CUDA-core rows)
+    bool t5_fits = false;
+    if (sp.row_mode == 3) {
+        uint64_t need = 1ull << 30;
+        for (uint32_t i = 0; i < p->n; ++i) {
+            int64_t trec = 0;
+            mxfp4_mats(p->lps[i], &trec);
+            need += (uint64_t)trec * (uint64_t)p->lps[i].g.n_as;
+        }
+        size_t free_b = 0, total_b = 0;
+        t5_fits = cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && need <= (uint64_t)free_b;
+    }
+    if (!(sp.row_mode == 3 && ((t5_fits && choose_stack_tiles_t5(sp, threads, smem)) ||
+                               choose_stack_tiles_tc(sp, threads, smem))) &&
         !choose_stack_tiles(sp, threads, smem))
         return GX_ERR_ALIGN;
     sp.split = sp.row_mode == 3 ? 4 : (sp.row_mode == 1 || (sp.row_mode == 2 && sp.k * sp.Rd == 32)) ? 2 : 1;
@@ -1946,7 +1961,7 @@ int gx_stack_plan_info_get(const gx_stack_plan * p, gx_stack_plan_info * info) {
         info->grid = p->grid;
         info->threads = p->threads;
         info->ctas_per_sm = p->per_sm;
-        info->stages = p->sp.C;
+        info->stages = p->sp.row_mode == 5 ? p->sp.tc_na : p->sp.C;
         info->rows_gate_up = p->sp.Rg;
         info->rows_down = p->sp.Rd;
         info->smem_bytes = p->smem;

@@ -333,12 +333,16 @@ typedef struct gx_stack_plan_info {
     int32_t grid;             /* CTAs of the stack kernel */
     int32_t threads;          /* threads per CTA */
     int32_t ctas_per_sm;
-    int32_t stages;           /* bulk-copy ring stages per CTA */
+    int32_t stages;           /* bulk-copy ring stages per CTA (tensor_cores 2: TMA ring stages) */
     int32_t rows_gate_up;     /* gate (and up) rows per gate/up unit */
     int32_t rows_down;        /* down rows per expert per down unit */
     uint32_t smem_bytes;      /* dynamic shared memory per CTA */
-    int32_t tensor_cores;     /* 1: the block dots of the stack's jobs run on the tensor cores (MXFP4 rows,
-                                 tcgen05 kind::f8f6f4; opt-in with GX_STACK_MMA=1) */
+    int32_t tensor_cores;     /* where the block dots of MXFP4 jobs run: 2 on the tensor cores (tcgen05
+                                 kind::f8f6f4) fed by TMA from the plan's copy of the slots in a
+                                 tensor-core record layout (the default for k = 4 stacks whose copies
+                                 fit in free device memory; the copy follows the arena's fills), 1 on
+                                 the tensor cores with CUDA-core repacking (GX_STACK_MMA=1), 0 on the
+                                 CUDA cores (GX_STACK_MMA=0, and every other stack) */
 } gx_stack_plan_info;
 int gx_stack_plan_create(gx_arena * arena, uint32_t first_layer, uint32_t n_layers, const gx_layer_desc * desc,
                          const float * const * x, const float * const * w, float * const * out, int64_t k, int64_t T,

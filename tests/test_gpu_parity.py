@@ -413,10 +413,13 @@ def test_stack_plan_graph_matches_oracle(gxlib, orc, dev, name, T, layers, layer
     assert info["stack_kernel"] == (1 if expect else 0), info
     if expect:
         # each ring stage belongs to one of the two weight-producer warps; the
-        # tensor-core MXFP4 jobs (k = 4) have one producer and three stages
-        mx_tc = m.type_gate == gxlib.TYPE_MXFP4 and k == 4 and os.environ.get("GX_STACK_MMA") == "1"
-        assert info["tensor_cores"] == (1 if mx_tc else 0), info
-        assert info["stages"] % (1 if mx_tc else 2) == 0, info
+        # tensor-core MXFP4 jobs (k = 4) run on the TMA-fed row mode by default
+        # (its ring a multiple of 4 stages), or with one producer (GX_STACK_MMA=1)
+        env = os.environ.get("GX_STACK_MMA")
+        mx = m.type_gate == gxlib.TYPE_MXFP4 and k == 4
+        want_tc = (1 if env == "1" else 0 if env == "0" else 2) if mx else 0
+        assert info["tensor_cores"] == want_tc, info
+        assert info["stages"] % {0: 2, 1: 1, 2: 4}[want_tc] == 0, info
     call = StackCall(arena, 0, m.layers, ptr(x), ptr(w), ptr(out), k, T)
     rng = np.random.default_rng(5 + T)
     stream = torch.cuda.current_stream()
