@@ -388,6 +388,7 @@ def headline(args, gx, torch, sg, dev, local):
         res["e2e_device_router"] = {"value": args.steps / (ms_r / 1e3), "unit": "tok/s",
                                     "h2d_bytes_per_step": NL * H * 4 + NL * E * 4, "d2h_bytes_per_step": NL * H * 4}
         res["plan"] = plan.info()
+        plan.close()   # one plan at a time: a tensor-core plan holds a copy of every slot
         # the stack kernel's duration: CUDA events recorded inside the graph around it
         kplan = sg.plan(arena, timing=True)
         stack_ms = 0.0
@@ -396,7 +397,6 @@ def headline(args, gx, torch, sg, dev, local):
             stack_ms += kplan.timing()[0]
         kplan.close()
         res["stack_ms"] = stack_ms / args.steps
-        plan.close()
     return arena, res
 
 
@@ -527,10 +527,14 @@ def stack_line(args, gx, torch, name, dev, local, stream, extras):
     # DRAM traffic of one launch: the per-layer figure of an ncu capture of the
     # same kernel and row types, times the layers streamed
     traffic = None
+    tensor_cores = res["plan"].get("tensor_cores", 0) if res["plan"]["stack_kernel"] else 0
     tp = ROOT / "profiles" / "traffic.json"
     if tp.exists():
-        per_layer = json.loads(tp.read_text()).get(model.name, {}).get("k_stack_per_layer")
+        key = "k_stack_per_layer_tma_tensor_cores" if tensor_cores == 2 else "k_stack_per_layer"
+        per_layer = json.loads(tp.read_text()).get(model.name, {}).get(key)
         traffic = per_layer * model.layers if per_layer else None
+    kernel = "k_stack (persistent: all layers, gate/up+act, down+combine"
+    kernel += "; MXFP4 block dots on tcgen05, codes loaded by TMA)" if tensor_cores == 2 else ")"
     metric, config, dtype = single_config(gx, model)
     line = {
         "metric": metric, "value": args.steps / (res["ms"] / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
@@ -540,7 +544,7 @@ def stack_line(args, gx, torch, name, dev, local, stream, extras):
         "config": config, "e2e": res["e2e"], "e2e_device_router": res["e2e_device_router"],
         "gpu_launches": (1 if res["plan"]["stack_kernel"] else 3 * model.layers) * args.steps,
         "plan": res["plan"], "hit_rate": res["hit_rate"],
-        "roofline": {"bound": "hbm", "kernel": "k_stack (persistent: all layers, gate/up+act, down+combine)",
+        "roofline": {"bound": "hbm", "kernel": kernel,
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes_per_launch": dbytes,
                      "avg_launch_ms": res["stack_ms"]},
