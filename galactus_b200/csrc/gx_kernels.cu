@@ -854,6 +854,13 @@ static uint32_t stack_layout_t5(StackParams & p, int & threads) {
     p.dots_off = p.wt_off + (uint32_t)p.NL * 32u;
     p.slots_off = p.dots_off + (uint32_t)p.C * 32u * 4u;
     p.grid_off = p.slots_off + (uint32_t)align_up((uint64_t)p.NL * p.T * p.k * 4u, 16);
+    // the job table: every job of a CTA of a 148-CTA grid, or what the rest holds
+    const int64_t nj = (int64_t)p.NL * p.T * ((int64_t)p.k * (p.I / p.Rg) + p.H / p.Rd);
+    const int64_t want = (nj + 147) / 148;
+    p.t5_jobs_off = p.grid_off;
+    const int64_t room = p.grid_off <= kMaxSmem ? (int64_t)(kMaxSmem - p.grid_off) / 8 : 0;
+    p.t5_jobs = (int32_t)(want < room ? want : room);
+    p.grid_off += (uint32_t)(8 * p.t5_jobs);
     return p.grid_off <= kMaxSmem ? p.grid_off : 0;
 }
 

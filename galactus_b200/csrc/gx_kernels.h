@@ -157,6 +157,8 @@ struct StackParams {
     int32_t nbuf_d;            // down-input buffers (kStackBufs, or 1 in row mode 4)
     int32_t tc_na;             // row mode 4: A-tile slots (MMA steps in flight); row mode 5: ring stages
     const CUtensorMap * t5_maps;   // row mode 5: [NL][3] codes of gate (64-row boxes), up (64), down (32)
+    uint32_t t5_jobs_off;      // row mode 5: the CTA's job table in shared memory (8 bytes per job)
+    int32_t t5_jobs;           // its capacity (jobs past it are computed where used)
     StackLayer layers[kStackMaxLayers];
 };
 

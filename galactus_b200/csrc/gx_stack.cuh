@@ -888,6 +888,12 @@ __global__ void __launch_bounds__(TCM == 4 ? kTcThreads : TCM == 5 ? kT5Threads
         if constexpr (TCM == 5) t5_init_bars(t5_team(smem, p.tc_off, (p.H > p.I ? p.H : p.I) / 32, p.tc_na));
         mbar_fence_init();
     }
+    if constexpr (TCM == 5) {
+        // row mode 5: the CTA's jobs, decoded once
+        const StackGeom g = stack_geom(p);
+        uint2 * jobs = reinterpret_cast<uint2 *>(smem + p.t5_jobs_off);
+        for (int jl = tid; jl < mine && jl < p.t5_jobs; jl += blockDim.x) jobs[jl] = t5_pack(stack_job(g, b + jl * G));
+    }
     __syncthreads();
 
     if constexpr (TCM == 5) {

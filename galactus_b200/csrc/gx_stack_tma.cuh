@@ -151,6 +151,47 @@ __device__ __forceinline__ void t5_init_bars(const T5Team & t) {
     mbar_init(t.fin, kT5Issuers);
 }
 
+// A job of row mode 5 in 8 bytes: L | gu << 8 | t << 9, r0 | pair << 16
+// (L < 128 layers, r0 and pair below 2^16).
+__device__ __forceinline__ uint2 t5_pack(const StackJob & J) {
+    return make_uint2((uint32_t)J.L | ((uint32_t)J.gu << 8) | ((uint32_t)J.t << 9),
+                      (uint32_t)J.r0 | ((uint32_t)J.pair << 16));
+}
+
+// Job jl of this CTA: from the table the prologue filled, else decoded here.
+__device__ __forceinline__ StackJob t5_job(const StackParams & p, const StackGeom & g, int b, int G, int jl) {
+    if (jl < p.t5_jobs) {
+        extern __shared__ __align__(128) uint8_t smem[];
+        const uint2 v = reinterpret_cast<const uint2 *>(smem + p.t5_jobs_off)[jl];
+        StackJob J;
+        J.L = (int)(v.x & 0xffu);
+        J.gu = (int)((v.x >> 8) & 1u);
+        J.t = (int)(v.x >> 9);
+        J.r0 = (int)(v.y & 0xffffu);
+        J.pair = (int)(v.y >> 16);
+        return J;
+    }
+    return stack_job(g, b + jl * G);
+}
+
+// tc_job over the job table: the key and buffer of the job's inputs, its
+// blocks per row and its B rows (buffer counts are 1 or 2).
+__device__ __forceinline__ TcJob t5_tcjob(const StackParams & p, const StackGeom & g, int b, int G, int jl,
+                                          const uint8_t * xbuf, const uint8_t * dbuf) {
+    TcJob q;
+    q.J = t5_job(p, g, b, G, jl);
+    q.cs = 0;
+    q.n = jl;
+    q.key = q.J.L * p.T + q.J.t;
+    q.bi = q.J.gu ? (q.key & (kStackBufs - 1)) : (p.nbuf_d == 2 ? (q.key & 1) : 0);
+    q.kk = q.J.gu ? 1 : p.k;
+    q.NB = (q.J.gu ? p.H : p.I) >> 5;
+    q.S = 0;
+    q.inb = q.J.gu ? xbuf + q.bi * p.alx.pitch : dbuf + q.bi * p.k * p.ald.pitch;
+    q.in_doff = q.J.gu ? p.alx.d_off : p.ald.d_off;
+    return q;
+}
+
 // Q8_0 quantization of one 32-element block held by a warp (lane = element),
 // the same quants and fp16 scale as quant_block_split, stored as e4m3 digits
 // (quant_block_digits' layout).
@@ -173,7 +214,7 @@ __device__ __forceinline__ void quant_value_digits(float v, uint8_t * dst, int m
 // copy per 64 gate/up rows or per expert's 32 down rows).
 __device__ __forceinline__ void t5_issue_scales(const StackParams & p, const T5Team & tm, const StackGeom & g, int b,
                                                 int G, int jn, const int32_t * slots, const StackWeights * wt) {
-    const StackJob J = stack_job(g, b + jn * G);
+    const StackJob J = t5_job(p, g, b, G, jn);
     const StackWeights w = wt[J.L];
     const int32_t * sl = slots + J.L * p.T * p.k;
     const int NB = (J.gu ? p.H : p.I) / 32;
@@ -205,7 +246,7 @@ __device__ __forceinline__ void t5_producer(const StackParams & p, const T5Team 
     uint32_t gc = 0;
     bool ok = true;
     for (int jl = 0; jl < mine && ok; ++jl) {
-        const StackJob J = stack_job(g, b + jl * G);
+        const StackJob J = t5_job(p, g, b, G, jl);
         const int32_t * sl = slots + J.L * p.T * p.k + J.pair;
         const int NB = (J.gu ? p.H : p.I) / 32, nch = (NB + kT5Chunk - 1) / kT5Chunk;
         const int nsub_all = (NB + kT5Sub - 1) / kT5Sub;   // boxes along the row
@@ -299,7 +340,7 @@ __device__ __forceinline__ void t5_issuer(const StackParams & p, const T5Team & 
     uint32_t gc = 0;            // chunks so far
     bool ok = true;
     for (int jl = 0; jl < mine && ok; ++jl) {
-        const TcJob q = tc_job(p, g, b, G, jl, xbuf, dbuf);
+        const TcJob q = t5_tcjob(p, g, b, G, jl, xbuf, dbuf);
         // the job's inputs (B digits) are in
         int okin = 1;
         if (lane == 0) okin = t5_wait_input(q, fillw, xbar, dbar) ? 1 : 0;
@@ -371,7 +412,7 @@ __device__ __forceinline__ void t5_epilogue(const StackParams & p, const T5Team 
     uint32_t ts = 0, tph = 0;   // TMEM slot and the parity of its use
     bool ok = true;
     for (int jl = 0; jl < mine && ok; ++jl) {
-        const TcJob q = tc_job(p, g, b, G, jl, xbuf, dbuf);
+        const TcJob q = t5_tcjob(p, g, b, G, jl, xbuf, dbuf);
         const StackJob & J = q.J;
         const int p2 = jl & 1, NB = q.NB, nch = (NB + kT5Chunk - 1) / kT5Chunk;
         // the job's scales landed; its input buffer (the activation scales read here) holds its key
@@ -452,7 +493,7 @@ __device__ __forceinline__ void t5_tail(const StackParams & p, const T5Team & tm
     const StackGeom g = stack_geom(p);
     bool ok = true;
     for (int jl = 0; jl < mine && ok; ++jl) {
-        const TcJob q = tc_job(p, g, b, G, jl, xbuf, dbuf);
+        const TcJob q = t5_tcjob(p, g, b, G, jl, xbuf, dbuf);
         const StackJob & J = q.J;
         const int p2 = jl & 1;
         if (!tc_warp_wait(tm.xfull + p2, (uint32_t)((jl >> 1) & 1), lane)) {
