@@ -630,6 +630,15 @@ def run_single(args):
             line["qwen3_30b"] = l2
         line["olmoe_single_layer"], cfg1_ids = olmoe_line(args, gx, torch, dev, stream)
         line["ep_1gpu"] = ep_measure(args, gx, torch, 1, 0, local, dev, None)
+        # configs 5 and 4 as one-GPU stacks of 8 layers x 16 experts, all
+        # resident (their 58- and 94-layer host tiers do not fit host memory;
+        # the work per layer is the full model's)
+        for key, nm in (("deepseek_v3_8x16", "deepseek-v3"), ("qwen3_235b_8x16", "qwen3-235b")):
+            sub = argparse.Namespace(**{**vars(args), "layers": 8, "experts": 16})
+            _, l3, _ = stack_line(sub, gx, torch, nm, dev, local, stream, False)
+            for k in ("n_gpus", "steps", "warmup", "higher_is_better", "scaling", "vs_baseline", "unit"):
+                l3.pop(k, None)
+            line[key] = l3
     if args.cpu_tokens > 0:
         line["cpu_baseline"] = cpu_baseline_leg(args, gx, model, traces, cfg1_ids)
     print(json.dumps(line), flush=True)
